@@ -1,0 +1,178 @@
+/*
+ * backend_cuda.h — B200 (sm_100a) CUDA backend for the qwen3.c token mixers.
+ *
+ * Plays the role c/backend_vulkan.h plays for c/qwen.c, for the token-mixing
+ * hot path only: the gated GQA full-attention layers and the GatedDeltaNet
+ * linear-attention layers, decode and prefill. Each declaration names the
+ * reference interface it replaces (file:line in the reference project).
+ *
+ * Conventions (as in the reference backend):
+ *   - Every int-returning call returns 1 on success and 0 on failure; the
+ *     reason is in coli_cuda_last_error(). There is NO CPU fallback inside the
+ *     backend: a 0 is the caller's signal, exactly like a coli_vk_* 0
+ *     (c/qwen.c:592, 635, 691, 745). A device-side failure marks the backend
+ *     not ready and every later call returns 0 (c/backend_vulkan.c:1836).
+ *   - Host-pointer entry points take fp32 row-major arrays the caller owns and
+ *     copy them in and out per call (synchronous). *_dev entry points take
+ *     device pointers, run asynchronously on the backend stream and never
+ *     copy; their `dtype` is 0 for fp32 or 1 for bf16 activations.
+ *   - State is device-resident and keyed by a per-type layer index (`layer`
+ *     counts full-attention layers for KV, GDN layers for GDN state, like the
+ *     reference's kvi / gi), plus a request index `req` for batched decode.
+ *     KV cache: bf16 [batch][KH][max_t][hd]. GDN state: fp32
+ *     [batch][VH][KD][VD] (the reference's [VH][KD][VD] per request). Conv
+ *     history: fp32 [batch][conv_k-1][conv_dim] (the reference ring's slots
+ *     1..conv_k-1; slot 0 is dead state, always overwritten before use).
+ *   - Single host thread; calls are not reentrant (c/backend_vulkan.c:1838).
+ *   - Shapes: hd = 256 with H/KH = 8 for GQA; KD = VD = 128, VH = 2*KH and
+ *     conv_k = 4 for GDN (the Qwen3.5/3.6-MoE token mixers). Other shapes
+ *     return 0 with an error.
+ */
+#ifndef COLI_BACKEND_CUDA_H
+#define COLI_BACKEND_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- lifecycle: replaces coli_vk_init / coli_vk_shutdown / coli_vk_available
+ * (c/backend_vulkan.h:37-39) and coli_vk_mem_info (:40). */
+int  coli_cuda_init(int device);
+void coli_cuda_shutdown(void);
+int  coli_cuda_available(void);
+void coli_cuda_mem_info(size_t *used_bytes, size_t *tensor_count);
+/* New: the reason for the last 0 return (never NULL). */
+const char *coli_cuda_last_error(void);
+/* New: wait for queued *_dev work and check the device error word. */
+int  coli_cuda_sync(void);
+/* New: the cudaStream_t the backend launches on; set it to run inside a
+ * caller's stream (or a CUDA graph capture). NULL restores the default. */
+void *coli_cuda_get_stream(void);
+int  coli_cuda_set_stream(void *stream);
+
+/* ---- New: per-kernel device timing (CUDA events recorded on the launching
+ * stream around every launch of the named kernel while enabled) and a count
+ * of every kernel this library launched. Replaces the reference's wall-clock
+ * and Vulkan timestamp profiling (c/qwen.c:163, c/backend_vulkan.c:1130-1213).
+ * Kernel ids: 0 GQA split-KV decode, 1 GDN decode, 2 GQA prefill,
+ * 3 GDN chunked prefill, 4 GQA combine. ktimer_read synchronises, sums the
+ * recorded intervals and clears them. */
+enum { COLI_K_GQA_SPLIT = 0, COLI_K_GDN_DECODE = 1, COLI_K_GQA_PREFILL = 2,
+       COLI_K_GDN_PREFILL = 3, COLI_K_GQA_COMBINE = 4, COLI_K_COUNT = 5 };
+int  coli_cuda_ktimer_enable(int on);
+int  coli_cuda_ktimer_read(int kernel, double *total_ms, int *launches);
+long long coli_cuda_launch_count(void);
+
+/* ---- capability probes: coli_vk_gdn_available (c/backend_vulkan.h:151),
+ * coli_vk_gqa_available (:162), coli_vk_gqa_full_available (:173),
+ * coli_vk_gdn_full_available (:265). */
+int  coli_cuda_gdn_available(void);
+int  coli_cuda_gqa_available(void);
+int  coli_cuda_gqa_full_available(void);
+int  coli_cuda_gdn_full_available(void);
+
+/* ---- KV cache: coli_vk_kv_ensure / coli_vk_kv_row / coli_vk_kv_reset
+ * (c/backend_vulkan.h:114-116, impl c/backend_vulkan.c:1705-1743) with a
+ * request dimension. `row` = kh*max_t + pos, as in the reference. Host rows
+ * are fp32 and stored as bf16. kv_ensure zero-fills a new cache; calling it
+ * again with the same geometry keeps the contents. kv_reset drops all layers. */
+int  coli_cuda_kv_ensure(int layer, int batch, int KH, int max_t, int hd);
+int  coli_cuda_kv_row(int layer, int req, int row, const float *k, const float *v);
+/* New: n consecutive rows starting at row0 (bulk upload / read-back). */
+int  coli_cuda_kv_rows(int layer, int req, int row0, int n, const float *k, const float *v);
+int  coli_cuda_kv_read(int layer, int req, int row0, int n, float *k, float *v);
+void coli_cuda_kv_reset(void);
+/* New: device base pointers of a layer's bf16 K and V caches. */
+int  coli_cuda_kv_device_ptr(int layer, void **k, void **v);
+/* Resident q_norm / k_norm weights [hd] of a full layer:
+ * coli_vk_gqa_norm_weight (c/backend_vulkan.h:172). */
+int  coli_cuda_gqa_norm_weight(int layer, const float *qnw, const float *knw, int hd);
+
+/* ---- GQA attention core: coli_vk_gqa (c/backend_vulkan.h:163-164,
+ * c/backend_vulkan.c:2167-2199). q [S][H][2*hd] holds roped q | gate per
+ * head; query row s sees cache rows 0..T-S+s of request 0; ctx [S][H][hd]
+ * = softmax(q k^T * scale) v * sigmoid(gate). st0 must be 0 (the only value
+ * the engine passes, c/qwen.c:623, 629). */
+int  coli_cuda_gqa(int layer, const float *q, float *ctx, int S, int H, int KH, int hd,
+                   int max_t, int st0, int T, float scale);
+
+/* ---- GQA block minus projections for S tokens of one request at
+ * pos_base..pos_base+S-1: the body of attention() between the projections
+ * and o_proj (c/qwen.c:598-663): q/k zero-centred RMSNorm with the resident
+ * norm weights, partial RoPE (rot dims, theta), K/V append, causal attention
+ * with scale 1/sqrt(hd), sigmoid output gate. qg [S][H][2*hd] raw q|gate,
+ * k/v [S][KH][hd] raw, ctx [S][H][hd]. The device part of
+ * coli_vk_gqa_full (c/backend_vulkan.h:174-177). */
+int  coli_cuda_gqa_step(int layer, int req, int S, int pos_base, const float *qg, const float *k,
+                        const float *v, float *ctx, int H, int KH, int hd, int rot, float eps,
+                        float theta);
+int  coli_cuda_gqa_step_dev(int layer, int req, int S, int pos_base, const void *qg, const void *k,
+                            const void *v, void *ctx, int H, int KH, int hd, int rot, float eps,
+                            float theta, int dtype);
+
+/* ---- New: batched GQA decode, one new token for each request b < B at its
+ * own position pos[b] (requests 0..B-1 of the layer's cache). Same per-row
+ * semantics as coli_cuda_gqa_step with S = 1. The _dev form takes pos on the
+ * device (int32 [B]). */
+int  coli_cuda_gqa_decode(int layer, int B, const float *qg, const float *k, const float *v,
+                          const int *pos, float *ctx, int H, int KH, int hd, int rot, float eps,
+                          float theta);
+int  coli_cuda_gqa_decode_dev(int layer, int B, const void *qg, const void *k, const void *v,
+                              const int *pos_dev, void *ctx, int H, int KH, int hd, int rot,
+                              float eps, float theta, int dtype);
+
+/* ---- GatedDeltaNet state: coli_vk_gdn_state_ensure / coli_vk_gdn_reset
+ * (c/backend_vulkan.h:152-153), coli_vk_gdn_conv_ensure / _weight (:266-267),
+ * coli_vk_gdn_ba_weight (:206) for the per-layer A_log, dt_bias, gnorm.
+ * gdn_reset zeroes every state and conv history in place. */
+int  coli_cuda_gdn_state_ensure(int layer, int batch, int VH, int KD, int VD);
+int  coli_cuda_gdn_conv_ensure(int layer, int batch, int conv_k, int conv_dim);
+int  coli_cuda_gdn_conv_weight(int layer, const float *cw, int conv_k, int conv_dim);
+int  coli_cuda_gdn_params(int layer, const float *A_log, const float *dt_bias, const float *gnorm,
+                          int VH, int VD);
+void coli_cuda_gdn_reset(void);
+/* New (state parity / checkpoint): one request's state [VH][KD][VD] and conv
+ * ring [conv_k][conv_dim] in the reference's layout (slot conv_k-1 newest;
+ * get writes zeros to the dead slot 0, set ignores it). */
+int  coli_cuda_gdn_state_get(int layer, int req, float *state);
+int  coli_cuda_gdn_state_set(int layer, int req, const float *state);
+int  coli_cuda_gdn_conv_get(int layer, int req, float *ring);
+int  coli_cuda_gdn_conv_set(int layer, int req, const float *ring);
+
+/* ---- GDN recurrence on pre-normalised inputs: coli_vk_gdn
+ * (c/backend_vulkan.h:154-156). Request 0; qn/kn [KH*KD] (q already scaled
+ * by 1/sqrt(KD)), v/z [VH*VD], decay/beta [VH], gnorm [VD] -> y [VH*VD]. */
+int  coli_cuda_gdn(int layer, const float *qn, const float *kn, const float *v, const float *z,
+                   const float *decay, const float *beta, const float *gnorm, float *y,
+                   int KH, int KD, int VH, int VD, float eps);
+
+/* ---- GDN decode, fused conv4 + SiLU + L2 norm + gates + recurrence + gated
+ * RMSNorm, one token for each request b < B: gdn_step() after the
+ * projections (c/qwen.c:697-773); the device part of coli_vk_gdn_full
+ * (c/backend_vulkan.h:268-270). qkv [B][conv_dim] pre-conv (q|k|v),
+ * z [B][VH*VD], a/b [B][VH] -> y [B][VH*VD] (the out_proj input). */
+int  coli_cuda_gdn_decode(int layer, int B, const float *qkv, const float *z, const float *a,
+                          const float *b, float *y, int KH, int KD, int VH, int VD, float eps);
+int  coli_cuda_gdn_decode_dev(int layer, int B, const void *qkv, const void *z, const void *a,
+                              const void *b, void *y, int KH, int KD, int VH, int VD, float eps,
+                              int dtype);
+
+/* ---- GDN prefill of S tokens of one request, carrying the conv history and
+ * state in and out: the reference's S sequential gdn_step calls
+ * (c/qwen.c:1376-1380) and the device part of coli_vk_gdn_full_seq
+ * (c/backend_vulkan.h:274-278). Row layouts as in coli_cuda_gdn_decode. */
+int  coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const float *z,
+                           const float *a, const float *b, float *y, int KH, int KD, int VH, int VD,
+                           float eps);
+int  coli_cuda_gdn_prefill_dev(int layer, int req, int S, const void *qkv, const void *z,
+                               const void *a, const void *b, void *y, int KH, int KD, int VH,
+                               int VD, float eps, int dtype);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COLI_BACKEND_CUDA_H */

@@ -205,6 +205,44 @@ void orc_gdn_step(const float *qkv, const float *z, const float *a, const float 
 }
 
 /*
+ * The recurrence + gated RMSNorm alone, on pre-normalised inputs
+ * (c/qwen.c:748-773; the contract of the reference's coli_vk_gdn):
+ * qn/kn [KH*KD], v/z [VH*VD], decay/beta [VH], gnorm [VD] -> y [VH*VD].
+ */
+void orc_gdn_recur(const float *qn, const float *kn, const float *v, const float *z,
+                   const float *decay, const float *beta, const float *gnorm, float *state,
+                   float *y, int KH, int KD, int VH, int VD, float eps)
+{
+    int grp = VH / KH;
+    for (int h = 0; h < VH; h++) {
+        int src = h / grp;
+        const float *qh = qn + src * KD, *kh = kn + src * KD, *vh = v + h * VD;
+        float *Sh = state + (size_t)h * KD * VD;
+        float *mem = calloc((size_t)VD, sizeof(float));
+        float *dl = malloc((size_t)VD * sizeof(float));
+        for (int kd = 0; kd < KD; kd++) {
+            float *row = Sh + (size_t)kd * VD;
+            float kk = kh[kd];
+            for (int vd = 0; vd < VD; vd++) { row[vd] *= decay[h]; mem[vd] += row[vd] * kk; }
+        }
+        for (int vd = 0; vd < VD; vd++) dl[vd] = (vh[vd] - mem[vd]) * beta[h];
+        float *yh = y + (size_t)h * VD;
+        for (int vd = 0; vd < VD; vd++) yh[vd] = 0;
+        for (int kd = 0; kd < KD; kd++) {
+            float *row = Sh + (size_t)kd * VD;
+            float kk = kh[kd], qq = qh[kd];
+            for (int vd = 0; vd < VD; vd++) { row[vd] += kk * dl[vd]; yh[vd] += row[vd] * qq; }
+        }
+        const float *zh = z + (size_t)h * VD;
+        double ms = 0;
+        for (int vd = 0; vd < VD; vd++) ms += (double)yh[vd] * yh[vd];
+        float r = 1.f / sqrtf((float)(ms / VD) + eps);
+        for (int vd = 0; vd < VD; vd++) yh[vd] = yh[vd] * r * gnorm[vd] * orc_silu(zh[vd]);
+        free(mem); free(dl);
+    }
+}
+
+/*
  * S GatedDeltaNet tokens in sequence for one request: the reference prefill
  * is exactly S gdn_step calls (c/qwen.c:1378-1379). Row strides: qkv CD,
  * z VH*VD, a/b VH, y VH*VD.

@@ -38,6 +38,7 @@ class Oracle:
         lib.orc_gqa_attend.argtypes = [_f32p] * 4 + [_c_int] * 6 + [_c_float]
         lib.orc_gdn_step.argtypes = [_f32p] * 11 + [_c_int] * 5 + [_c_float]
         lib.orc_gdn_seq.argtypes = [_f32p] * 11 + [_c_int] * 6 + [_c_float]
+        lib.orc_gdn_recur.argtypes = [_f32p] * 9 + [_c_int] * 4 + [_c_float]
         lib.orc_threads.restype = _c_int
         lib.orc_set_threads.argtypes = [_c_int]
 
@@ -74,6 +75,14 @@ class Oracle:
         y = np.zeros((S, VH * VD), np.float32)
         self.lib.orc_gdn_seq(_p(qkv), _p(z), _p(a), _p(b), _p(conv_w), _p(A_log), _p(dt_bias),
                              _p(gnorm), _p(ring), _p(state), _p(y), S, KH, KD, VH, VD, K, eps)
+        return y
+
+    def gdn_recur(self, qn, kn, v, z, decay, beta, gnorm, state, KH, eps=1e-6):
+        """Post-norm recurrence only; state [VH,KD,VD] updated in place."""
+        VH, KD, VD = state.shape
+        y = np.zeros(VH * VD, np.float32)
+        self.lib.orc_gdn_recur(_p(qn), _p(kn), _p(v), _p(z), _p(decay), _p(beta), _p(gnorm),
+                               _p(state), _p(y), KH, KD, VH, VD, eps)
         return y
 
 

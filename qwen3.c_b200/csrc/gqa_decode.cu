@@ -1,0 +1,368 @@
+// Gated GQA decode: split-KV flash-decode over the resident bf16 KV cache.
+//
+// Semantics follow the reference's attention() for query rows that sit at the
+// end of the cache (c/qwen.c:598-663): per-head zero-centred RMSNorm of q and
+// k, partial NeoX RoPE on the first `rot` dims, K/V append, causal softmax
+// attention over rows 0..pos with scale 1/sqrt(hd), then ctx *= sigmoid(gate).
+//
+// Kernels
+//   gqa_prologue_kernel  q/k norm + RoPE; bf16 q to scratch; k/v rows appended
+//                        to the cache (one CTA per head vector).
+//   gqa_split_kernel     one CTA per (query row, KV head, KV split). Each warp
+//                        streams 16-token K/V tiles through its own TMA ring
+//                        (128B-swizzled boxes, mbarrier completion) and runs
+//                        S^T = K Q^T and O^T += V^T P^T on bf16 mma.sync with
+//                        all 8 query heads of the KV head in the N dimension,
+//                        online softmax in registers (log2 domain), P^T
+//                        formed from the score fragments with movmatrix. The
+//                        warps' partial (max, sum, O) are merged in shared
+//                        memory and one partial per CTA goes to scratch.
+//   gqa_combine_kernel   log-sum-exp merge of the split partials, the
+//                        sigmoid output gate, ctx out.
+// The dominant kernel is HBM bound: 2*hd*2 bytes of K+V per cached token per
+// KV head.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace coli {
+
+constexpr int GQA_HD = 256, GQA_GRP = 8, GQA_TILE = 16;
+constexpr int GQA_TILE_BYTES = GQA_TILE * GQA_HD * 2;  // one K (or V) tile: 8 KiB
+
+// ------------------------------------------------------------------ prologue
+template <typename TI>
+__global__ void __launch_bounds__(GQA_HD)
+gqa_prologue_kernel(GqaPrologueArgs p)
+{
+    const int n = blockIdx.x, j = blockIdx.y, d = threadIdx.x;
+    const int H = p.H, KH = p.KH;
+    const int pos = p.pos[n];
+    const float *w;
+    float x;
+    if (j < H) {
+        x = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * H + j) * 2 * GQA_HD + d]);
+        w = p.qnw;
+    } else {
+        x = to_f32(static_cast<const TI *>(p.k)[((size_t)n * KH + (j - H)) * GQA_HD + d]);
+        w = p.knw;
+    }
+    // zero-centred RMSNorm, sum of squares in double (c/qwen.c:326-330)
+    __shared__ double red[8];
+    __shared__ float vec[GQA_HD];
+    double s2 = (double)x * x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    if ((d & 31) == 0) red[d >> 5] = s2;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float r = 1.f / sqrtf((float)(tot / GQA_HD) + p.eps);
+    float y = x * r * (1.f + w[d]);
+    vec[d] = y;
+    __syncthreads();
+    // partial NeoX RoPE on dims [0, rot) (c/qwen.c:570-579)
+    const int half = p.rot >> 1;
+    if (d < p.rot) {
+        const int jj = d < half ? d : d - half;
+        const float inv = powf(p.theta, -2.0f * jj / p.rot);
+        const float ang = (float)pos * inv;
+        const float cs = cosf(ang), sn = sinf(ang);
+        const float lo = vec[jj], hi = vec[jj + half];
+        y = d < half ? lo * cs - hi * sn : hi * cs + lo * sn;
+    }
+    if (j < H) {
+        p.qout[((size_t)n * H + j) * GQA_HD + d] = __float2bfloat16_rn(y);
+    } else {
+        const int kh = j - H;
+        const int creq = p.creq ? p.creq[n] : n;
+        const size_t row = ((size_t)creq * KH + kh) * p.max_t + pos;
+        p.kcache[row * GQA_HD + d] = __float2bfloat16_rn(y);
+        const float v = to_f32(static_cast<const TI *>(p.v)[((size_t)n * KH + kh) * GQA_HD + d]);
+        p.vcache[row * GQA_HD + d] = __float2bfloat16_rn(v);
+    }
+}
+
+// ------------------------------------------------------------------ split-KV
+template <int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                 GqaSplitArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(16) __nv_bfloat16 qsm[GQA_GRP * GQA_HD];
+    __shared__ __align__(8) uint64_t full[WARPS][STAGES];
+
+    const int split = blockIdx.x, kh = blockIdx.y, n = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int KH = p.KH;
+
+    // q of the 8 heads sharing this KV head (bf16, roped)
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)n * p.H + kh * GQA_GRP) * GQA_HD);
+        uint4 *dst = reinterpret_cast<uint4 *>(qsm);
+        for (int i = tid; i < GQA_GRP * GQA_HD / 8; i += WARPS * 32) dst[i] = src[i];
+    }
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&full[warp][s], 1);
+        fence_mbar_init();
+    }
+    if (tid == 0) { tma_prefetch_desc(&tmK); tma_prefetch_desc(&tmV); }
+    __syncthreads();
+
+    const int T = p.pos[n] + 1;
+    const int start = split * p.chunk;
+    const int end = min(T, start + p.chunk);
+    const int ntiles = end > start ? (end - start + GQA_TILE - 1) / GQA_TILE : 0;
+    const int my_tiles = ntiles > warp ? (ntiles - warp + WARPS - 1) / WARPS : 0;
+    const int creq = p.creq ? p.creq[n] : n;
+    const int rowbase = (creq * KH + kh) * p.max_t;
+
+    uint8_t *wbuf = smem + (size_t)warp * STAGES * 2 * GQA_TILE_BYTES;
+    auto issue = [&](int it) {
+        const int s = it % STAGES;
+        const int row = rowbase + start + (warp + it * WARPS) * GQA_TILE;
+        uint8_t *kb = wbuf + (size_t)s * 2 * GQA_TILE_BYTES;
+        uint8_t *vb = kb + GQA_TILE_BYTES;
+        mbar_expect_tx(&full[warp][s], 2 * GQA_TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            tma_load_2d(kb + c * 2048, &tmK, 64 * c, row, &full[warp][s]);
+            tma_load_2d(vb + c * 2048, &tmV, 64 * c, row, &full[warp][s]);
+        }
+    };
+    if (lane == 0)
+        for (int it = 0; it < STAGES && it < my_tiles; ++it) issue(it);
+
+    // Q^T as the B operand: b0 = (dim = 16kk + 2(lane&3) + {0,1}, head = lane>>2), b1 = dim + 8
+    uint32_t qf[16][2];
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+        const __nv_bfloat16 *qrow = qsm + (lane >> 2) * GQA_HD + kk * 16 + (lane & 3) * 2;
+        qf[kk][0] = *reinterpret_cast<const uint32_t *>(qrow);
+        qf[kk][1] = *reinterpret_cast<const uint32_t *>(qrow + 8);
+    }
+
+    float acc[16][4];
+#pragma unroll
+    for (int mt = 0; mt < 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const float sl2 = p.scale_log2;
+    const int r8 = lane & 7, mi = lane >> 3;
+
+    for (int it = 0; it < my_tiles; ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[warp][s], (it / STAGES) & 1)) break;  // error raised; finish quietly
+        const uint32_t kb = smem_u32(wbuf + (size_t)s * 2 * GQA_TILE_BYTES);
+        const uint32_t vb = kb + GQA_TILE_BYTES;
+        const int tok0 = start + (warp + it * WARPS) * GQA_TILE;
+        const int valid = min(GQA_TILE, end - tok0);
+
+        // S^T[16 tok x 8 heads] = K[16 x 256] . Q^T[256 x 8]
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+            const int tok = (mi & 1) * 8 + r8;
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+                const int chunk = (kk & 3) * 2 + (mi >> 1);
+                const uint32_t addr = kb + (kk >> 2) * 2048 + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(addr, a0, a1, a2, a3);
+                mma_bf16_16816(sc, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+            }
+        }
+        // online softmax per head (heads h0 = 2(lane&3), h1 = h0 + 1)
+        const int ta = lane >> 2, tb = ta + 8;
+        float x0 = ta < valid ? sc[0] * sl2 : -INFINITY;
+        float x1 = ta < valid ? sc[1] * sl2 : -INFINITY;
+        float x2 = tb < valid ? sc[2] * sl2 : -INFINITY;
+        float x3 = tb < valid ? sc[3] * sl2 : -INFINITY;
+        float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int o = 4; o <= 16; o <<= 1) {
+            t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+            t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+        }
+        const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
+        const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
+        const float al0 = exp2f(m0 - u0), al1 = exp2f(m1 - u1);
+        const float p0 = exp2f(x0 - u0), p1 = exp2f(x1 - u1);
+        const float p2 = exp2f(x2 - u0), p3 = exp2f(x3 - u1);
+        m0 = n0; m1 = n1;
+        l0 = l0 * al0 + (p0 + p2);
+        l1 = l1 * al1 + (p1 + p3);
+#pragma unroll
+        for (int mt = 0; mt < 16; ++mt) {
+            acc[mt][0] *= al0; acc[mt][1] *= al1; acc[mt][2] *= al0; acc[mt][3] *= al1;
+        }
+        const uint32_t pb0 = movmatrix_t(pack_bf16(p0, p1));
+        const uint32_t pb1 = movmatrix_t(pack_bf16(p2, p3));
+        if (valid < GQA_TILE) {
+            // rows past the end of the request are never weighted; clear them
+            // so stale non-finite cache contents cannot leak through 0 * inf
+            uint8_t *vgen = wbuf + (size_t)s * 2 * GQA_TILE_BYTES + GQA_TILE_BYTES;
+            for (int i = lane; i < (GQA_TILE - valid) * 32; i += 32) {
+                const int row = valid + (i >> 5), c = (i & 31) >> 3, ch = i & 7;
+                *reinterpret_cast<uint4 *>(vgen + c * 2048 + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+        // O^T[256 dims x 8 heads] += V^T[256 x 16 tok] . P^T[16 tok x 8 heads]
+        {
+            const int tok = (mi >> 1) * 8 + r8;
+#pragma unroll
+            for (int mt = 0; mt < 16; ++mt) {
+                const int chunk = (mt & 3) * 2 + (mi & 1);
+                const uint32_t addr = vb + (mt >> 2) * 2048 + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(addr, a0, a1, a2, a3);
+                mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && it + STAGES < my_tiles) {
+            fence_proxy_async();
+            issue(it + STAGES);
+        }
+    }
+#pragma unroll
+    for (int o = 4; o <= 16; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+
+    // ---- merge the warps' partials in shared memory (stage buffers reused)
+    __syncthreads();
+    float *Osm = reinterpret_cast<float *>(smem);               // [WARPS][8][256]
+    float *MLsm = Osm + WARPS * GQA_GRP * GQA_HD;                // [WARPS][8][2]
+    {
+        float *O = Osm + warp * GQA_GRP * GQA_HD;
+        const int h0 = (lane & 3) * 2, dr = lane >> 2;
+#pragma unroll
+        for (int mt = 0; mt < 16; ++mt) {
+            O[h0 * GQA_HD + mt * 16 + dr] = acc[mt][0];
+            O[(h0 + 1) * GQA_HD + mt * 16 + dr] = acc[mt][1];
+            O[h0 * GQA_HD + mt * 16 + dr + 8] = acc[mt][2];
+            O[(h0 + 1) * GQA_HD + mt * 16 + dr + 8] = acc[mt][3];
+        }
+        if (lane < 4) {
+            MLsm[(warp * GQA_GRP + h0) * 2] = m0;
+            MLsm[(warp * GQA_GRP + h0) * 2 + 1] = l0;
+            MLsm[(warp * GQA_GRP + h0 + 1) * 2] = m1;
+            MLsm[(warp * GQA_GRP + h0 + 1) * 2 + 1] = l1;
+        }
+    }
+    __syncthreads();
+    const size_t pidx = (((size_t)n * KH + kh) * p.n_splits + split) * GQA_GRP;
+    for (int i = tid; i < GQA_GRP * GQA_HD; i += WARPS * 32) {
+        const int h = i / GQA_HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) M = fmaxf(M, MLsm[(w * GQA_GRP + h) * 2]);
+        float o = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) {
+            const float mw = MLsm[(w * GQA_GRP + h) * 2];
+            const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+            o += Osm[(w * GQA_GRP + h) * GQA_HD + (i % GQA_HD)] * f;
+            L += MLsm[(w * GQA_GRP + h) * 2 + 1] * f;
+        }
+        p.part_o[pidx * GQA_HD + i] = o;
+        if ((i % GQA_HD) == 0) {
+            p.part_ml[(pidx + h) * 2] = M;
+            p.part_ml[(pidx + h) * 2 + 1] = L;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ combine
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(GQA_HD)
+gqa_combine_kernel(GqaCombineArgs p)
+{
+    const int n = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int kh = h / GQA_GRP, hl = h % GQA_GRP;
+    const size_t base = ((size_t)n * p.KH + kh) * p.n_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, p.part_ml[((base + s) * GQA_GRP + hl) * 2]);
+    float o = 0.f, L = 0.f;
+    for (int s = 0; s < p.n_splits; ++s) {
+        const size_t pi = (base + s) * GQA_GRP + hl;
+        const float ms = p.part_ml[pi * 2];
+        const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+        o += p.part_o[pi * GQA_HD + d] * f;
+        L += p.part_ml[pi * 2 + 1] * f;
+    }
+    const float gate = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * p.H + h) * 2 * GQA_HD + GQA_HD + d]);
+    static_cast<TO *>(p.ctx)[((size_t)n * p.H + h) * GQA_HD + d] = from_f32<TO>(o / L * sigmoidf_(gate));
+}
+
+// ------------------------------------------------------------------ launch
+constexpr int SPLIT_WARPS = 4, SPLIT_STAGES = 3;
+
+size_t gqa_split_smem_bytes()
+{
+    size_t ring = (size_t)SPLIT_WARPS * SPLIT_STAGES * 2 * GQA_TILE_BYTES;
+    size_t merge = (size_t)SPLIT_WARPS * GQA_GRP * (GQA_HD + 2) * 4;
+    return (ring > merge ? ring : merge) + 1024;
+}
+
+cudaError_t launch_gqa_prologue(const GqaPrologueArgs &a, int in_bf16, cudaStream_t st)
+{
+    dim3 grid(a.nq, a.H + a.KH);
+    if (in_bf16) gqa_prologue_kernel<__nv_bfloat16><<<grid, GQA_HD, 0, st>>>(a);
+    else gqa_prologue_kernel<float><<<grid, GQA_HD, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gqa_split(const CUtensorMap &tk, const CUtensorMap &tv, const GqaSplitArgs &a,
+                             cudaStream_t st)
+{
+    auto kern = gqa_split_kernel<SPLIT_WARPS, SPLIT_STAGES>;
+    const size_t smem = gqa_split_smem_bytes();
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    dim3 grid(a.n_splits, a.KH, a.nq);
+    kern<<<grid, SPLIT_WARPS * 32, smem, st>>>(tk, tv, a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gqa_combine(const GqaCombineArgs &a, int in_bf16, int out_bf16, cudaStream_t st)
+{
+    dim3 grid(a.nq, a.H);
+    if (in_bf16 && out_bf16) gqa_combine_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, GQA_HD, 0, st>>>(a);
+    else if (!in_bf16 && !out_bf16) gqa_combine_kernel<float, float><<<grid, GQA_HD, 0, st>>>(a);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+int gqa_pick_splits(int nq, int KH, int tmax, int num_sms)
+{
+    const int tiles = (tmax + GQA_TILE - 1) / GQA_TILE;
+    int best = 1;
+    double best_eff = -1.0;
+    for (int s = 1; s <= 256; ++s) {
+        const int per = (tiles + s - 1) / s;        // tiles per CTA
+        if (s > 1 && per < 2 * SPLIT_WARPS) break;  // keep every warp busy for >= 2 tiles
+        const long ctas = (long)nq * KH * s;
+        const long waves = (ctas + num_sms - 1) / num_sms;
+        // wave-quantisation efficiency, with a mild preference for fewer splits
+        const double eff = (double)ctas / (double)(waves * num_sms) - 0.002 * s;
+        if (eff > best_eff + 1e-9) { best_eff = eff; best = s; }
+    }
+    return best;
+}
+
+int gqa_chunk_for(int tmax, int n_splits)
+{
+    const int tiles = (tmax + GQA_TILE - 1) / GQA_TILE;
+    return ((tiles + n_splits - 1) / n_splits) * GQA_TILE;
+}
+
+}  // namespace coli

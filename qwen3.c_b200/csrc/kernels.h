@@ -1,0 +1,61 @@
+// Launch interfaces between the host backend (backend.cu) and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace coli {
+
+// ---------------------------------------------------------------- GDN decode
+struct GdnDecodeArgs {
+    const void *qkv;      // [B][CD] pre-conv (fused) or [B][in_stride] = qn|kn|v (prenorm)
+    const void *z;        // [B][VH*VD]
+    const void *a, *b;    // [B][VH] (fused)
+    const float *decay, *beta;  // [B][VH] (prenorm)
+    const float *conv_w;  // [CD][4]
+    const float *A_log, *dt_bias, *gnorm;
+    float *hist;          // [B][3][CD] conv history (fused)
+    float *state;         // [B][VH][KD][VD]
+    void *y;              // [B][VH*VD]
+    int B, KH, KD, VH, VD, in_stride;
+    float eps;
+};
+cudaError_t launch_gdn_decode(const GdnDecodeArgs &a, int in_bf16, int out_bf16, int prenorm,
+                              cudaStream_t st);
+
+// ---------------------------------------------------------------- GQA decode
+struct GqaPrologueArgs {
+    const void *qg;       // [nq][H][2*hd] raw q | gate
+    const void *k, *v;    // [nq][KH][hd] raw
+    const float *qnw, *knw;
+    const int *pos;       // [nq] position of each query row (sees rows 0..pos)
+    const int *creq;      // [nq] cache request of each query row (nullptr = identity)
+    __nv_bfloat16 *qout;  // [nq][H][hd] normed + roped q
+    __nv_bfloat16 *kcache, *vcache;  // [reqs][KH][max_t][hd]
+    int nq, H, KH, max_t, rot;
+    float eps, theta;
+};
+struct GqaSplitArgs {
+    const __nv_bfloat16 *q;  // [nq][H][hd] roped
+    const int *pos, *creq;
+    float *part_o;           // [nq][KH][n_splits][8][hd]
+    float *part_ml;          // [nq][KH][n_splits][8][2]
+    int nq, H, KH, max_t, n_splits, chunk;
+    float scale_log2;
+};
+struct GqaCombineArgs {
+    const float *part_o, *part_ml;
+    const void *qg;          // gate source [nq][H][2*hd]
+    void *ctx;               // [nq][H][hd]
+    int nq, H, KH, n_splits;
+};
+cudaError_t launch_gqa_prologue(const GqaPrologueArgs &a, int in_bf16, cudaStream_t st);
+cudaError_t launch_gqa_split(const CUtensorMap &tk, const CUtensorMap &tv, const GqaSplitArgs &a,
+                             cudaStream_t st);
+cudaError_t launch_gqa_combine(const GqaCombineArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
+size_t gqa_split_smem_bytes();
+int gqa_pick_splits(int nq, int KH, int tmax, int num_sms);
+int gqa_chunk_for(int tmax, int n_splits);
+
+}  // namespace coli
