@@ -1,0 +1,433 @@
+"""Benchmark of the qwen3.c token-mixer hot path on B200.
+
+Headline (BASELINE metric "decode attn-layer tok/s @32k ctx"): one gated GQA
+decode step of one full-attention layer for a batch of 64 requests, each at
+context 32768 (Qwen3.5-35B-A3B shapes: 16 Q / 2 KV heads, head_dim 256, bf16
+KV cache resident in HBM). One "step" = every request decodes one token
+through the layer's attention (q/k norm + RoPE + KV append + split-KV
+attention + gate). value = requests*GPUs / step time (tokens/s for the layer).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU: launched by torchrun, one rank per GPU; decode shards by request
+(each rank owns its own 64 requests and their KV cache, no collective on the
+data path) -> weak scaling. Timing: CUDA events on the launching stream,
+barrier + synchronize on both sides, max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B_REQ = 64          # requests per GPU
+T_CTX = 32768       # context length (cache rows per request, incl. the new token)
+H, KH, HD, ROT = 16, 2, 256, 64
+EPS, THETA = 1e-6, 1e7
+GDN_B = 256         # secondary: GatedDeltaNet decode batch
+GDN_BYTES_PER_REQ = 4_194_304 + 196_608 + 24_704 + 8_192
+
+
+def _pkg():
+    import __graft_entry__ as ge
+    return ge._pkg()
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, x):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_port_baseline(n_req=8):
+    """Oracle port (c/qwen.c:598-663 restated) on the host cores: one decode
+    token per request at context T_CTX, requests one after another (the
+    reference engine is single-sequence)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle
+    synth = _pkg().synth
+    orc = Oracle()
+    Kc = synth.bf16_round(synth.normal(1, (KH, T_CTX, HD)))
+    Vc = synth.bf16_round(synth.normal(2, (KH, T_CTX, HD)))
+    qn, kn = synth.normal(3, (HD,), std=0.1), synth.normal(4, (HD,), std=0.1)
+    t0 = time.perf_counter()
+    for r in range(n_req):
+        qg = synth.normal(10 + r, (1, H, 2 * HD))
+        k, v = synth.normal(100 + r, (1, KH, HD)), synth.normal(200 + r, (1, KH, HD))
+        orc.gqa_prologue(qg, k, v, qn, kn, T_CTX - 1, Kc, Vc)
+        orc.gqa_attend(qg, Kc, Vc, T_CTX - 1)
+    dt = time.perf_counter() - t0
+    return {"value": n_req / dt, "unit": "tok/s", "cores": orc.threads(), "kind": "port",
+            "sample": f"{n_req} requests x 1 decode token at context {T_CTX} (oracle/oracle.c "
+                      f"prologue+attend, OpenMP over heads as in c/qwen.c:640)"}
+
+
+def reference_arm(args):
+    """The reference's own attention() (c/qwen.c:581-666, compiled unmodified
+    into oracle/_ref) on the host cores, same workload shape; falls back to the
+    oracle port if the reference library was not built."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Reference
+    synth = _pkg().synth
+    if not Reference.available():
+        res = cpu_port_baseline()
+        kind, cores = "port", res["cores"]
+        step_fn = None
+    else:
+        kind = "reference"
+    D = 2048
+    per_step = 1
+    times = []
+    if kind == "reference":
+        ref = Reference()
+        cores = ref.threads()
+        Wq = synth.normal(1, (H * 2 * HD, D), std=0.02)
+        Wk = synth.normal(2, (KH * HD, D), std=0.02)
+        Wv = synth.normal(3, (KH * HD, D), std=0.02)
+        Wo = synth.normal(4, (D, H * HD), std=0.02)
+        qn, kn = synth.normal(5, (HD,), std=0.1), synth.normal(6, (HD,), std=0.1)
+        Kc = synth.normal(7, (KH, T_CTX, HD))
+        Vc = synth.normal(8, (KH, T_CTX, HD))
+
+        def step_fn(i):
+            for r in range(per_step):
+                x = synth.normal(1000 + i * per_step + r, (1, D))
+                ref.attention(x, T_CTX - 1, H, KH, HD, Wq, Wk, Wv, Wo, qn, kn, Kc, Vc)
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            step_fn(i)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        value = per_step * len(times) / sum(times)
+        sample = (f"{per_step} requests per step x 1 decode token at context {T_CTX}; each "
+                  "attention() call includes its q/k/v/o projections (D=2048)")
+    else:
+        value = res["value"]
+        sample = res["sample"]
+    line = {"metric": "decode attn-layer tok/s @32k ctx", "value": value, "unit": "tok/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def workload_config():
+    return {"workload": "gated GQA decode step, one full-attention layer (BASELINE config 2)",
+            "requests_per_gpu": B_REQ, "context": T_CTX, "q_heads": H, "kv_heads": KH,
+            "head_dim": HD, "kv_cache": "bf16 resident", "l2": "inputs larger than L2 (4.3 GB KV per step)"}
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args, ws, rank, local):
+    import torch
+    pkg = _pkg()
+    be = pkg.Backend(local)
+    torch.cuda.set_device(local)
+    st = torch.cuda.Stream()          # a real stream: the backend launches on it, events time it
+    torch.cuda.set_stream(st)
+    be.set_stream(st.cuda_stream)
+    peak_hbm, peak_tc, peak_kind = _peaks()
+
+    # ---- state: a 64-request bf16 KV cache at 32k context, random contents
+    layer = 0
+    be.kv_ensure(layer, B_REQ, KH, T_CTX)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    qn = (torch.randn(HD, generator=g, device="cuda") * 0.1).cpu().numpy()
+    kn = (torch.randn(HD, generator=g, device="cuda") * 0.1).cpu().numpy()
+    be.gqa_norm_weight(layer, qn, kn)
+    rows = torch.empty(KH * T_CTX, HD, dtype=torch.bfloat16, device="cuda")
+    rows2 = torch.empty_like(rows)
+    for r in range(B_REQ):
+        rows.normal_(generator=g)
+        rows2.normal_(generator=g)
+        be.kv_rows_dev(layer, r, 0, KH * T_CTX, rows.data_ptr(), rows2.data_ptr(), 1)
+    del rows, rows2
+    qg = torch.randn(B_REQ, H, 2 * HD, generator=g, device="cuda").bfloat16()
+    k = torch.randn(B_REQ, KH, HD, generator=g, device="cuda").bfloat16()
+    v = (torch.randn(B_REQ, KH, HD, generator=g, device="cuda") / 16).bfloat16()
+    pos = torch.full((B_REQ,), T_CTX - 1, dtype=torch.int32, device="cuda")
+    ctx = torch.empty(B_REQ, H, HD, dtype=torch.bfloat16, device="cuda")
+    be.sync()
+
+    def step():
+        be.gqa_decode_dev(layer, B_REQ, qg.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(),
+                          ctx.data_ptr(), H, KH, HD, ROT, EPS, THETA, 1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    launches0 = be.launch_count()
+    be.ktimer_enable(True)
+    be.ktimer_read(be.K_GQA_SPLIT)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    be.ktimer_enable(False)
+    be.sync()
+    ms_local = e0.elapsed_time(e1)
+    split_ms, split_n = be.ktimer_read(be.K_GQA_SPLIT)
+    comb_ms, comb_n = be.ktimer_read(be.K_GQA_COMBINE)
+    launches = be.launch_count() - launches0
+    barrier(ws)
+    ms = max_over_ranks(ws, ms_local)
+    ms_step = ms / args.steps
+    value = ws * B_REQ / (ms_step / 1e3)
+
+    # roofline of the dominant kernel (split-KV attention): algorithmic bytes =
+    # the K and V rows every request reads: B * KH * T * hd * 2 B * 2
+    split_bytes = B_REQ * KH * T_CTX * HD * 2 * 2
+    split_avg_s = split_ms / max(split_n, 1) / 1e3
+    achieved = split_bytes / split_avg_s / 1e9
+    step_bytes = B_REQ * (2048 * T_CTX + 2048 + 16384 + 8192)
+
+    # ---- e2e through the public host API (pinned fp32 host buffers)
+    e2e = run_e2e(be, layer, args, st)
+
+    secondary = run_gdn_secondary(be, args, st, peak_hbm)
+
+    if rank != 0:
+        return
+    line = {
+        "metric": "decode attn-layer tok/s @32k ctx", "value": value, "unit": "tok/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random bf16 KV cache and activations)",
+        "config": dict(workload_config(), parallelism=f"requests sharded over {ws} GPU(s), no collective"),
+        "roofline": {"bound": "hbm", "kernel": "gqa_split_kernel", "achieved": achieved,
+                     "peak": peak_hbm, "unit": "GB/s", "frac": achieved / peak_hbm,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "traffic": traffic_from_profile(), "bytes_per_launch": split_bytes,
+                     "avg_launch_us": split_avg_s * 1e6,
+                     "step_frac": step_bytes / (ms_step / 1e3) / 1e9 / peak_hbm},
+        "kernels_ms_per_step": {"gqa_split": split_ms / max(split_n, 1),
+                                "gqa_combine": comb_ms / max(comb_n, 1)},
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "secondary": secondary,
+    }
+    if not args.no_cpu:
+        line["cpu_baseline"] = cpu_port_baseline()
+    print(json.dumps(line))
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of gqa_split_kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gqa_split_decode_b64_t32k.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            return float(ln.split(":")[1])
+    return None
+
+
+def run_e2e(be, layer, args, st):
+    import torch
+    n = max(10, args.steps // 10)
+    qg = torch.randn(B_REQ, H, 2 * HD).pin_memory()
+    k = torch.randn(B_REQ, KH, HD).pin_memory()
+    v = (torch.randn(B_REQ, KH, HD) / 16).pin_memory()
+    pos = torch.full((B_REQ,), T_CTX - 1, dtype=torch.int32).pin_memory()
+    ctx = torch.empty(B_REQ, H, HD).pin_memory()
+    import ctypes
+    fp = ctypes.POINTER(ctypes.c_float)
+    ip = ctypes.POINTER(ctypes.c_int)
+
+    def call():
+        rc = be.lib.coli_cuda_gqa_decode(
+            layer, B_REQ, ctypes.cast(qg.data_ptr(), fp), ctypes.cast(k.data_ptr(), fp),
+            ctypes.cast(v.data_ptr(), fp), ctypes.cast(pos.data_ptr(), ip),
+            ctypes.cast(ctx.data_ptr(), fp), H, KH, HD, ROT, EPS, THETA)
+        if rc != 1:
+            raise RuntimeError(be.last_error())
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        call()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    h2d = qg.numel() * 4 + k.numel() * 4 + v.numel() * 4 + pos.numel() * 4
+    d2h = ctx.numel() * 4
+    return {"value": B_REQ / (ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": n,
+            "api": "coli_cuda_gqa_decode (fp32 host buffers, pinned)"}
+
+
+def run_gdn_secondary(be, args, st, peak_hbm):
+    """GatedDeltaNet decode at batch 256, bf16 activations."""
+    import torch
+    KHg, KD, VHg, VD = 16, 128, 32, 128
+    CD = 2 * KHg * KD + VHg * VD
+    g = torch.Generator(device="cuda").manual_seed(99)
+    be.gdn_setup(0, GDN_B, (torch.randn(CD, 4, generator=g, device="cuda") * 0.3).cpu().numpy(),
+                 (torch.rand(VHg, generator=g, device="cuda") * 2.77).cpu().numpy(),
+                 torch.randn(VHg, generator=g, device="cuda").cpu().numpy(),
+                 (1 + 0.1 * torch.randn(VD, generator=g, device="cuda")).cpu().numpy())
+    qkv = torch.randn(GDN_B, CD, generator=g, device="cuda").bfloat16()
+    z = torch.randn(GDN_B, VHg * VD, generator=g, device="cuda").bfloat16()
+    a = torch.randn(GDN_B, VHg, generator=g, device="cuda").bfloat16()
+    b = torch.randn(GDN_B, VHg, generator=g, device="cuda").bfloat16()
+    y = torch.empty(GDN_B, VHg * VD, dtype=torch.bfloat16, device="cuda")
+    n = max(20, args.steps // 5)
+
+    def step():
+        be.gdn_decode_dev(0, GDN_B, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
+                          y.data_ptr(), 16, 128, 32, 128, 1e-6, 1)
+    for _ in range(max(3, args.warmup)):
+        step()
+    be.sync()
+    be.ktimer_enable(True)
+    be.ktimer_read(be.K_GDN_DECODE)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    be.ktimer_enable(False)
+    kms, kn = be.ktimer_read(be.K_GDN_DECODE)
+    ms = e0.elapsed_time(e1) / n
+    bytes_ = GDN_B * GDN_BYTES_PER_REQ
+    kavg = kms / max(kn, 1)
+    return {"gdn_decode": {"metric": "GDN decode tok/s (one layer)", "batch": GDN_B,
+                           "value": GDN_B / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+                           "kernel_us": kavg * 1e3,
+                           "achieved_GBs": bytes_ / (kavg / 1e3) / 1e9,
+                           "frac_of_hbm": bytes_ / (kavg / 1e3) / 1e9 / peak_hbm,
+                           "bytes_per_step": bytes_}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            reference_arm(args)
+        return
+    ws, rank, local = dist_setup()
+    run_ours(args, ws, rank, local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -85,6 +85,10 @@ int  coli_cuda_kv_row(int layer, int req, int row, const float *k, const float *
 int  coli_cuda_kv_rows(int layer, int req, int row0, int n, const float *k, const float *v);
 int  coli_cuda_kv_read(int layer, int req, int row0, int n, float *k, float *v);
 void coli_cuda_kv_reset(void);
+/* New: n rows from device memory (dtype 0 fp32 / 1 bf16), e.g. rows an
+ * engine-side prefill produced on the GPU. Asynchronous on the backend stream. */
+int  coli_cuda_kv_rows_dev(int layer, int req, int row0, int n, const void *k, const void *v,
+                           int dtype);
 /* New: device base pointers of a layer's bf16 K and V caches. */
 int  coli_cuda_kv_device_ptr(int layer, void **k, void **v);
 /* Resident q_norm / k_norm weights [hd] of a full layer:

@@ -44,6 +44,7 @@ SIGNATURES = {
     "coli_cuda_kv_rows": ([_i, _i, _i, _i, _fp, _fp], _i),
     "coli_cuda_kv_read": ([_i, _i, _i, _i, _fp, _fp], _i),
     "coli_cuda_kv_reset": ([], None),
+    "coli_cuda_kv_rows_dev": ([_i] * 4 + [_vp, _vp, _i], _i),
     "coli_cuda_kv_device_ptr": ([_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp)], _i),
     "coli_cuda_gqa_norm_weight": ([_i, _fp, _fp, _i], _i),
     "coli_cuda_gqa": ([_i, _fp, _fp] + [_i] * 7 + [_f], _i),
@@ -163,6 +164,9 @@ class Backend:
         self._ok(self.lib.coli_cuda_kv_read(layer, req, row0, n, k.ctypes.data_as(_fp),
                                             v.ctypes.data_as(_fp)), "kv_read")
         return k, v
+
+    def kv_rows_dev(self, layer, req, row0, n, k_ptr, v_ptr, dtype=1):
+        self._ok(self.lib.coli_cuda_kv_rows_dev(layer, req, row0, n, k_ptr, v_ptr, dtype), "kv_rows_dev")
 
     def kv_reset(self):
         self.lib.coli_cuda_kv_reset()

@@ -22,6 +22,7 @@
 
 #include "gdn_decode.cu"
 #include "gqa_decode.cu"
+#include "gqa_prefill.cu"
 
 namespace {
 
@@ -39,7 +40,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
 struct KvLayer {
     __nv_bfloat16 *k = nullptr, *v = nullptr;
     int batch = 0, KH = 0, max_t = 0, hd = 0;
-    CUtensorMap tmK, tmV;
+    CUtensorMap tmK, tmV;      // 16-row boxes (decode)
+    CUtensorMap tmK64, tmV64;  // 64-row boxes (prefill)
     float *qnw = nullptr, *knw = nullptr;  // [hd] resident norm weights
 };
 
@@ -166,16 +168,30 @@ void *scratch(Slot s, size_t bytes)
 
 int check_layer(int layer) { return layer >= 0 && layer < MAX_LAYERS; }
 
-int make_kv_tmap(CUtensorMap *m, void *base, int rows, int hd)
+int make_kv_tmap(CUtensorMap *m, void *base, int rows, int hd, int box_rows = 16)
 {
     cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
-    cuuint32_t box[2] = {64, 16};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = G.encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 1;
+}
+
+// Roped bf16 q [S][H][hd] as a 3D map (d, head, row) with 64 x 1 x 128 boxes.
+int make_q_tmap(CUtensorMap *m, void *base, int S, int H, int hd)
+{
+    cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)S};
+    cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)H * hd * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = G.encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled (q) failed (%d)", (int)r);
     return 1;
 }
 
@@ -264,10 +280,14 @@ int gqa_shape_ok(KvLayer &L, int H, int KH, int hd)
     return 1;
 }
 
+constexpr int PREFILL_MIN_ROWS = 64;
+int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void *qg, void *ctx,
+                     int in_bf16, int out_bf16, float scale);
+
 // prologue + attention for nq rows (pos_d/creq_d on device)
 int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, const int *pos_d,
              const int *creq_d, int tmax, void *ctx, int H, int KH, int hd, int rot, float eps,
-             float theta, int in_bf16, int out_bf16)
+             float theta, int in_bf16, int out_bf16, int prefill_req = -1, int pos_base = 0)
 {
     KvLayer &L = G.kv[layer];
     if (!gqa_shape_ok(L, H, KH, hd)) return 0;
@@ -282,7 +302,27 @@ int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, co
     pa.nq = nq; pa.H = H; pa.KH = KH; pa.max_t = L.max_t; pa.rot = rot; pa.eps = eps; pa.theta = theta;
     CK(launch_gqa_prologue(pa, in_bf16, stream()));
     g_launches += 1;
+    if (prefill_req >= 0 && nq >= PREFILL_MIN_ROWS)
+        return gqa_prefill_rows(L, prefill_req, nq, pos_base, H, qg, ctx, in_bf16, out_bf16,
+                                1.f / sqrtf((float)hd));
     return gqa_attend(L, nq, H, pos_d, creq_d, tmax, qg, ctx, in_bf16, out_bf16, 1.f / sqrtf((float)hd));
+}
+
+// Causal prefill of S rows of one request on the tensor cores; the roped bf16
+// q is already in S_Q and the new K/V rows are in the cache.
+int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void *qg, void *ctx,
+                     int in_bf16, int out_bf16, float scale)
+{
+    CUtensorMap tq;
+    if (!make_q_tmap(&tq, G.slot[S_Q], S, H, L.hd)) return 0;
+    GqaPrefillArgs a;
+    a.qg = qg; a.ctx = ctx; a.S = S; a.H = H; a.KH = L.KH; a.max_t = L.max_t; a.req = req;
+    a.pos_base = pos_base; a.n_qtiles = (S + 127) / 128; a.scale_log2 = scale * 1.4426950408889634f;
+    kt_mark(COLI_K_GQA_PREFILL);
+    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, in_bf16, out_bf16, stream()));
+    kt_mark(COLI_K_GQA_PREFILL);
+    g_launches += 1;
+    return 1;
 }
 
 // ---------------------------------------------------------------- GDN helpers
@@ -464,6 +504,8 @@ int coli_cuda_kv_ensure(int layer, int batch, int KH, int max_t, int hd)
     L.batch = batch; L.KH = KH; L.max_t = max_t; L.hd = hd;
     if (!make_kv_tmap(&L.tmK, L.k, batch * KH * max_t, hd)) return 0;
     if (!make_kv_tmap(&L.tmV, L.v, batch * KH * max_t, hd)) return 0;
+    if (!make_kv_tmap(&L.tmK64, L.k, batch * KH * max_t, hd, 64)) return 0;
+    if (!make_kv_tmap(&L.tmV64, L.v, batch * KH * max_t, hd, 64)) return 0;
     return 1;
 }
 
@@ -505,6 +547,29 @@ int coli_cuda_kv_rows(int layer, int req, int row0, int n, const float *k, const
 int coli_cuda_kv_read(int layer, int req, int row0, int n, float *k, float *v)
 {
     return kv_rows_impl(layer, req, row0, n, k, v, 1);
+}
+
+__global__ void rows_to_bf16_kernel(const void *src, __nv_bfloat16 *dst, size_t n, int bf16)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = bf16 ? static_cast<const __nv_bfloat16 *>(src)[i]
+                      : __float2bfloat16_rn(static_cast<const float *>(src)[i]);
+}
+
+int coli_cuda_kv_rows_dev(int layer, int req, int row0, int n, const void *k, const void *v, int dtype)
+{
+    READY();
+    if (!check_layer(layer) || !G.kv[layer].k) return fail("KV layer %d not allocated", layer);
+    KvLayer &L = G.kv[layer];
+    if (req < 0 || req >= L.batch || row0 < 0 || n < 0 || row0 + n > L.KH * L.max_t) return fail("KV row range out of bounds");
+    if (n == 0) return 1;
+    const size_t base = ((size_t)req * L.KH * L.max_t + row0) * L.hd;
+    const size_t cnt = (size_t)n * L.hd;
+    const int blocks = (int)((cnt + 255) / 256 < 4096 ? (cnt + 255) / 256 : 4096);
+    if (k) { rows_to_bf16_kernel<<<blocks, 256, 0, stream()>>>(k, L.k + base, cnt, dtype); CK(cudaGetLastError()); }
+    if (v) { rows_to_bf16_kernel<<<blocks, 256, 0, stream()>>>(v, L.v + base, cnt, dtype); CK(cudaGetLastError()); }
+    g_launches += (k != nullptr) + (v != nullptr);
+    return 1;
 }
 
 void coli_cuda_kv_reset(void)
@@ -568,7 +633,11 @@ int coli_cuda_gqa(int layer, const float *q, float *ctx, int S, int H, int KH, i
     split_q_kernel<<<S * H, hd, 0, stream()>>>(qd, qb, S * H, hd);
     CK(cudaGetLastError());
     g_launches += 2;
-    if (!gqa_attend(L, S, H, pos_d, creq_d, T, qd, out, 0, 0, scale)) return 0;
+    if (S >= PREFILL_MIN_ROWS) {
+        if (!gqa_prefill_rows(L, 0, S, T - S, H, qd, out, 0, 0, scale)) return 0;
+    } else if (!gqa_attend(L, S, H, pos_d, creq_d, T, qd, out, 0, 0, scale)) {
+        return 0;
+    }
     if (!download(ctx, out, (size_t)S * H * hd * 4)) return 0;
     return check_dev_error();
 }
@@ -608,7 +677,7 @@ int coli_cuda_gqa_step_dev(int layer, int req, int S, int pos_base, const void *
     CK(cudaGetLastError());
     g_launches += 1;
     return gqa_rows(layer, S, qg, k, v, pos_d, creq_d, pos_base + S, ctx, H, KH, hd, rot, eps, theta,
-                    dtype, dtype);
+                    dtype, dtype, req, pos_base);
 }
 
 int coli_cuda_gqa_decode(int layer, int B, const float *qg, const float *k, const float *v,

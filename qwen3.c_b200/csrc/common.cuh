@@ -54,10 +54,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait; returns false (and raises error 1) on time-out.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait; returns false (and raises error 1) after COLI_WAIT_NS of
+// polling (or COLI_SPIN_LIMIT polls, whichever comes first).
+#ifndef COLI_WAIT_NS
+#define COLI_WAIT_NS 2000000000ull
+#endif
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < COLI_SPIN_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1; i < COLI_SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 0) {
+            if (globaltimer_ns() - t0 > COLI_WAIT_NS) break;
+            if (*(volatile int *)&g_dev_error) return false;  // another CTA gave up: bail out
+        }
+    }
     raise_error(1);
     return false;
 }

@@ -59,3 +59,15 @@ int gqa_pick_splits(int nq, int KH, int tmax, int num_sms);
 int gqa_chunk_for(int tmax, int n_splits);
 
 }  // namespace coli
+
+namespace coli {
+// ---------------------------------------------------------------- GQA prefill
+struct GqaPrefillArgs {
+    const void *qg;   // [S][H][2*hd] raw q | gate (gate read in the epilogue)
+    void *ctx;        // [S][H][hd]
+    int S, H, KH, max_t, req, pos_base, n_qtiles;
+    float scale_log2;
+};
+cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+                               const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
+}  // namespace coli

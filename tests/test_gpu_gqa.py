@@ -159,3 +159,26 @@ def test_bf16_device_path(be, orc):
         orc.gqa_prologue(q1, k1, v[r:r + 1].copy(), qnw, knw, T - 1, Kc, Vc)
         want = orc.gqa_attend(q1, Kc, Vc, T - 1)
         assert_close(ctx[r].float().cpu().numpy(), want[0], what=f"bf16 req {r}")
+
+
+@pytest.mark.parametrize("S,pos_base", [(64, 0), (1000, 0), (200, 77), (130, 4000)])
+def test_tensor_core_prefill_vs_oracle(be, orc, S, pos_base):
+    """S >= 64 rows of one request run the tcgen05 prefill kernel."""
+    cfg = f"gqa_tc_prefill_{S}_{pos_base}"
+    max_t = pos_base + S + 5
+    be.kv_ensure(6, 1, KH, max_t)
+    qnw, knw = _norm_w(cfg)
+    be.gqa_norm_weight(6, qnw, knw)
+    Kc, Vc = _cache(cfg, max_t)
+    Kc[:, pos_base:] = 0
+    Vc[:, pos_base:] = 0
+    if pos_base:
+        _upload(be, 6, 0, Kc, Vc, pos_base)
+    qg = synth.normal(synth.seed_of(cfg, "qg"), (S, H, 2 * HD))
+    k = synth.normal(synth.seed_of(cfg, "k"), (S, KH, HD))
+    v = synth.normal(synth.seed_of(cfg, "v"), (S, KH, HD))
+    ctx = be.gqa_step(6, 0, pos_base, qg, k, v)
+    q1, k1 = qg.copy(), k.copy()
+    orc.gqa_prologue(q1, k1, v.copy(), qnw, knw, pos_base, Kc, Vc)
+    want = orc.gqa_attend(q1, synth.bf16_round(Kc), synth.bf16_round(Vc), pos_base)
+    assert_close(ctx, want, what=f"tc prefill S={S} pos_base={pos_base}")
