@@ -128,6 +128,21 @@ int  coli_cuda_gqa_decode_dev(int layer, int B, const void *qg, const void *k, c
                               const int *pos_dev, void *ctx, int H, int KH, int hd, int rot,
                               float eps, float theta, int dtype);
 
+/* ---- No counterpart in the reference. Batched GQA decode that allocates no
+ * device memory, for callers that cannot call cudaMalloc while serving (a
+ * memory budget fixed at start-up, or no allocation allowed once decoding
+ * runs). Same arguments and results as coli_cuda_gqa_decode_dev (device
+ * pointers, pos on the device, dtype 0 fp32 / 1 bf16). Its intermediates live
+ * in one fixed 8 MiB device array inside the library, which every GPU that
+ * loads the library holds until exit; a call whose batch does not fit returns
+ * 0 with the limit in the error message (about 340 requests). The first call
+ * on a device looks up that array's device address, so make it before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * race. */
+int  coli_cuda_gqa_decode_noalloc(int layer, int B, const void *qg, const void *k, const void *v,
+                                  const int *pos_dev, void *ctx, int H, int KH, int hd, int rot,
+                                  float eps, float theta, int dtype);
+
 /* ---- GatedDeltaNet state: coli_vk_gdn_state_ensure / coli_vk_gdn_reset
  * (c/backend_vulkan.h:152-153), coli_vk_gdn_conv_ensure / _weight (:266-267),
  * coli_vk_gdn_ba_weight (:206) for the per-layer A_log, dt_bias, gnorm.

@@ -52,6 +52,7 @@ SIGNATURES = {
     "coli_cuda_gqa_step_dev": ([_i] * 4 + [_vp] * 4 + [_i] * 4 + [_f, _f, _i], _i),
     "coli_cuda_gqa_decode": ([_i, _i, _fp, _fp, _fp, _ip, _fp] + [_i] * 4 + [_f, _f], _i),
     "coli_cuda_gqa_decode_dev": ([_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 4 + [_f, _f, _i], _i),
+    "coli_cuda_gqa_decode_noalloc": ([_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 4 + [_f, _f, _i], _i),
     "coli_cuda_gdn_state_ensure": ([_i] * 5, _i),
     "coli_cuda_gdn_conv_ensure": ([_i] * 4, _i),
     "coli_cuda_gdn_conv_weight": ([_i, _fp, _i, _i], _i),
@@ -222,6 +223,11 @@ class Backend:
                        theta=1e7, dtype=1):
         self._ok(self.lib.coli_cuda_gqa_decode_dev(layer, B, qg, k, v, pos, ctx, H, KH, hd, rot, eps,
                                                    theta, dtype), "gqa_decode_dev")
+
+    def gqa_decode_noalloc(self, layer, B, qg, k, v, pos, ctx, H=16, KH=2, hd=256, rot=64,
+                           eps=1e-6, theta=1e7, dtype=1):
+        self._ok(self.lib.coli_cuda_gqa_decode_noalloc(layer, B, qg, k, v, pos, ctx, H, KH, hd, rot,
+                                                       eps, theta, dtype), "gqa_decode_noalloc")
 
     def gqa_step_dev(self, layer, req, S, pos_base, qg, k, v, ctx, H=16, KH=2, hd=256, rot=64,
                      eps=1e-6, theta=1e7, dtype=1):

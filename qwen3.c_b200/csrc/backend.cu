@@ -947,3 +947,6 @@ int coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const flo
 }
 
 }  // extern "C"
+
+// Fixed-scratch decode entry point (no device allocation on its path).
+#include "noalloc.cu"
