@@ -285,9 +285,12 @@ def run_ours(args, ws, rank, local):
     step_bytes = B_REQ * (2048 * T_CTX + 2048 + 16384 + 8192)
 
     # ---- e2e through the public host API (pinned fp32 host buffers)
-    e2e = run_e2e(be, layer, args, st)
-
-    secondary = run_gdn_secondary(be, args, st, peak_hbm)
+    e2e = run_e2e(be, layer, args, st) if not args.quick else None
+    secondary = {}
+    if not args.quick:
+        be.kv_reset()
+        secondary.update(run_gdn_secondary(be, args, st, peak_hbm))
+        secondary.update(run_prefill_secondary(be, args, st, peak_tc))
 
     if rank != 0:
         return
@@ -406,6 +409,52 @@ def run_gdn_secondary(be, args, st, peak_hbm):
                            "bytes_per_step": bytes_}}
 
 
+def run_prefill_secondary(be, args, st, peak_tc):
+    """Causal gated-GQA prefill of one layer, S in {8192,
+    32768}, batch 1, bf16 q/k/v ~ N(0,1): prologue + tcgen05 flash kernel."""
+    import torch
+    out = {}
+    layer = 1
+    for S in (8192, 32768):
+        be.kv_ensure(layer, 1, KH, S)
+        g = torch.Generator(device="cuda").manual_seed(S)
+        be.gqa_norm_weight(layer, (0.1 * torch.randn(HD, generator=g, device="cuda")).cpu().numpy(),
+                           (0.1 * torch.randn(HD, generator=g, device="cuda")).cpu().numpy())
+        qg = torch.randn(S, H, 2 * HD, generator=g, device="cuda").bfloat16()
+        k = torch.randn(S, KH, HD, generator=g, device="cuda").bfloat16()
+        v = torch.randn(S, KH, HD, generator=g, device="cuda").bfloat16()
+        ctx = torch.empty(S, H, HD, dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            be.gqa_step_dev(layer, 0, S, 0, qg.data_ptr(), k.data_ptr(), v.data_ptr(),
+                            ctx.data_ptr(), H, KH, HD, ROT, EPS, THETA, 1)
+        for _ in range(3):
+            step()
+        be.sync()
+        reps = 10 if S <= 8192 else 4
+        be.ktimer_enable(True)
+        be.ktimer_read(be.K_GQA_PREFILL)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        be.ktimer_enable(False)
+        kms, kn = be.ktimer_read(be.K_GQA_PREFILL)
+        ms = e0.elapsed_time(e1) / reps
+        flops = 8192.0 * S * (S + 1)
+        kavg = kms / max(kn, 1)
+        out[f"gqa_prefill_{S}"] = {
+            "metric": "GQA prefill tok/s (one layer, causal)", "S": S, "value": S / (ms / 1e3),
+            "unit": "tok/s", "ms_per_call": ms, "kernel_ms": kavg,
+            "achieved_TFLOPs": flops / (kavg / 1e3) / 1e12,
+            "frac_of_bf16_peak": flops / (kavg / 1e3) / 1e12 / peak_tc}
+        del qg, k, v, ctx
+        be.kv_reset()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -413,7 +462,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--requests", type=int, default=B_REQ, help="decode requests per GPU")
+    ap.add_argument("--context", type=int, default=T_CTX, help="decode context length")
+    ap.add_argument("--quick", action="store_true",
+                    help="headline kernel only (no e2e / secondary / CPU legs), for profiling")
     args = ap.parse_args()
+    globals()["B_REQ"], globals()["T_CTX"] = args.requests, args.context
+    if args.quick:
+        args.no_cpu = True
     if args.warmup < 3:
         args.warmup = 3
     ws = int(os.environ.get("WORLD_SIZE", "1"))
