@@ -23,6 +23,7 @@
 #include "gdn_decode.cu"
 #include "gqa_decode.cu"
 #include "gqa_prefill.cu"
+#include "gdn_prefill.cu"
 
 namespace {
 
@@ -57,7 +58,7 @@ struct GdnLayer {
 
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
-            S_COUNT };
+            S_GQ, S_GK, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -357,6 +358,59 @@ int gdn_decode_run(int layer, int B, int req0, const void *qkv, const void *z, c
     CK(launch_gdn_decode(ga, bf16, bf16, 0, stream()));
     kt_mark(COLI_K_GDN_DECODE);
     g_launches += 1;
+    return 1;
+}
+
+int make_f32_3d(CUtensorMap *m, void *base, int d0, int d1, int d2, int box0, int box1)
+{
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)d0 * 4, (cuuint64_t)d0 * d1 * 4};
+    cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = G.encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled (fp32 3d) failed (%d)", (int)r);
+    return 1;
+}
+
+// Chunk-parallel GDN prefill (gdn_prefill.cu) for S >= GDN_CHUNK_MIN_ROWS.
+constexpr int GDN_CHUNK_MIN_ROWS = 64;
+int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *z, const void *a,
+                        const void *b, void *y, int KH, int KD, int VH, int VD, float eps, int dtype)
+{
+    GdnLayer &L = G.gdn[layer];
+    if (!gdn_shape_ok(L, KH, KD, VH, VD, 1)) return 0;
+    if (req < 0 || req >= L.batch || req >= L.hbatch) return fail("request out of range");
+    const int nch = (S + 63) / 64;
+    GdnPrefillArgs p;
+    memset(&p, 0, sizeof(p));
+    p.qkv = qkv; p.z = z; p.a = a; p.b = b;
+    p.conv_w = L.conv_w; p.A_log = L.A_log; p.dt_bias = L.dt_bias; p.gnorm = L.gnorm;
+    p.hist = L.hist + (size_t)req * 3 * L.conv_dim;
+    p.state = L.state + (size_t)req * VH * KD * VD;
+    p.y = y;
+    p.Qh = (float *)scratch(S_GQ, (size_t)KH * S * 128 * 4);
+    p.Kh = (float *)scratch(S_GK, (size_t)KH * S * 128 * 4);
+    p.Vh = (float *)scratch(S_GV, (size_t)VH * S * 128 * 4);
+    p.GL = (float *)scratch(S_GL, (size_t)VH * S * 4);
+    p.BETA = (float *)scratch(S_GB, (size_t)VH * S * 4);
+    p.W = (float *)scratch(S_GW, (size_t)nch * VH * 64 * 128 * 4);
+    p.U = (float *)scratch(S_GU, (size_t)nch * VH * 64 * 128 * 4);
+    p.M = (float *)scratch(S_GM, (size_t)nch * VH * 64 * 64 * 4);
+    if (!p.Qh || !p.Kh || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M) return 0;
+    p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
+    GdnPrefillMaps m;
+    if (!make_f32_3d(&m.Q, p.Qh, 128, S, KH, 32, 64) || !make_f32_3d(&m.K, p.Kh, 128, S, KH, 32, 64) ||
+        !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
+        !make_f32_3d(&m.W, p.W, 128, 64, nch * VH, 32, 64) ||
+        !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||
+        !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64))
+        return 0;
+    kt_mark(COLI_K_GDN_PREFILL);
+    CK(launch_gdn_prefill(p, m, dtype, stream()));
+    kt_mark(COLI_K_GDN_PREFILL);
+    g_launches += 4;
     return 1;
 }
 
@@ -914,7 +968,9 @@ int coli_cuda_gdn_prefill_dev(int layer, int req, int S, const void *qkv, const 
     READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
     if (S < 1) return fail("bad S");
-    // Sequential token steps through the fused decode kernel (exact recurrence).
+    if (S >= GDN_CHUNK_MIN_ROWS)
+        return gdn_prefill_chunked(layer, req, S, qkv, z, a, b, y, KH, KD, VH, VD, eps, dtype);
+    // Short runs: sequential token steps through the fused decode kernel.
     const int CD = 2 * KH * KD + VH * VD;
     const size_t es = dtype ? 2 : 4;
     for (int s = 0; s < S; ++s) {

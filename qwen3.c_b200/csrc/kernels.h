@@ -71,3 +71,26 @@ struct GqaPrefillArgs {
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
 }  // namespace coli
+
+namespace coli {
+// ---------------------------------------------------------------- GDN prefill
+struct GdnPrefillArgs {
+    const void *qkv, *z, *a, *b;          // [S][CD], [S][VH*VD], [S][VH], [S][VH]
+    const float *conv_w, *A_log, *dt_bias, *gnorm;
+    float *hist;                          // [3][CD] of the request (read, then rewritten)
+    float *state;                         // [VH][KD][VD] of the request (in/out)
+    void *y;                              // [S][VH*VD]
+    float *Qh, *Kh;                       // scratch [KH][S][128]
+    float *Vh;                            // scratch [VH][S][128]
+    float *GL, *BETA;                     // scratch [VH][S]
+    float *W, *U;                         // scratch [nchunks][VH][64][128]
+    float *M;                             // scratch [nchunks][VH][64][64]
+    int S, KH, VH;
+    float eps;
+};
+struct GdnPrefillMaps {
+    CUtensorMap Q, K, V, W, U, M;
+};
+cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
+                               cudaStream_t st);
+}  // namespace coli

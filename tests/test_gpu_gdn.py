@@ -92,7 +92,7 @@ def test_prenormalised_mirror(be, orc):
 
 
 def test_state_after_4096_steps(be, orc):
-    """North-star state parity: rel-L2 <= 1e-3 after 4096 sequential steps."""
+    """North-star state parity: rel-L2 <= 1e-3 after 4096 sequential decode steps."""
     cfg = "gdn_4096"
     S = 4096
     prm = gdn_params(cfg)
@@ -102,10 +102,30 @@ def test_state_after_4096_steps(be, orc):
     s_ref, r_ref = state.copy(), ring.copy()
     y_ref = orc.gdn_seq(ins["qkv"], ins["z"], ins["a"], ins["b"], prm["conv_w"], prm["A_log"],
                         prm["dt_bias"], prm["gnorm"], r_ref, s_ref, KH=KH_G, KD=KD)
-    y = be.gdn_prefill(3, 0, ins["qkv"], ins["z"], ins["a"], ins["b"])
+    y = np.concatenate([be.gdn_decode(3, ins["qkv"][t:t + 1], ins["z"][t:t + 1], ins["a"][t:t + 1],
+                                      ins["b"][t:t + 1]) for t in range(S)])
     err = rel_l2(be.gdn_state_get(3, 0), s_ref)
     assert err <= STATE_REL_L2, err
     assert_close(y[-64:], y_ref[-64:], what="last outputs")
+
+
+@pytest.mark.parametrize("S", [64, 100, 1000, 4096])
+def test_chunked_prefill_vs_sequential_oracle(be, orc, S):
+    """S >= 64 tokens run the chunk-parallel kernels; the oracle is the
+    reference's token-by-token recurrence from the same carried state."""
+    cfg = f"gdn_chunked_{S}"
+    prm = gdn_params(cfg)
+    state, ring = gdn_state0(cfg)
+    _setup(be, 5, 1, prm, [(state, ring)])
+    ins = gdn_inputs(cfg, S)
+    s_ref, r_ref = state.copy(), ring.copy()
+    y_ref = orc.gdn_seq(ins["qkv"], ins["z"], ins["a"], ins["b"], prm["conv_w"], prm["A_log"],
+                        prm["dt_bias"], prm["gnorm"], r_ref, s_ref, KH=KH_G, KD=KD)
+    y = be.gdn_prefill(5, 0, ins["qkv"], ins["z"], ins["a"], ins["b"])
+    assert_close(y, y_ref, what=f"chunked prefill S={S}")
+    err = rel_l2(be.gdn_state_get(5, 0), s_ref)
+    assert err <= 1e-2, err
+    np.testing.assert_array_equal(be.gdn_conv_get(5, 0)[1:], r_ref[1:])
 
 
 def test_bf16_device_path(be, orc):
