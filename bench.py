@@ -225,6 +225,14 @@ def run_ours(args, ws, rank, local):
     torch.cuda.set_stream(st)
     be.set_stream(st.cuda_stream)
     peak_hbm, peak_tc, peak_kind = _peaks()
+    if args.only:  # one secondary leg alone (profiling runs)
+        fn = {"gdn": run_gdn_secondary, "prefill": run_prefill_secondary,
+              "gdnprefill": run_gdn_prefill_secondary, "stack": run_stack_decode,
+              "stackprefill": run_stack_prefill}[args.only]
+        res = fn(be, args, st, peak_tc if args.only in ("prefill", "stackprefill") else peak_hbm)
+        if rank == 0:
+            print(json.dumps(res))
+        return
 
     # ---- state: a 64-request bf16 KV cache at 32k context, random contents
     layer = 0
@@ -291,6 +299,7 @@ def run_ours(args, ws, rank, local):
         be.kv_reset()
         secondary.update(run_gdn_secondary(be, args, st, peak_hbm))
         secondary.update(run_prefill_secondary(be, args, st, peak_tc))
+        secondary.update(run_gdn_prefill_secondary(be, args, st, peak_hbm))
 
     if rank != 0:
         return
@@ -415,7 +424,7 @@ def run_prefill_secondary(be, args, st, peak_tc):
     import torch
     out = {}
     layer = 1
-    for S in (8192, 32768):
+    for S in [int(x) for x in args.lengths.split(",")]:
         be.kv_ensure(layer, 1, KH, S)
         g = torch.Generator(device="cuda").manual_seed(S)
         be.gqa_norm_weight(layer, (0.1 * torch.randn(HD, generator=g, device="cuda")).cpu().numpy(),
@@ -455,6 +464,130 @@ def run_prefill_secondary(be, args, st, peak_tc):
     return out
 
 
+def run_gdn_prefill_secondary(be, args, st, peak_hbm):
+    """GatedDeltaNet chunk-64 prefill of one layer, batch 1,
+    bf16 inputs, zero initial state and conv history, fp32 state.
+    Algorithmic bytes = S x 32,896 (qkv, z, a, b in; y out; bf16) + 2 MiB state."""
+    import torch
+    KHg, KD, VHg, VD = 16, 128, 32, 128
+    CD = 2 * KHg * KD + VHg * VD
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(7)
+    be.gdn_setup(2, 1, (torch.randn(CD, 4, generator=g, device="cuda") * 0.3).cpu().numpy(),
+                 (torch.rand(VHg, generator=g, device="cuda") * 2.77).cpu().numpy(),
+                 torch.randn(VHg, generator=g, device="cuda").cpu().numpy(),
+                 (1 + 0.1 * torch.randn(VD, generator=g, device="cuda")).cpu().numpy())
+    for S in [int(x) for x in args.lengths.split(",")]:
+        qkv = torch.randn(S, CD, generator=g, device="cuda").bfloat16()
+        z = torch.randn(S, VHg * VD, generator=g, device="cuda").bfloat16()
+        a = torch.randn(S, VHg, generator=g, device="cuda").bfloat16()
+        b = torch.randn(S, VHg, generator=g, device="cuda").bfloat16()
+        y = torch.empty(S, VHg * VD, dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            be.gdn_reset()
+            be.gdn_prefill_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
+                               y.data_ptr(), KHg, KD, VHg, VD, 1e-6, 1)
+        for _ in range(2):
+            step()
+        be.sync()
+        reps = 5
+        be.ktimer_enable(True)
+        be.ktimer_read(be.K_GDN_PREFILL)
+        tot = 0.0
+        for _ in range(reps):
+            be.gdn_reset()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            be.gdn_prefill_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
+                               y.data_ptr(), KHg, KD, VHg, VD, 1e-6, 1)
+            e1.record(st)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        be.ktimer_enable(False)
+        be.ktimer_read(be.K_GDN_PREFILL)
+        ms = tot / reps
+        bytes_ = S * 32896 + 2 * 1024 * 1024
+        out[f"gdn_prefill_{S}"] = {
+            "metric": "GDN chunked prefill tok/s (one layer)", "S": S, "value": S / (ms / 1e3),
+            "unit": "tok/s", "ms_per_call": ms, "achieved_GBs": bytes_ / (ms / 1e3) / 1e9,
+            "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm}
+        del qkv, z, a, b, y
+    return out
+
+
+def _dist():
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(), dist.get_rank()
+    return 1, 0
+
+
+def run_stack_decode(be, args, st, peak_hbm):
+    """BASELINE config 5 (i): the 40-layer mixer stack (30 GDN + 10 gated GQA)
+    decoding one token for a batch of 256 requests at context 32768, sharded
+    by request over the GPUs (no collective on the data path). 256 requests do
+    not fit one GPU (~175 GiB of KV + state), so one GPU runs 128 and the
+    per-request rate is what scales."""
+    import torch
+    pkg = _pkg()
+    ws, rank = _dist()
+    total = args.stack_batch
+    b0, b1 = pkg.sharding.request_shard(total, ws, rank)
+    B = min(b1 - b0, 128)
+    stack = pkg.stack.MixerStack(be, seed=1000 + rank)
+    stack.setup_decode(B, T_CTX)
+    for _ in range(max(3, args.warmup // 4)):
+        stack.decode_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    n = max(5, args.steps // 50)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        stack.decode_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1) / n)
+    reqs = B * ws
+    bytes_ = stack.decode_bytes_per_request() * B
+    return {"stack_decode": {
+        "metric": "40-layer mixer stack decode tok/s", "requests_total": reqs,
+        "requests_per_gpu": B, "context": T_CTX, "n_gpus": ws, "value": reqs / (ms / 1e3),
+        "unit": "tok/s", "ms_per_step": ms, "per_gpu_GBs": bytes_ / (ms / 1e3) / 1e9,
+        "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm, "steps": n}}
+
+
+def run_stack_prefill(be, args, st, peak_tc):
+    """BASELINE config 5 (ii): prefill of one 32k-token prompt through the
+    40-layer mixer stack, heads sharded over the GPUs, each layer's output
+    all-gathered over NCCL."""
+    import torch
+    pkg = _pkg()
+    ws, rank = _dist()
+    S = int(args.lengths.split(",")[-1])
+    stack = pkg.stack.MixerStack(be, seed=7)
+    stack.setup_prefill(S, ws, rank)
+    stack.prefill()
+    torch.cuda.synchronize()
+    barrier(ws)
+    reps = 2
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        be.gdn_reset()
+        stack.prefill()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1) / reps)
+    flops, gdn_bytes = stack.prefill_flops_bytes()
+    return {"stack_prefill": {
+        "metric": "40-layer mixer stack prefill tok/s", "S": S, "n_gpus": ws,
+        "value": S / (ms / 1e3), "unit": "tok/s", "ms": ms,
+        "gqa_TFLOP": flops / 1e12, "gdn_GB": gdn_bytes / 1e9,
+        "parallelism": f"heads sharded over {ws} GPU(s) + NCCL all-gather per layer"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,6 +599,11 @@ def main():
     ap.add_argument("--context", type=int, default=T_CTX, help="decode context length")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e / secondary / CPU legs), for profiling")
+    ap.add_argument("--only", choices=["gdn", "prefill", "gdnprefill", "stack", "stackprefill"],
+                    default=None,
+                    help="run one secondary leg alone and print its JSON (profiling)")
+    ap.add_argument("--lengths", default="8192,32768", help="prefill lengths of the secondary legs")
+    ap.add_argument("--stack-batch", type=int, default=256, help="stack decode requests (all GPUs)")
     args = ap.parse_args()
     globals()["B_REQ"], globals()["T_CTX"] = args.requests, args.context
     if args.quick:

@@ -117,6 +117,17 @@ int  coli_cuda_gqa_step_dev(int layer, int req, int S, int pos_base, const void 
                             const void *v, void *ctx, int H, int KH, int hd, int rot, float eps,
                             float theta, int dtype);
 
+/* ---- New (no reference counterpart: the reference is single-device):
+ * head-sharded causal prefill for one rank of a multi-GPU prefill. Computes
+ * query heads [h0, h0+nh) of inputs laid out with all H / KH heads (qg
+ * [S][H][2*hd], k/v [S][KH][hd]); the layer's cache holds only the KV heads
+ * those query heads read (h0/8 .. (h0+nh-1)/8), and ctx is [S][nh][hd]. The
+ * per-rank ctx blocks are then all-gathered by the caller. S >= 64. */
+int  coli_cuda_gqa_prefill_heads_dev(int layer, int req, int S, int pos_base, const void *qg,
+                                     const void *k, const void *v, void *ctx, int H, int KH,
+                                     int hd, int rot, float eps, float theta, int dtype, int h0,
+                                     int nh);
+
 /* ---- New: batched GQA decode, one new token for each request b < B at its
  * own position pos[b] (requests 0..B-1 of the layer's cache). Same per-row
  * semantics as coli_cuda_gqa_step with S = 1. The _dev form takes pos on the
@@ -189,6 +200,16 @@ int  coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const fl
 int  coli_cuda_gdn_prefill_dev(int layer, int req, int S, const void *qkv, const void *z,
                                const void *a, const void *b, void *y, int KH, int KD, int VH,
                                int VD, float eps, int dtype);
+
+/* ---- New (no reference counterpart): head-sharded GDN prefill for one rank.
+ * Owns K heads [kh0, kh0+nkh) and their V heads [2*kh0, 2*kh0+2*nkh) of
+ * inputs laid out with all KH / VH heads; the layer's state holds only the
+ * owned V heads (state_ensure with VH = 2*nkh), its conv history is the full
+ * width (only owned channels are read and advanced) and its params are the
+ * full VH arrays. y is [S][2*nkh*VD]. S >= 64. */
+int  coli_cuda_gdn_prefill_heads_dev(int layer, int req, int S, const void *qkv, const void *z,
+                                     const void *a, const void *b, void *y, int KH, int KD,
+                                     int VH, int VD, float eps, int dtype, int kh0, int nkh);
 
 #ifdef __cplusplus
 }

@@ -53,6 +53,8 @@ SIGNATURES = {
     "coli_cuda_gqa_decode": ([_i, _i, _fp, _fp, _fp, _ip, _fp] + [_i] * 4 + [_f, _f], _i),
     "coli_cuda_gqa_decode_dev": ([_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 4 + [_f, _f, _i], _i),
     "coli_cuda_gqa_decode_noalloc": ([_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 4 + [_f, _f, _i], _i),
+    "coli_cuda_gqa_prefill_heads_dev": ([_i] * 4 + [_vp] * 4 + [_i] * 4 + [_f, _f, _i, _i, _i], _i),
+    "coli_cuda_gdn_prefill_heads_dev": ([_i, _i, _i] + [_vp] * 5 + [_i] * 4 + [_f, _i, _i, _i], _i),
     "coli_cuda_gdn_state_ensure": ([_i] * 5, _i),
     "coli_cuda_gdn_conv_ensure": ([_i] * 4, _i),
     "coli_cuda_gdn_conv_weight": ([_i, _fp, _i, _i], _i),
@@ -228,6 +230,18 @@ class Backend:
                            eps=1e-6, theta=1e7, dtype=1):
         self._ok(self.lib.coli_cuda_gqa_decode_noalloc(layer, B, qg, k, v, pos, ctx, H, KH, hd, rot,
                                                        eps, theta, dtype), "gqa_decode_noalloc")
+
+    def gqa_prefill_heads_dev(self, layer, req, S, pos_base, qg, k, v, ctx, h0, nh, H=16, KH=2,
+                              hd=256, rot=64, eps=1e-6, theta=1e7, dtype=1):
+        self._ok(self.lib.coli_cuda_gqa_prefill_heads_dev(layer, req, S, pos_base, qg, k, v, ctx, H,
+                                                          KH, hd, rot, eps, theta, dtype, h0, nh),
+                 "gqa_prefill_heads_dev")
+
+    def gdn_prefill_heads_dev(self, layer, req, S, qkv, z, a, b, y, kh0, nkh, KH=16, KD=128,
+                              VH=32, VD=128, eps=1e-6, dtype=1):
+        self._ok(self.lib.coli_cuda_gdn_prefill_heads_dev(layer, req, S, qkv, z, a, b, y, KH, KD, VH,
+                                                          VD, eps, dtype, kh0, nkh),
+                 "gdn_prefill_heads_dev")
 
     def gqa_step_dev(self, layer, req, S, pos_base, qg, k, v, ctx, H=16, KH=2, hd=256, rot=64,
                      eps=1e-6, theta=1e7, dtype=1):

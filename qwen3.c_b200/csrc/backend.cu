@@ -252,7 +252,7 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     float *po = (float *)scratch(S_PO, (size_t)nq * L.KH * ns * 8 * 256 * 4);
     float *pml = (float *)scratch(S_PML, (size_t)nq * L.KH * ns * 8 * 2 * 4);
     if (!po || !pml) return 0;
-    GqaSplitArgs sa;
+    GqaSplitArgs sa{};
     sa.q = (const __nv_bfloat16 *)G.slot[S_Q];
     sa.pos = pos_d;
     sa.creq = creq_d;
@@ -263,7 +263,7 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     kt_mark(COLI_K_GQA_SPLIT);
     CK(launch_gqa_split(L.tmK, L.tmV, sa, stream()));
     kt_mark(COLI_K_GQA_SPLIT);
-    GqaCombineArgs ca;
+    GqaCombineArgs ca{};
     ca.part_o = po; ca.part_ml = pml; ca.qg = qg_gate; ca.ctx = ctx;
     ca.nq = nq; ca.H = H; ca.KH = L.KH; ca.n_splits = ns;
     kt_mark(COLI_K_GQA_COMBINE);
@@ -297,7 +297,7 @@ int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, co
     if (tmax > L.max_t) return fail("position %d beyond max_t %d", tmax - 1, L.max_t);
     __nv_bfloat16 *q = (__nv_bfloat16 *)scratch(S_Q, (size_t)nq * H * hd * 2);
     if (!q) return 0;
-    GqaPrologueArgs pa;
+    GqaPrologueArgs pa{};
     pa.qg = qg; pa.k = k; pa.v = v; pa.qnw = L.qnw; pa.knw = L.knw; pa.pos = pos_d; pa.creq = creq_d;
     pa.qout = q; pa.kcache = L.k; pa.vcache = L.v;
     pa.nq = nq; pa.H = H; pa.KH = KH; pa.max_t = L.max_t; pa.rot = rot; pa.eps = eps; pa.theta = theta;
@@ -316,7 +316,7 @@ int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void
 {
     CUtensorMap tq;
     if (!make_q_tmap(&tq, G.slot[S_Q], S, H, L.hd)) return 0;
-    GqaPrefillArgs a;
+    GqaPrefillArgs a{};
     a.qg = qg; a.ctx = ctx; a.S = S; a.H = H; a.KH = L.KH; a.max_t = L.max_t; a.req = req;
     a.pos_base = pos_base; a.n_qtiles = (S + 127) / 128; a.scale_log2 = scale * 1.4426950408889634f;
     kt_mark(COLI_K_GQA_PREFILL);
@@ -377,10 +377,18 @@ int make_f32_3d(CUtensorMap *m, void *base, int d0, int d1, int d2, int box0, in
 // Chunk-parallel GDN prefill (gdn_prefill.cu) for S >= GDN_CHUNK_MIN_ROWS.
 constexpr int GDN_CHUNK_MIN_ROWS = 64;
 int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *z, const void *a,
-                        const void *b, void *y, int KH, int KD, int VH, int VD, float eps, int dtype)
+                        const void *b, void *y, int KHin, int KD, int VHin, int VD, float eps,
+                        int dtype, int kh0 = 0, int nkh = -1)
 {
     GdnLayer &L = G.gdn[layer];
-    if (!gdn_shape_ok(L, KH, KD, VH, VD, 1)) return 0;
+    if (nkh < 0) nkh = KHin;
+    const int KH = nkh, VH = 2 * nkh;  // heads this call owns
+    if (!L.state || L.VH != VH || L.KD != KD || L.VD != VD || KD != 128 || VD != 128 || VHin != 2 * KHin)
+        return fail("GDN state/shape mismatch (state VH=%d, owned VH=%d)", L.VH, VH);
+    if (kh0 < 0 || kh0 + nkh > KHin) return fail("bad K head range");
+    if (!L.hist || !L.conv_w || L.conv_k != 4 || L.conv_dim != 2 * KHin * KD + VHin * VD)
+        return fail("GDN conv history/weights not set for this layer");
+    if (!L.A_log || L.pVH != VHin) return fail("GDN A_log/dt_bias/gnorm not set for %d V heads", VHin);
     if (req < 0 || req >= L.batch || req >= L.hbatch) return fail("request out of range");
     const int nch = (S + 63) / 64;
     GdnPrefillArgs p;
@@ -400,6 +408,7 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.M = (float *)scratch(S_GM, (size_t)nch * VH * 64 * 64 * 4);
     if (!p.Qh || !p.Kh || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
+    p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
     GdnPrefillMaps m;
     if (!make_f32_3d(&m.Q, p.Qh, 128, S, KH, 32, 64) || !make_f32_3d(&m.K, p.Kh, 128, S, KH, 32, 64) ||
         !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
@@ -771,6 +780,49 @@ int coli_cuda_gqa_decode_dev(int layer, int B, const void *qg, const void *k, co
                     dtype, dtype);
 }
 
+int coli_cuda_gqa_prefill_heads_dev(int layer, int req, int S, int pos_base, const void *qg,
+                                    const void *k, const void *v, void *ctx, int H, int KH,
+                                    int hd, int rot, float eps, float theta, int dtype, int h0,
+                                    int nh)
+{
+    READY();
+    if (!check_layer(layer)) return fail("layer %d out of range", layer);
+    KvLayer &L = G.kv[layer];
+    if (!L.k) return fail("KV layer %d not allocated", layer);
+    if (!L.qnw) return fail("q/k norm weights of layer %d not set", layer);
+    if (hd != 256 || H != 8 * KH) return fail("unsupported GQA shape H=%d KH=%d hd=%d", H, KH, hd);
+    if (nh < 1 || h0 < 0 || h0 + nh > H) return fail("bad head range [%d, %d)", h0, h0 + nh);
+    const int kh0 = h0 / 8, nkh = (h0 + nh - 1) / 8 + 1 - kh0;
+    if (L.KH != nkh) return fail("cache holds %d KV heads; heads [%d, %d) need %d", L.KH, h0, h0 + nh, nkh);
+    if (S < PREFILL_MIN_ROWS) return fail("head-sharded prefill needs S >= %d", PREFILL_MIN_ROWS);
+    if (req < 0 || req >= L.batch || pos_base < 0 || pos_base + S > L.max_t) return fail("bad request / positions");
+    if (rot < 2 || rot > hd || (rot & 1)) return fail("bad rot %d", rot);
+    int *pos_d = (int *)scratch(S_POS, (size_t)S * 4);
+    int *creq_d = (int *)scratch(S_CREQ, (size_t)S * 4);
+    __nv_bfloat16 *q = (__nv_bfloat16 *)scratch(S_Q, (size_t)S * nh * hd * 2);
+    if (!pos_d || !creq_d || !q) return 0;
+    iota_kernel<<<(S + 255) / 256, 256, 0, stream()>>>(pos_d, creq_d, S, pos_base, req);
+    CK(cudaGetLastError());
+    GqaPrologueArgs pa{};
+    pa.qg = qg; pa.k = k; pa.v = v; pa.qnw = L.qnw; pa.knw = L.knw; pa.pos = pos_d; pa.creq = creq_d;
+    pa.qout = q; pa.kcache = L.k; pa.vcache = L.v;
+    pa.nq = S; pa.H = nh; pa.KH = nkh; pa.max_t = L.max_t; pa.rot = rot; pa.eps = eps; pa.theta = theta;
+    pa.h0 = h0; pa.kh0 = kh0; pa.Hin = H; pa.KHin = KH;
+    CK(launch_gqa_prologue(pa, dtype, stream()));
+    CUtensorMap tq;
+    if (!make_q_tmap(&tq, q, S, nh, hd)) return 0;
+    GqaPrefillArgs a{};
+    a.qg = qg; a.ctx = ctx; a.S = S; a.H = nh; a.KH = nkh; a.max_t = L.max_t; a.req = req;
+    a.pos_base = pos_base; a.n_qtiles = (S + 127) / 128;
+    a.scale_log2 = (1.f / sqrtf((float)hd)) * 1.4426950408889634f;
+    a.h0 = h0; a.kh0 = kh0; a.Hin = H;
+    kt_mark(COLI_K_GQA_PREFILL);
+    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, dtype, dtype, stream()));
+    kt_mark(COLI_K_GQA_PREFILL);
+    g_launches += 3;
+    return 1;
+}
+
 // ------------------------------------------------------------------ GDN state
 int coli_cuda_gdn_state_ensure(int layer, int batch, int VH, int KD, int VD)
 {
@@ -981,6 +1033,16 @@ int coli_cuda_gdn_prefill_dev(int layer, int req, int S, const void *qkv, const 
             return 0;
     }
     return 1;
+}
+
+int coli_cuda_gdn_prefill_heads_dev(int layer, int req, int S, const void *qkv, const void *z,
+                                    const void *a, const void *b, void *y, int KH, int KD, int VH,
+                                    int VD, float eps, int dtype, int kh0, int nkh)
+{
+    READY();
+    if (!check_layer(layer)) return fail("layer %d out of range", layer);
+    if (S < GDN_CHUNK_MIN_ROWS) return fail("head-sharded GDN prefill needs S >= %d", GDN_CHUNK_MIN_ROWS);
+    return gdn_prefill_chunked(layer, req, S, qkv, z, a, b, y, KH, KD, VH, VD, eps, dtype, kh0, nkh);
 }
 
 int coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const float *z,

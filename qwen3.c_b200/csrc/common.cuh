@@ -149,3 +149,19 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 }
 
 }  // namespace coli
+
+namespace coli {
+// Split cluster barrier. `arrive_relaxed` is used where the arriving thread
+// has already consumed (not merely issued) every load the barrier orders, so
+// it need not wait for its own outstanding stores; `arrive_release` publishes
+// prior writes (shared memory read through DSMEM afterwards).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+}  // namespace coli

@@ -69,6 +69,7 @@ gdn_decode_kernel(GdnDecodeArgs p)
         ak += wk.x * hk0; ak += wk.y * hk1; ak += wk.z * hk2; ak += wk.w * xk;
         const float qc = siluf_(aq), kc = siluf_(ak);
         // ---- v channels of this CTA's 32 columns; this CTA owns their history
+        float vh1 = 0.f, vh2 = 0.f, vxv = 0.f;
         if (t < GDN_CB) {
             const int cv = 2 * key_dim + vh * GDN_VD + cblk * GDN_CB + t;
             const float h0 = hist[cv], h1 = hist[CD + cv], h2 = hist[2 * CD + cv];
@@ -77,7 +78,7 @@ gdn_decode_kernel(GdnDecodeArgs p)
             float av = 0.f;
             av += wv.x * h0; av += wv.y * h1; av += wv.z * h2; av += wv.w * xv;
             vs[t] = siluf_(av);
-            hist[cv] = h1; hist[CD + cv] = h2; hist[2 * CD + cv] = xv;
+            vh1 = h1; vh2 = h2; vxv = xv;
             zs[t] = siluf_(to_f32(static_cast<const TI *>(p.z)[(size_t)b * VH * GDN_VD + vh * GDN_VD + cblk * GDN_CB + t]));
         }
         // ---- L2 norms over the 128 channels of the K head
@@ -98,9 +99,15 @@ gdn_decode_kernel(GdnDecodeArgs p)
         const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)b * VH + vh]), bv = to_f32(static_cast<const TI *>(p.b)[(size_t)b * VH + vh]);
         beta = sigmoidf_(bv);
         decay = expf(-expf(p.A_log[vh]) * softplusf_(av + p.dt_bias[vh]));
-        // All CTAs of the cluster have read the old q/k history: the owner
-        // (rank 0) may now shift it.
-        cluster.sync();
+        // All CTAs of the cluster have read (and used) the old q/k history:
+        // the owner (rank 0) may now shift it. The history stores are issued
+        // only after this barrier, so the arrive does not wait on them.
+        cluster_arrive_relaxed();
+        cluster_wait();
+        if (t < GDN_CB) {
+            const int cv = 2 * key_dim + vh * GDN_VD + cblk * GDN_CB + t;
+            hist[cv] = vh1; hist[CD + cv] = vh2; hist[2 * CD + cv] = vxv;
+        }
         if (rank == 0) {
             hist[cq] = hq1; hist[CD + cq] = hq2; hist[2 * CD + cq] = xq;
             hist[ck] = hk1; hist[CD + ck] = hk2; hist[2 * CD + ck] = xk;
@@ -156,7 +163,6 @@ gdn_decode_kernel(GdnDecodeArgs p)
         const float kk = ks[r], qq = qs[r];
         S[i].x += kk * dl.x; S[i].y += kk * dl.y; S[i].z += kk * dl.z; S[i].w += kk * dl.w;
         yp.x += S[i].x * qq; yp.y += S[i].y * qq; yp.z += S[i].z * qq; yp.w += S[i].w * qq;
-        __stcs(reinterpret_cast<float4 *>(Sbase + (size_t)r * GDN_VD + 4 * c4), S[i]);
     }
 #pragma unroll
     for (int o = 8; o <= 16; o <<= 1) {
@@ -176,8 +182,15 @@ gdn_decode_kernel(GdnDecodeArgs p)
         for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
         if (t == 0) ss_sh = s2;
     }
-    // ---- gated RMSNorm over the V head's 128 columns (4 CTAs of the cluster)
-    cluster.sync();
+    // ---- gated RMSNorm over the V head's 128 columns (4 CTAs of the cluster).
+    // Publish the statistic, then stream the state back while peers arrive.
+    cluster_arrive_release();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = warp * 4 + rs + 16 * i;
+        __stcs(reinterpret_cast<float4 *>(Sbase + (size_t)r * GDN_VD + 4 * c4), S[i]);
+    }
+    cluster_wait();
     if (t < GDN_CB) {
         const int first = rank & 4;
         double tot = 0.0;
@@ -188,7 +201,9 @@ gdn_decode_kernel(GdnDecodeArgs p)
         const float out = yv * r * p.gnorm[col] * zs[t];
         static_cast<TO *>(p.y)[(size_t)b * VH * GDN_VD + vh * GDN_VD + col] = from_f32<TO>(out);
     }
-    cluster.sync();  // keep shared memory alive until every peer has read it
+    // keep shared memory alive until every peer has read (and used) it
+    cluster_arrive_relaxed();
+    cluster_wait();
 }
 
 template <typename TI, typename TO, bool PRENORM>

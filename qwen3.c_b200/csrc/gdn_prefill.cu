@@ -92,8 +92,10 @@ __global__ void __launch_bounds__(PFG_D)
 gdn_pf_prologue_kernel(GdnPrefillArgs p)
 {
     const int s = blockIdx.x, kh = blockIdx.y, t = threadIdx.x;
-    const int KH = p.KH, VH = p.VH, S = p.S;
-    const int key_dim = KH * PFG_D, CD = 2 * key_dim + VH * PFG_D;
+    const int S = p.S;
+    const int KHin = p.KHin ? p.KHin : p.KH, VHin = p.VHin ? p.VHin : p.VH;
+    const int kg = p.kh0 + kh;                    // K head in the input layout
+    const int key_dim = KHin * PFG_D, CD = 2 * key_dim + VHin * PFG_D;
     const TI *x = static_cast<const TI *>(p.qkv);
     auto tap = [&](int ch, int j) -> float {  // pre-conv value of channel ch at token s-3+j
         const int ts = s - 3 + j;
@@ -105,7 +107,7 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
         a += w.x * tap(ch, 0); a += w.y * tap(ch, 1); a += w.z * tap(ch, 2); a += w.w * tap(ch, 3);
         return siluf_(a);
     };
-    const float qc = conv(kh * PFG_D + t), kc = conv(key_dim + kh * PFG_D + t);
+    const float qc = conv(kg * PFG_D + t), kc = conv(key_dim + kg * PFG_D + t);
     __shared__ float red[2][4];
     float sq = qc * qc, sk = kc * kc;
 #pragma unroll
@@ -123,28 +125,33 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
     p.Kh[((size_t)kh * S + s) * PFG_D + t] = kc * rk;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-        const int vh = kh * 2 + j;
-        p.Vh[((size_t)vh * S + s) * PFG_D + t] = conv(2 * key_dim + vh * PFG_D + t);
+        const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
+        p.Vh[((size_t)vh * S + s) * PFG_D + t] = conv(2 * key_dim + vg * PFG_D + t);
         if (t == 0) {
-            const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VH + vh]);
-            const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VH + vh]);
+            const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
+            const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
             // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
-            p.GL[(size_t)vh * S + s] = -expf(p.A_log[vh]) * softplusf_(av + p.dt_bias[vh]);
+            p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
             p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
         }
     }
 }
 
-// New conv history = the last 3 pre-conv rows. Needs S >= 3 (the host routes
-// shorter runs through the token-by-token decode kernel).
+// New conv history = the last 3 pre-conv rows of the owned channels. Needs
+// S >= 3 (the host routes shorter runs through the token-by-token decode kernel).
 template <typename TI>
 __global__ void gdn_pf_hist_kernel(GdnPrefillArgs p)
 {
-    const int CD = 2 * p.KH * PFG_D + p.VH * PFG_D;
+    const int KHin = p.KHin ? p.KHin : p.KH, VHin = p.VHin ? p.VHin : p.VH;
+    const int key_dim = KHin * PFG_D, CD = 2 * key_dim + VHin * PFG_D;
+    const int q0 = p.kh0 * PFG_D, q1 = q0 + p.KH * PFG_D;
+    const int v0 = 2 * key_dim + 2 * p.kh0 * PFG_D, v1 = v0 + 2 * p.KH * PFG_D;
     const TI *x = static_cast<const TI *>(p.qkv);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * CD; i += gridDim.x * blockDim.x) {
         const int j = i / CD, ch = i - j * CD;
-        p.hist[i] = to_f32(x[(size_t)(p.S - 3 + j) * CD + ch]);
+        const bool own = (ch >= q0 && ch < q1) || (ch >= key_dim + q0 && ch < key_dim + q1) ||
+                         (ch >= v0 && ch < v1);
+        if (own) p.hist[i] = to_f32(x[(size_t)(p.S - 3 + j) * CD + ch]);
     }
 }
 
@@ -312,6 +319,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
     const int S = p.S, nchunks = (S + PFG_C - 1) / PFG_C;
     const int VD = PFG_D, VH = p.VH;
+    const int VHin = p.VHin ? p.VHin : VH, vg = 2 * p.kh0 + h;  // V head in the input layout
 
     auto load_wu = [&](int n) {
         mbar_expect_tx(&bar_wu, (PFG_C * PFG_D + PFG_C * SCAN_CB) * 4);
@@ -499,7 +507,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int col = cblk * SCAN_CB + nt * 8 + 2 * tq + e;
-                        const float z = to_f32(static_cast<const TI *>(p.z)[(size_t)t * VH * VD + h * VD + col]);
+                        const float z = to_f32(static_cast<const TI *>(p.z)[(size_t)t * VHin * VD + vg * VD + col]);
                         const float out = y[nt][2 * half + e] * rinv * p.gnorm[col] * siluf_(z);
                         static_cast<TO *>(p.y)[(size_t)t * VH * VD + h * VD + col] = from_f32<TO>(out);
                     }
@@ -533,7 +541,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
 {
     if (a.S < 3) return cudaErrorInvalidValue;
     const int nchunks = (a.S + PFG_C - 1) / PFG_C;
-    const int CD = 2 * a.KH * PFG_D + a.VH * PFG_D;
+    const int CD = 2 * (a.KHin ? a.KHin : a.KH) * PFG_D + (a.VHin ? a.VHin : a.VH) * PFG_D;
     cudaError_t e;
     if (bf16) gdn_pf_prologue_kernel<__nv_bfloat16><<<dim3(a.S, a.KH), PFG_D, 0, st>>>(a);
     else gdn_pf_prologue_kernel<float><<<dim3(a.S, a.KH), PFG_D, 0, st>>>(a);

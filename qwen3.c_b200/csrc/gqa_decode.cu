@@ -36,14 +36,15 @@ gqa_prologue_kernel(GqaPrologueArgs p)
 {
     const int n = blockIdx.x, j = blockIdx.y, d = threadIdx.x;
     const int H = p.H, KH = p.KH;
+    const int Hin = p.Hin ? p.Hin : H, KHin = p.KHin ? p.KHin : KH;
     const int pos = p.pos[n];
     const float *w;
     float x;
     if (j < H) {
-        x = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * H + j) * 2 * GQA_HD + d]);
+        x = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * Hin + p.h0 + j) * 2 * GQA_HD + d]);
         w = p.qnw;
     } else {
-        x = to_f32(static_cast<const TI *>(p.k)[((size_t)n * KH + (j - H)) * GQA_HD + d]);
+        x = to_f32(static_cast<const TI *>(p.k)[((size_t)n * KHin + p.kh0 + (j - H)) * GQA_HD + d]);
         w = p.knw;
     }
     // zero-centred RMSNorm, sum of squares in double (c/qwen.c:326-330)
@@ -78,7 +79,7 @@ gqa_prologue_kernel(GqaPrologueArgs p)
         const int creq = p.creq ? p.creq[n] : n;
         const size_t row = ((size_t)creq * KH + kh) * p.max_t + pos;
         p.kcache[row * GQA_HD + d] = __float2bfloat16_rn(y);
-        const float v = to_f32(static_cast<const TI *>(p.v)[((size_t)n * KH + kh) * GQA_HD + d]);
+        const float v = to_f32(static_cast<const TI *>(p.v)[((size_t)n * KHin + p.kh0 + kh) * GQA_HD + d]);
         p.vcache[row * GQA_HD + d] = __float2bfloat16_rn(v);
     }
 }

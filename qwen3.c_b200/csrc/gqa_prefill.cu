@@ -6,13 +6,13 @@
 // sigmoid(gate). The prologue (q/k norm, RoPE, K/V append) runs before this
 // kernel (gqa_prologue_kernel), so the new rows are already in the cache.
 //
-// One CTA = 128 query rows of one Q head. Warp roles (192 threads):
-//   warp 0      TMA producer: Q tile once, then K/V tiles of 64 keys into a
-//               2-stage ring (128B-swizzled boxes).
+// One CTA = 128 query rows of one Q head. Warp roles (320 threads):
+//   warp 0      TMA producers (lane 0: Q once, then K; lane 1: V): 64-key
+//               tiles into separate 2-stage K and V rings (128B swizzle).
 //   warp 1      MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
 //               two TMEM score buffers (M=128, N=64, K=256), then
 //               O += P V (M=128, N=256, K=64) with V read MN-major.
-//   warps 2..5  softmax: one thread per query row (TMEM lane), scores read
+//   warps 2..9  softmax: two threads per query row (TMEM lane), scores read
 //               with tcgen05.ld, causal mask, online softmax in the log2
 //               domain with lazy rescaling (O is corrected in TMEM only when
 //               the running max grows by more than 2^8), P written to shared
@@ -30,13 +30,15 @@ constexpr int PF_BM = 128, PF_BN = 64, PF_HD = 256;
 constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB
 constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 32 KiB per K (or V) tile
 constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 16 KiB
-constexpr int PF_SMEM = PF_Q_BYTES + 4 * PF_KV_BYTES + 2 * PF_P_BYTES + 1024;
-constexpr int PF_THREADS = 192;
+constexpr int PF_SMEM = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES + 1024;
+constexpr int PF_THREADS = 320;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 struct PfBars {
-    uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
+    uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
+    float mx[2][2][PF_BM];   // per-tile row max of each half (double-buffered)
+    float lsum[2][PF_BM];    // final row sums of each half
 };
 
 template <typename TI, typename TO>
@@ -50,14 +52,15 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint8_t *sQ = smem;
     uint8_t *sK = sQ + PF_Q_BYTES;              // [2][32 KiB]
     uint8_t *sV = sK + 2 * PF_KV_BYTES;         // [2][32 KiB]
-    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // [2][16 KiB]
+    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // 16 KiB, one P tile
     __shared__ PfBars bars;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H;
     const int h = blockIdx.x % H;
     const int qt = p.n_qtiles - 1 - (int)(blockIdx.x / H);  // heaviest tiles first
-    const int kh = h / 8;
+    const int kh = (p.h0 + h) / 8 - p.kh0;                  // KV head in this call's cache
+    const int Hin = p.Hin ? p.Hin : H;
     const int q0 = qt * PF_BM;                              // first query row of the tile
     const int last_row = min(p.S, q0 + PF_BM) - 1;
     const int nt = (p.pos_base + last_row) / PF_BN + 1;     // KV tiles touched
@@ -68,10 +71,11 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars.k_full[i], 1);
             mbar_init(&bars.v_full[i], 1);
-            mbar_init(&bars.kv_empty[i], 1);
+            mbar_init(&bars.k_empty[i], 1);
+            mbar_init(&bars.v_empty[i], 1);
             mbar_init(&bars.s_full[i], 1);
-            mbar_init(&bars.s_free[i], 128);
-            mbar_init(&bars.p_full[i], 128);
+            mbar_init(&bars.s_free[i], 256);
+            mbar_init(&bars.p_full[i], 256);
             mbar_init(&bars.pv_done[i], 1);
         }
         fence_mbar_init();
@@ -84,21 +88,31 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const uint32_t tS0 = tbase, tO = tbase + 128;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ TMA producers
+        // Lane 0 streams K (a stage frees as soon as its S MMA completes),
+        // lane 1 streams V (freed after its PV MMA), so the next K tile is in
+        // flight while the current tile's softmax and PV still run.
         if (lane == 0) {
-            tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK); tma_prefetch_desc(&tmV);
+            tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
             mbar_expect_tx(&bars.q_full, PF_Q_BYTES);
             for (int c = 0; c < 4; ++c) tma_load_3d(sQ + c * (PF_BM * 128), &tmQ, 64 * c, h, q0, &bars.q_full);
             for (int j = 0; j < nt; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&bars.kv_empty[s], ((j >> 1) - 1) & 1)) break;
-                const int row = kvrow0 + j * PF_BN;
+                if (j >= 2 && !mbar_wait(&bars.k_empty[s], ((j >> 1) - 1) & 1)) break;
                 mbar_expect_tx(&bars.k_full[s], PF_KV_BYTES);
                 for (int c = 0; c < 4; ++c)
-                    tma_load_2d(sK + s * PF_KV_BYTES + c * (PF_BN * 128), &tmK, 64 * c, row, &bars.k_full[s]);
+                    tma_load_2d(sK + s * PF_KV_BYTES + c * (PF_BN * 128), &tmK, 64 * c,
+                                kvrow0 + j * PF_BN, &bars.k_full[s]);
+            }
+        } else if (lane == 1) {
+            tma_prefetch_desc(&tmV);
+            for (int j = 0; j < nt; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait(&bars.v_empty[s], ((j >> 1) - 1) & 1)) break;
                 mbar_expect_tx(&bars.v_full[s], PF_KV_BYTES);
                 for (int c = 0; c < 4; ++c)
-                    tma_load_2d(sV + s * PF_KV_BYTES + c * (PF_BN * 128), &tmV, 64 * c, row, &bars.v_full[s]);
+                    tma_load_2d(sV + s * PF_KV_BYTES + c * (PF_BN * 128), &tmV, 64 * c,
+                                kvrow0 + j * PF_BN, &bars.v_full[s]);
             }
         }
     } else if (warp == 1) {
@@ -115,13 +129,13 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tc::fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_BN / 16; ++kk) {
-                    const uint64_t da = tc::desc_k_sw128(aP + b * PF_P_BYTES + kk * 32);
+                    const uint64_t da = tc::desc_k_sw128(aP + kk * 32);
                     const uint64_t db = tc::desc_mn_sw128(aV + b * PF_KV_BYTES + kk * 16 * 128,
                                                           PF_BN * 128, 1024);
                     tc::mma_bf16(tO, da, db, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc::commit(&bars.pv_done[b]);
-                tc::commit(&bars.kv_empty[b]);
+                tc::commit(&bars.v_empty[b]);
                 return true;
             };
             for (int j = 0; ok && j < nt; ++j) {
@@ -137,41 +151,45 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                  tc::desc_k_sw128(aK + s * PF_KV_BYTES + offk), ID_QK, kk > 0 ? 1u : 0u);
                 }
                 tc::commit(&bars.s_full[s]);
+                tc::commit(&bars.k_empty[s]);
                 if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
             }
             if (ok) issue_pv(nt - 1);
         }
     } else {
         // ------------------------------------------------ softmax + epilogue
+        // Two threads per query row: warps 2-5 take score columns 0-31 and O
+        // columns 0-127, warps 6-9 columns 32-63 and O 128-255 of the same
+        // TMEM lanes. Row maxima are exchanged through shared memory under a
+        // named barrier of the 256 softmax threads. Waits never break out of
+        // the loop (a time-out raises the error word and the loop runs on), so
+        // every thread meets every named barrier.
+        const int half = (warp - 2) >> 2;
         const int row = 32 * (warp & 3) + lane;            // TMEM lane == query row in tile
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         const int srow = q0 + row;                         // query row index in [0, S)
         const int qpos = p.pos_base + srow;
         const float sl2 = p.scale_log2;
         float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int i = 0; i < nt && ok; ++i) {
+        for (int i = 0; i < nt; ++i) {
             const int b = i & 1;
-            if (!mbar_wait(&bars.s_full[b], (i >> 1) & 1)) { ok = false; break; }
+            mbar_wait(&bars.s_full[b], (i >> 1) & 1);
             tc::fence_after();
-            float x[64];
-            {
-                float t0[32], t1[32];
-                tc::ld32(tS0 + b * PF_BN + lane_off, t0);
-                tc::ld32(tS0 + b * PF_BN + 32 + lane_off, t1);
-                tc::wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) { x[c] = t0[c]; x[32 + c] = t1[c]; }
-            }
+            float x[32];
+            tc::ld32(tS0 + b * PF_BN + 32 * half + lane_off, x);
+            tc::wait_ld();
             tc::fence_before();
             mbar_arrive(&bars.s_free[b]);
-            const int key0 = i * PF_BN;
+            const int key0 = i * PF_BN + 32 * half;
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
+            for (int c = 0; c < 32; ++c) {
                 x[c] = (key0 + c <= qpos) ? x[c] * sl2 : -INFINITY;
                 mx = fmaxf(mx, x[c]);
             }
+            bars.mx[b][half][row] = mx;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            mx = fmaxf(mx, bars.mx[b][half ^ 1][row]);
             const float mnew = fmaxf(m, mx);
             if (i == 0) {
                 m = mnew;
@@ -179,17 +197,18 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const bool need = mnew > m + PF_RESCALE_LOG2;
                 if (__any_sync(0xffffffffu, need)) {
                     // O must be complete up to tile i-1 before it is rescaled
-                    if (!mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1)) { ok = false; break; }
+                    mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
                     tc::fence_after();
                     const float alpha = need ? exp2f(m - mnew) : 1.f;
 #pragma unroll 1
-                    for (int c = 0; c < PF_HD / 32; ++c) {
+                    for (int c = 0; c < PF_HD / 64; ++c) {
                         float o[32];
-                        tc::ld32(tO + 32 * c + lane_off, o);
+                        const uint32_t col = tO + 128 * half + 32 * c + lane_off;
+                        tc::ld32(col, o);
                         tc::wait_ld();
 #pragma unroll
                         for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                        tc::st32(tO + 32 * c + lane_off, o);
+                        tc::st32(col, o);
                     }
                     tc::wait_st();
                     if (need) { l *= alpha; m = mnew; }
@@ -197,39 +216,47 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             const float mu = (m == -INFINITY) ? 0.f : m;
             float rs = 0.f;
-            uint32_t pk[32];
+            uint32_t pk[16];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
+            for (int c = 0; c < 16; ++c) {
                 const float p0 = exp2f(x[2 * c] - mu), p1 = exp2f(x[2 * c + 1] - mu);
                 rs += p0 + p1;
                 pk[c] = pack_bf16(p0, p1);
             }
             l += rs;
-            // P buffer b was last read by PV(i-2)
-            if (i >= 2 && !mbar_wait(&bars.pv_done[b], ((i - 2) >> 1) & 1)) { ok = false; break; }
-            uint8_t *prow = sP + b * PF_P_BYTES + row * 128;
+            // the single P buffer was last read by PV(i-1)
+            if (i >= 1) mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
+            uint8_t *prow = sP + row * 128;
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch)
+            for (int q = 0; q < 4; ++q) {
+                const int ch = 4 * half + q;
                 *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) =
-                    make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            }
             fence_proxy_async();
             mbar_arrive(&bars.p_full[b]);
         }
-        if (ok && mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
-            tc::fence_after();
+        // row sum = both halves' partial sums (same running max)
+        bars.lsum[half][row] = l;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        l += bars.lsum[half ^ 1][row];
+        mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1);
+        tc::fence_after();
+        {
             const float inv_l = 1.f / l;
             const bool valid = srow < p.S;
-            const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * H + h) * 2 * PF_HD + PF_HD;
+            const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD;
             TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD;
 #pragma unroll 1
-            for (int c = 0; c < PF_HD / 32; ++c) {
+            for (int c = 0; c < PF_HD / 64; ++c) {
                 float o[32];
-                tc::ld32(tO + 32 * c + lane_off, o);
+                const int d0 = 128 * half + 32 * c;
+                tc::ld32(tO + d0 + lane_off, o);
                 tc::wait_ld();
                 if (valid) {
 #pragma unroll
                     for (int e = 0; e < 32; ++e)
-                        out[32 * c + e] = from_f32<TO>(o[e] * inv_l * sigmoidf_(to_f32(gate[32 * c + e])));
+                        out[d0 + e] = from_f32<TO>(o[e] * inv_l * sigmoidf_(to_f32(gate[d0 + e])));
                 }
             }
         }

@@ -35,6 +35,9 @@ struct GqaPrologueArgs {
     __nv_bfloat16 *kcache, *vcache;  // [reqs][KH][max_t][hd]
     int nq, H, KH, max_t, rot;
     float eps, theta;
+    // head-sharded prefill: this call computes query heads [h0, h0+H) and KV
+    // heads [kh0, kh0+KH) of inputs laid out with Hin / KHin heads (0 = H / KH)
+    int h0, kh0, Hin, KHin;
 };
 struct GqaSplitArgs {
     const __nv_bfloat16 *q;  // [nq][H][hd] roped
@@ -67,6 +70,7 @@ struct GqaPrefillArgs {
     void *ctx;        // [S][H][hd]
     int S, H, KH, max_t, req, pos_base, n_qtiles;
     float scale_log2;
+    int h0, kh0, Hin;  // head-sharded prefill (see GqaPrologueArgs); 0 = unsharded
 };
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
@@ -87,6 +91,10 @@ struct GdnPrefillArgs {
     float *M;                             // scratch [nchunks][VH][64][64]
     int S, KH, VH;
     float eps;
+    // head-sharded prefill: this call owns K heads [kh0, kh0+KH) (V heads
+    // [2*kh0, 2*kh0+2*KH)) of inputs laid out with KHin / VHin heads (0 = KH / VH);
+    // state, y and scratch hold only the owned heads
+    int kh0, KHin, VHin;
 };
 struct GdnPrefillMaps {
     CUtensorMap Q, K, V, W, U, M;

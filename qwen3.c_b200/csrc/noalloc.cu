@@ -90,20 +90,20 @@ extern "C" int coli_cuda_gqa_decode_noalloc(int layer, int B, const void *qg, co
     float *pml = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(po) +
                                            align256((size_t)B * KH * ns * 8 * hd * 4));
 
-    GqaPrologueArgs pa;
+    GqaPrologueArgs pa{};
     pa.qg = qg; pa.k = k; pa.v = v; pa.qnw = L.qnw; pa.knw = L.knw; pa.pos = pos_dev; pa.creq = nullptr;
     pa.qout = q; pa.kcache = L.k; pa.vcache = L.v;
     pa.nq = B; pa.H = H; pa.KH = KH; pa.max_t = L.max_t; pa.rot = rot; pa.eps = eps; pa.theta = theta;
     CK(launch_gqa_prologue(pa, dtype, stream()));
 
-    GqaSplitArgs sa;
+    GqaSplitArgs sa{};
     sa.q = q; sa.pos = pos_dev; sa.creq = nullptr; sa.part_o = po; sa.part_ml = pml;
     sa.nq = B; sa.H = H; sa.KH = KH; sa.max_t = L.max_t; sa.n_splits = ns;
     sa.chunk = gqa_chunk_for(L.max_t, ns);
     sa.scale_log2 = (1.f / sqrtf((float)hd)) * 1.4426950408889634f;
     CK(launch_gqa_split(L.tmK, L.tmV, sa, stream()));
 
-    GqaCombineArgs ca;
+    GqaCombineArgs ca{};
     ca.part_o = po; ca.part_ml = pml; ca.qg = qg; ca.ctx = ctx;
     ca.nq = B; ca.H = H; ca.KH = KH; ca.n_splits = ns;
     CK(launch_gqa_combine(ca, dtype, dtype, stream()));
