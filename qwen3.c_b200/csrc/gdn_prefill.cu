@@ -242,8 +242,17 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (tid < PFG_C) {
         const int c = tid;
         for (int i = 0; i < PFG_C; ++i) {
-            float acc = (i == c) ? 1.f : 0.f;
-            for (int j = c; j < i; ++j) acc -= sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
+            // four independent partial sums shorten the dependent FMA chain
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            int j = c;
+            for (; j + 3 < i; j += 4) {
+                a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
+                a1 += sA[i * PREP_LD + j + 1] * sT[(j + 1) * PREP_LD + c];
+                a2 += sA[i * PREP_LD + j + 2] * sT[(j + 2) * PREP_LD + c];
+                a3 += sA[i * PREP_LD + j + 3] * sT[(j + 3) * PREP_LD + c];
+            }
+            for (; j < i; ++j) a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
+            const float acc = ((i == c) ? 1.f : 0.f) - ((a0 + a1) + (a2 + a3));
             sT[i * PREP_LD + c] = i < c ? 0.f : acc;
         }
     }
