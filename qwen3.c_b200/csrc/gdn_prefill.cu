@@ -15,8 +15,8 @@
 // (decay 1, beta 0, zero q/k/v: TMA zero-fills them), so they change nothing.
 //
 // Kernels
-//   gdn_pf_prologue_kernel  per (token, K head): conv4 over the token and its
-//                           3 predecessors (or the carried history) + SiLU,
+//   gdn_pf_prologue_kernel  per (64-token run, K head): sliding conv4 (history
+//                           carried in from the previous call) + SiLU,
 //                           q/k L2 norm, gates -> Q, K, V (fp32, head-major),
 //                           log-decay and beta per V head.
 //   gdn_pf_hist_kernel      carries the last 3 pre-conv rows out as history.
@@ -43,12 +43,16 @@ namespace coli {
 constexpr int PFG_C = 64, PFG_D = 128;
 
 // ---------------------------------------------------------------- tf32 MMA
+// fp32 -> tf32 with round-to-nearest. Operands that reach the MMA straight
+// from shared memory (ldmatrix) are rounded once where they are produced
+// (tf32r), since the MMA itself would truncate the low mantissa bits.
 __device__ __forceinline__ uint32_t f2tf32(float x)
 {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return r;
 }
+__device__ __forceinline__ float tf32r(float x) { return __uint_as_float(f2tf32(x)); }
 // D[16x8] += A[16x8] . B[8x8] in tf32 with fp32 accumulation.
 __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1)
@@ -66,6 +70,39 @@ __device__ __forceinline__ float sw_ld(const float *tile, int rows, int row, int
 {
     const int region = col >> 5, c = col & 31;
     return tile[region * rows * 32 + row * 32 + (((c >> 2) ^ (row & 7)) << 2) + (c & 3)];
+}
+
+// ldmatrix on fp32 data: an 8-row x 16-byte block delivers to lane l the
+// word at (row l/4, column l%4), which is exactly the tf32 m16n8k8 fragment
+// element (g, tq); four such blocks make an A fragment, two a B fragment.
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+// A fragment (16 rows from row0, k columns 8ks..8ks+7) of a 64-row fp32 tile
+// that TMA wrote as 128B-swizzled 32-column boxes.
+__device__ __forceinline__ void lda_sw(uint32_t tile, int row0, int ks, int lane, uint32_t (&a)[4])
+{
+    const int mat = lane >> 3, row = row0 + ((mat & 1) << 3) + (lane & 7);
+    const int chunk = ((ks & 3) << 1) + (mat >> 1);
+    ldsm_x4(tile + (ks >> 2) * (PFG_C * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+}
+// B fragment (n rows n0..n0+7, k columns 8ks..) of a row-major [n][k] tile.
+__device__ __forceinline__ void ldb_rm(uint32_t tile, int ld, int n0, int ks, int lane, uint32_t &b0,
+                                       uint32_t &b1)
+{
+    const int mat = (lane >> 3) & 1;
+    ldsm_x2(tile + ((n0 + (lane & 7)) * ld + ks * 8 + mat * 4) * 4, b0, b1);
+}
+
+// B fragment (n rows n0..n0+7, k columns 8ks..) of a 64-row swizzled tile
+// whose rows are the n index (e.g. K rows for K K^T).
+__device__ __forceinline__ void ldb_sw(uint32_t tile, int n0, int ks, int lane, uint32_t &b0, uint32_t &b1)
+{
+    const int mat = (lane >> 3) & 1, row = n0 + (lane & 7);
+    const int chunk = ((ks & 3) << 1) + mat;
+    ldsm_x2(tile + (ks >> 2) * (PFG_C * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1);
 }
 
 // Inclusive cumulative sum of the log decay of one chunk (one warp, 2 rows/lane).
@@ -87,52 +124,70 @@ __device__ __forceinline__ void chunk_cumsum(const float *gl, int t0, int S, int
 }
 
 // ---------------------------------------------------------------- prologue
+// One CTA walks a run of PRO_T tokens of one K head; thread t owns channel t
+// of q, k and of the head's two V heads, keeping the last three pre-conv
+// values in registers, so every input row is read once.
+constexpr int PRO_T = 64;
+
 template <typename TI>
 __global__ void __launch_bounds__(PFG_D)
 gdn_pf_prologue_kernel(GdnPrefillArgs p)
 {
-    const int s = blockIdx.x, kh = blockIdx.y, t = threadIdx.x;
-    const int S = p.S;
+    const int kh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int S = p.S, s_begin = blockIdx.x * PRO_T, s_end = min(S, s_begin + PRO_T);
     const int KHin = p.KHin ? p.KHin : p.KH, VHin = p.VHin ? p.VHin : p.VH;
     const int kg = p.kh0 + kh;                    // K head in the input layout
     const int key_dim = KHin * PFG_D, CD = 2 * key_dim + VHin * PFG_D;
     const TI *x = static_cast<const TI *>(p.qkv);
-    auto tap = [&](int ch, int j) -> float {  // pre-conv value of channel ch at token s-3+j
-        const int ts = s - 3 + j;
-        return ts >= 0 ? to_f32(x[(size_t)ts * CD + ch]) : p.hist[(size_t)(3 + ts) * CD + ch];
-    };
-    auto conv = [&](int ch) -> float {
-        const float4 w = *reinterpret_cast<const float4 *>(p.conv_w + (size_t)ch * 4);
-        float a = 0.f;
-        a += w.x * tap(ch, 0); a += w.y * tap(ch, 1); a += w.z * tap(ch, 2); a += w.w * tap(ch, 3);
-        return siluf_(a);
-    };
-    const float qc = conv(kg * PFG_D + t), kc = conv(key_dim + kg * PFG_D + t);
-    __shared__ float red[2][4];
-    float sq = qc * qc, sk = kc * kc;
+    const int ch[4] = {kg * PFG_D + t, key_dim + kg * PFG_D + t, 2 * key_dim + (2 * kg) * PFG_D + t,
+                       2 * key_dim + (2 * kg + 1) * PFG_D + t};
+    float4 w[4];
+    float h0[4], h1[4], h2[4];                     // values at tokens s-3, s-2, s-1
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    for (int c = 0; c < 4; ++c) {
+        w[c] = *reinterpret_cast<const float4 *>(p.conv_w + (size_t)ch[c] * 4);
+        auto tap = [&](int ts) -> float {
+            return ts >= 0 ? to_f32(x[(size_t)ts * CD + ch[c]]) : p.hist[(size_t)(3 + ts) * CD + ch[c]];
+        };
+        h0[c] = tap(s_begin - 3); h1[c] = tap(s_begin - 2); h2[c] = tap(s_begin - 1);
     }
-    if ((t & 31) == 0) { red[0][t >> 5] = sq; red[1][t >> 5] = sk; }
-    __syncthreads();
-    sq = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
-    sk = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
-    const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
-    const float rk = 1.f / sqrtf(sk + p.eps);
-    p.Qh[((size_t)kh * S + s) * PFG_D + t] = qc * rq;
-    p.Kh[((size_t)kh * S + s) * PFG_D + t] = kc * rk;
+    __shared__ float red[2][2][4];
+    for (int s = s_begin; s < s_end; ++s) {
+        const int par = s & 1;
+        float out[4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
-        p.Vh[((size_t)vh * S + s) * PFG_D + t] = conv(2 * key_dim + vg * PFG_D + t);
-        if (t == 0) {
-            const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
-            const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
-            // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
-            p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
-            p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
+        for (int c = 0; c < 4; ++c) {
+            const float xv = to_f32(x[(size_t)s * CD + ch[c]]);
+            float a = 0.f;
+            a += w[c].x * h0[c]; a += w[c].y * h1[c]; a += w[c].z * h2[c]; a += w[c].w * xv;
+            out[c] = siluf_(a);
+            h0[c] = h1[c]; h1[c] = h2[c]; h2[c] = xv;
+        }
+        float sq = out[0] * out[0], sk = out[1] * out[1];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        if (lane == 0) { red[par][0][warp] = sq; red[par][1][warp] = sk; }
+        __syncthreads();
+        sq = (red[par][0][0] + red[par][0][1]) + (red[par][0][2] + red[par][0][3]);
+        sk = (red[par][1][0] + red[par][1][1]) + (red[par][1][2] + red[par][1][3]);
+        const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
+        const float rk = 1.f / sqrtf(sk + p.eps);
+        p.Qh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[0] * rq);
+        p.Kh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[1] * rk);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
+            p.Vh[((size_t)vh * S + s) * PFG_D + t] = out[2 + j];
+            if (t == j) {
+                const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
+                const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
+                // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
+                p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
+                p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
+            }
         }
     }
 }
@@ -204,19 +259,19 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) kk[nt][e] = qk[nt][e] = 0.f;
-#pragma unroll 4
+        // Q and K were rounded to tf32 by the prologue: ldmatrix feeds them as is
+        const uint32_t aKs = smem_u32(sK), aQs = smem_u32(sQV);
+#pragma unroll 2
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;
-            const uint32_t ak0 = f2tf32(sw_ld(sK, PFG_C, r0 + g, c0)), ak1 = f2tf32(sw_ld(sK, PFG_C, r0 + g + 8, c0));
-            const uint32_t ak2 = f2tf32(sw_ld(sK, PFG_C, r0 + g, c1)), ak3 = f2tf32(sw_ld(sK, PFG_C, r0 + g + 8, c1));
-            const uint32_t aq0 = f2tf32(sw_ld(sQV, PFG_C, r0 + g, c0)), aq1 = f2tf32(sw_ld(sQV, PFG_C, r0 + g + 8, c0));
-            const uint32_t aq2 = f2tf32(sw_ld(sQV, PFG_C, r0 + g, c1)), aq3 = f2tf32(sw_ld(sQV, PFG_C, r0 + g + 8, c1));
+            uint32_t ak[4], aq[4];
+            lda_sw(aKs, r0, ks, lane, ak);
+            lda_sw(aQs, r0, ks, lane, aq);
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
-                const uint32_t b0 = f2tf32(sw_ld(sK, PFG_C, nt * 8 + g, c0));
-                const uint32_t b1 = f2tf32(sw_ld(sK, PFG_C, nt * 8 + g, c1));
-                mma_tf32(kk[nt], ak0, ak1, ak2, ak3, b0, b1);
-                mma_tf32(qk[nt], aq0, aq1, aq2, aq3, b0, b1);
+                uint32_t b0, b1;
+                ldb_sw(aKs, nt * 8, ks, lane, b0, b1);
+                mma_tf32(kk[nt], ak[0], ak[1], ak[2], ak[3], b0, b1);
+                mma_tf32(qk[nt], aq[0], aq[1], aq[2], aq[3], b0, b1);
             }
         }
         float *Mg = p.M + ((size_t)n * p.VH + h) * PFG_C * PFG_C;
@@ -227,7 +282,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const int i = r0 + g + ((e >> 1) << 3), j = nt * 8 + 2 * tq + (e & 1);
                 const float dec = expf(G[i] - G[j]);
                 sA[i * PREP_LD + j] = j < i ? bet[i] * dec * kk[nt][e] : 0.f;
-                Mg[i * PFG_C + j] = j <= i ? dec * qk[nt][e] : 0.f;
+                Mg[i * PFG_C + j] = j <= i ? tf32r(dec * qk[nt][e]) : 0.f;
             }
         }
     }
@@ -291,8 +346,8 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int nt = 0; nt < 8; ++nt) {
             const int col = half * 64 + nt * 8 + 2 * tq;
             const int ra = r0 + g, rb = ra + 8;
-            *reinterpret_cast<float2 *>(Wg + ra * PFG_D + col) = make_float2(w[nt][0], w[nt][1]);
-            *reinterpret_cast<float2 *>(Wg + rb * PFG_D + col) = make_float2(w[nt][2], w[nt][3]);
+            *reinterpret_cast<float2 *>(Wg + ra * PFG_D + col) = make_float2(tf32r(w[nt][0]), tf32r(w[nt][1]));
+            *reinterpret_cast<float2 *>(Wg + rb * PFG_D + col) = make_float2(tf32r(w[nt][2]), tf32r(w[nt][3]));
             *reinterpret_cast<float2 *>(Ug + ra * PFG_D + col) = make_float2(u[nt][0], u[nt][1]);
             *reinterpret_cast<float2 *>(Ug + rb * PFG_D + col) = make_float2(u[nt][2], u[nt][3]);
         }
@@ -301,10 +356,16 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
 // ---------------------------------------------------------------- chunk scan
 constexpr int SCAN_CB = 32;   // state columns per CTA
-constexpr int SCAN_LD = 40;   // padded row stride of the h / D operand tiles
+constexpr int SCAN_WARPS = 16;
+constexpr int HT_LD = 132;    // row stride (floats) of h^T [dv][dk]: 16B rows, conflict-free ldmatrix
+constexpr int DT_LD = 68;     // row stride (floats) of D^T [dv][token]
 
+// 16 warps share each chunk's products so every SM sub-partition interleaves
+// four warps: in phases (a) and (b) warp w owns token rows 16(w&3).. and state
+// columns 8(w>>2)..; in phase (c) it owns dk rows 16(w&7).. and columns
+// 16(w>>3)... Operand fragments come from shared memory with ldmatrix.
 template <typename TI, typename TO>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(128, 1)
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(SCAN_WARPS * 32, 1)
 gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmU,
                    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmM,
                    const __grid_constant__ CUtensorMap tmK, GdnPrefillArgs p)
@@ -317,11 +378,12 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     float *sK = sQ + PFG_C * PFG_D;           // [64 x 128]
     float *sM = sK + PFG_C * PFG_D;           // [64 x 64]
     float *sU = sM + PFG_C * PFG_C;           // [64 x 32]
-    float *sH = sU + PFG_C * SCAN_CB;         // h as [dk 128][40]
-    float *sD = sH + PFG_D * SCAN_LD;         // D as [token 64][40]
-    float *sDt = sD + PFG_C * SCAN_LD;        // e^{G_C - G} D as [token 64][40]
+    float *sHt = sU + PFG_C * SCAN_CB;        // h^T as [dv 32][HT_LD]
+    float *sD = sHt + SCAN_CB * HT_LD;        // D^T as [dv 32][DT_LD]
+    float *sDt = sD + SCAN_CB * DT_LD;        // (e^{G_C - G} D)^T as [dv 32][DT_LD]
     __shared__ float G[2][PFG_C];
     __shared__ float ss[2][PFG_C];
+    __shared__ float ssp[4][PFG_C];
     __shared__ __align__(8) uint64_t bar_wu, bar_qm, bar_k;
 
     const int cblk = blockIdx.x & 3, h = blockIdx.x >> 2, kh = h >> 1;
@@ -329,6 +391,8 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     const int S = p.S, nchunks = (S + PFG_C - 1) / PFG_C;
     const int VD = PFG_D, VH = p.VH;
     const int VHin = p.VHin ? p.VHin : VH, vg = 2 * p.kh0 + h;  // V head in the input layout
+    const uint32_t aW = smem_u32(sW), aQ = smem_u32(sQ), aM = smem_u32(sM);
+    const uint32_t aHt = smem_u32(sHt), aD = smem_u32(sD), aDt = smem_u32(sDt);
 
     auto load_wu = [&](int n) {
         mbar_expect_tx(&bar_wu, (PFG_C * PFG_D + PFG_C * SCAN_CB) * 4);
@@ -353,156 +417,141 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     if (tid == 0) { load_wu(0); load_qm(0); load_k(0); }
     if (warp == 0) chunk_cumsum(p.GL + (size_t)h * S, 0, S, lane, G[0]);
 
-    // state slice: warp owns dk rows 32w..32w+31 (2 m-tiles) x 32 columns (4 n-tiles)
-    float hs[2][4][4];
+    // phase (c) ownership: dk rows 16*mt.., state columns 16*nb.. (2 n-tiles)
+    const int mt = warp & 7, nb = warp >> 3;
+    float hs[2][4];
     float *state = p.state + (size_t)h * PFG_D * VD + cblk * SCAN_CB;
+    auto store_ht = [&]() {  // h (fp32 master, C fragments) -> h^T operand tile
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int ra = warp * 32 + mt * 16 + g, col = nt * 8 + 2 * tq;
-            const float2 x0 = *reinterpret_cast<const float2 *>(state + (size_t)ra * VD + col);
-            const float2 x1 = *reinterpret_cast<const float2 *>(state + (size_t)(ra + 8) * VD + col);
-            hs[mt][nt][0] = x0.x; hs[mt][nt][1] = x0.y; hs[mt][nt][2] = x1.x; hs[mt][nt][3] = x1.y;
-            *reinterpret_cast<float2 *>(sH + ra * SCAN_LD + col) = x0;
-            *reinterpret_cast<float2 *>(sH + (ra + 8) * SCAN_LD + col) = x1;
+        for (int j = 0; j < 2; ++j) {
+            const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
+            sHt[col * HT_LD + ra] = tf32r(hs[j][0]);
+            sHt[(col + 1) * HT_LD + ra] = tf32r(hs[j][1]);
+            sHt[col * HT_LD + ra + 8] = tf32r(hs[j][2]);
+            sHt[(col + 1) * HT_LD + ra + 8] = tf32r(hs[j][3]);
         }
+    };
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
+        const float2 x0 = *reinterpret_cast<const float2 *>(state + (size_t)ra * VD + col);
+        const float2 x1 = *reinterpret_cast<const float2 *>(state + (size_t)(ra + 8) * VD + col);
+        hs[j][0] = x0.x; hs[j][1] = x0.y; hs[j][2] = x1.x; hs[j][3] = x1.y;
+    }
+    store_ht();
     __syncthreads();
 
-    const int r0 = warp * 16;  // this warp's token rows in phases (a) and (b)
+    const int r0 = (warp & 3) * 16;  // phases (a), (b): token rows
+    const int nt = warp >> 2;        // phases (a), (b): state columns 8*nt..
+    // output columns of this thread, and their gated-norm weights
+    const int ocol = cblk * SCAN_CB + nt * 8 + 2 * tq;
+    const float gw0 = p.gnorm[ocol], gw1 = p.gnorm[ocol + 1];
     // A timed-out wait raises the device error word; the loop still runs to
     // the end so that every CTA of the cluster meets every cluster barrier.
     for (int n = 0; n < nchunks; ++n) {
         const int par = n & 1;
         const float *Gc = G[par];
+        // silu(z) inputs of this thread's output elements, loaded early so the
+        // global latency hides behind the chunk's products
+        float sz[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int t = n * PFG_C + r0 + g + 8 * (q >> 1);
+            sz[q] = t < S ? to_f32(static_cast<const TI *>(p.z)[(size_t)t * VHin * VD + vg * VD + ocol + (q & 1)])
+                          : 0.f;
+        }
         // ---- (a) D = U - W h   (accumulated as W h - U, negated below)
         mbar_wait(&bar_wu, par);
-        float d[4][4];
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
+        float d[4];
+        {
             const int col = nt * 8 + 2 * tq;
-            d[nt][0] = -sw_ld(sU, PFG_C, r0 + g, col);     d[nt][1] = -sw_ld(sU, PFG_C, r0 + g, col + 1);
-            d[nt][2] = -sw_ld(sU, PFG_C, r0 + g + 8, col); d[nt][3] = -sw_ld(sU, PFG_C, r0 + g + 8, col + 1);
+            d[0] = -sw_ld(sU, PFG_C, r0 + g, col);     d[1] = -sw_ld(sU, PFG_C, r0 + g, col + 1);
+            d[2] = -sw_ld(sU, PFG_C, r0 + g + 8, col); d[3] = -sw_ld(sU, PFG_C, r0 + g + 8, col + 1);
         }
-#pragma unroll 4
-        for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;
-            const uint32_t a0 = f2tf32(sw_ld(sW, PFG_C, r0 + g, c0)), a1 = f2tf32(sw_ld(sW, PFG_C, r0 + g + 8, c0));
-            const uint32_t a2 = f2tf32(sw_ld(sW, PFG_C, r0 + g, c1)), a3 = f2tf32(sw_ld(sW, PFG_C, r0 + g + 8, c1));
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const uint32_t b0 = f2tf32(sH[c0 * SCAN_LD + nt * 8 + g]);
-                const uint32_t b1 = f2tf32(sH[c1 * SCAN_LD + nt * 8 + g]);
-                mma_tf32(d[nt], a0, a1, a2, a3, b0, b1);
-            }
+        for (int ks = 0; ks < PFG_D / 8; ++ks) {
+            uint32_t a[4], b0, b1;
+            lda_sw(aW, r0, ks, lane, a);
+            ldb_rm(aHt, HT_LD, nt * 8, ks, lane, b0, b1);
+            mma_tf32(d, a[0], a[1], a[2], a[3], b0, b1);
         }
         {
             const float gC = Gc[PFG_C - 1];
             const float sa = expf(gC - Gc[r0 + g]), sb = expf(gC - Gc[r0 + g + 8]);
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const int col = nt * 8 + 2 * tq;
-                const float D0 = -d[nt][0], D1 = -d[nt][1], D2 = -d[nt][2], D3 = -d[nt][3];
-                *reinterpret_cast<float2 *>(sD + (r0 + g) * SCAN_LD + col) = make_float2(D0, D1);
-                *reinterpret_cast<float2 *>(sD + (r0 + g + 8) * SCAN_LD + col) = make_float2(D2, D3);
-                *reinterpret_cast<float2 *>(sDt + (r0 + g) * SCAN_LD + col) = make_float2(D0 * sa, D1 * sa);
-                *reinterpret_cast<float2 *>(sDt + (r0 + g + 8) * SCAN_LD + col) = make_float2(D2 * sb, D3 * sb);
-            }
+            const int col = nt * 8 + 2 * tq, ta = r0 + g, tb = ta + 8;
+            const float D0 = -d[0], D1 = -d[1], D2 = -d[2], D3 = -d[3];
+            sD[col * DT_LD + ta] = tf32r(D0);  sD[(col + 1) * DT_LD + ta] = tf32r(D1);
+            sD[col * DT_LD + tb] = tf32r(D2);  sD[(col + 1) * DT_LD + tb] = tf32r(D3);
+            sDt[col * DT_LD + ta] = tf32r(D0 * sa);  sDt[(col + 1) * DT_LD + ta] = tf32r(D1 * sa);
+            sDt[col * DT_LD + tb] = tf32r(D2 * sb);  sDt[(col + 1) * DT_LD + tb] = tf32r(D3 * sb);
         }
         __syncthreads();                                   // D complete; W/U free
         if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_wu(n + 1); }
 
         // ---- (b) Y = diag(gamma) Q h + M D
         mbar_wait(&bar_qm, par);
-        float y[4][4];
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) y[nt][0] = y[nt][1] = y[nt][2] = y[nt][3] = 0.f;
-#pragma unroll 4
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;
-            const uint32_t a0 = f2tf32(sw_ld(sQ, PFG_C, r0 + g, c0)), a1 = f2tf32(sw_ld(sQ, PFG_C, r0 + g + 8, c0));
-            const uint32_t a2 = f2tf32(sw_ld(sQ, PFG_C, r0 + g, c1)), a3 = f2tf32(sw_ld(sQ, PFG_C, r0 + g + 8, c1));
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const uint32_t b0 = f2tf32(sH[c0 * SCAN_LD + nt * 8 + g]);
-                const uint32_t b1 = f2tf32(sH[c1 * SCAN_LD + nt * 8 + g]);
-                mma_tf32(y[nt], a0, a1, a2, a3, b0, b1);
-            }
+            uint32_t a[4], b0, b1;
+            lda_sw(aQ, r0, ks, lane, a);
+            ldb_rm(aHt, HT_LD, nt * 8, ks, lane, b0, b1);
+            mma_tf32(y, a[0], a[1], a[2], a[3], b0, b1);
         }
         {
             const float ga = expf(Gc[r0 + g]), gb = expf(Gc[r0 + g + 8]);
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) { y[nt][0] *= ga; y[nt][1] *= ga; y[nt][2] *= gb; y[nt][3] *= gb; }
+            y[0] *= ga; y[1] *= ga; y[2] *= gb; y[3] *= gb;
         }
-#pragma unroll 2
+#pragma unroll
         for (int ks = 0; ks < PFG_C / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;
-            const uint32_t a0 = f2tf32(sw_ld(sM, PFG_C, r0 + g, c0)), a1 = f2tf32(sw_ld(sM, PFG_C, r0 + g + 8, c0));
-            const uint32_t a2 = f2tf32(sw_ld(sM, PFG_C, r0 + g, c1)), a3 = f2tf32(sw_ld(sM, PFG_C, r0 + g + 8, c1));
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const uint32_t b0 = f2tf32(sD[c0 * SCAN_LD + nt * 8 + g]);
-                const uint32_t b1 = f2tf32(sD[c1 * SCAN_LD + nt * 8 + g]);
-                mma_tf32(y[nt], a0, a1, a2, a3, b0, b1);
-            }
+            uint32_t a[4], b0, b1;
+            lda_sw(aM, r0, ks, lane, a);
+            ldb_rm(aD, DT_LD, nt * 8, ks, lane, b0, b1);
+            mma_tf32(y, a[0], a[1], a[2], a[3], b0, b1);
         }
-        // partial sum of squares of this CTA's 32 columns, per token row
+        // partial sum of squares of this warp's 8 columns, per token row
         {
-            float sa = 0.f, sb = 0.f;
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                sa += y[nt][0] * y[nt][0] + y[nt][1] * y[nt][1];
-                sb += y[nt][2] * y[nt][2] + y[nt][3] * y[nt][3];
-            }
+            float sa = y[0] * y[0] + y[1] * y[1], sb = y[2] * y[2] + y[3] * y[3];
             sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
             sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
-            if (tq == 0) { ss[par][r0 + g] = sa; ss[par][r0 + g + 8] = sb; }
+            if (tq == 0) { ssp[nt][r0 + g] = sa; ssp[nt][r0 + g + 8] = sb; }
         }
-        __syncthreads();                                   // Q/M and sH reads done
+        __syncthreads();                                   // Q/M and h^T reads done; ssp complete
         if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_qm(n + 1); }
-        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        if (tid < PFG_C) ss[par][tid] = (ssp[0][tid] + ssp[1][tid]) + (ssp[2][tid] + ssp[3][tid]);
+        __syncthreads();
+        cluster_arrive_release();
 
         // ---- (c) h = gamma_C h + K^T (e^{G_C - G} D)
         mbar_wait(&bar_k, par);
         {
             const float gam = expf(Gc[PFG_C - 1]);
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) hs[mt][nt][e] *= gam;
+                for (int e = 0; e < 4; ++e) hs[j][e] *= gam;
         }
-#pragma unroll 2
+#pragma unroll
         for (int ks = 0; ks < PFG_C / 8; ++ks) {
             const int c0 = ks * 8 + tq, c1 = c0 + 4;   // token index (k dimension)
+            const int ra = mt * 16 + g;                // dk row
+            // K was rounded to tf32 by the prologue: pass its bits as they are
+            const uint32_t a0 = __float_as_uint(sw_ld(sK, PFG_C, c0, ra)), a1 = __float_as_uint(sw_ld(sK, PFG_C, c0, ra + 8));
+            const uint32_t a2 = __float_as_uint(sw_ld(sK, PFG_C, c1, ra)), a3 = __float_as_uint(sw_ld(sK, PFG_C, c1, ra + 8));
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int ra = warp * 32 + mt * 16 + g;  // dk row
-                const uint32_t a0 = f2tf32(sw_ld(sK, PFG_C, c0, ra)), a1 = f2tf32(sw_ld(sK, PFG_C, c0, ra + 8));
-                const uint32_t a2 = f2tf32(sw_ld(sK, PFG_C, c1, ra)), a3 = f2tf32(sw_ld(sK, PFG_C, c1, ra + 8));
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    const uint32_t b0 = f2tf32(sDt[c0 * SCAN_LD + nt * 8 + g]);
-                    const uint32_t b1 = f2tf32(sDt[c1 * SCAN_LD + nt * 8 + g]);
-                    mma_tf32(hs[mt][nt], a0, a1, a2, a3, b0, b1);
-                }
+            for (int j = 0; j < 2; ++j) {
+                uint32_t b0, b1;
+                ldb_rm(aDt, DT_LD, (2 * nb + j) * 8, ks, lane, b0, b1);
+                mma_tf32(hs[j], a0, a1, a2, a3, b0, b1);
             }
         }
         if (warp == 0 && n + 1 < nchunks) chunk_cumsum(p.GL + (size_t)h * S, (n + 1) * PFG_C, S, lane, G[par ^ 1]);
-        __syncthreads();                                   // K, sDt reads done
+        __syncthreads();                                   // K, D~ reads done
         if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_k(n + 1); }
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                const int ra = warp * 32 + mt * 16 + g, col = nt * 8 + 2 * tq;
-                *reinterpret_cast<float2 *>(sH + ra * SCAN_LD + col) = make_float2(hs[mt][nt][0], hs[mt][nt][1]);
-                *reinterpret_cast<float2 *>(sH + (ra + 8) * SCAN_LD + col) = make_float2(hs[mt][nt][2], hs[mt][nt][3]);
-            }
+        store_ht();
 
         // ---- gated RMSNorm over the head's 128 columns (4 CTAs) and output
-        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+        cluster_wait();
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             const int i = r0 + g + 8 * half, t = n * PFG_C + i;
@@ -511,29 +560,22 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             for (int r = 0; r < 4; ++r) tot += *cluster.map_shared_rank(&ss[par][i], r);
             const float rinv = 1.f / sqrtf(tot / VD + p.eps);
             if (t < S) {
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = cblk * SCAN_CB + nt * 8 + 2 * tq + e;
-                        const float z = to_f32(static_cast<const TI *>(p.z)[(size_t)t * VHin * VD + vg * VD + col]);
-                        const float out = y[nt][2 * half + e] * rinv * p.gnorm[col] * siluf_(z);
-                        static_cast<TO *>(p.y)[(size_t)t * VH * VD + h * VD + col] = from_f32<TO>(out);
-                    }
-                }
+                const float o0 = y[2 * half] * rinv * gw0 * siluf_(sz[2 * half]);
+                const float o1 = y[2 * half + 1] * rinv * gw1 * siluf_(sz[2 * half + 1]);
+                TO *dst = static_cast<TO *>(p.y) + (size_t)t * VH * VD + h * VD + ocol;
+                dst[0] = from_f32<TO>(o0);
+                dst[1] = from_f32<TO>(o1);
             }
         }
-        __syncthreads();                                   // sH rewritten for the next chunk
+        __syncthreads();                                   // h^T rewritten for the next chunk
     }
     // final state back to HBM
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int ra = warp * 32 + mt * 16 + g, col = nt * 8 + 2 * tq;
-            *reinterpret_cast<float2 *>(state + (size_t)ra * VD + col) = make_float2(hs[mt][nt][0], hs[mt][nt][1]);
-            *reinterpret_cast<float2 *>(state + (size_t)(ra + 8) * VD + col) = make_float2(hs[mt][nt][2], hs[mt][nt][3]);
-        }
+    for (int j = 0; j < 2; ++j) {
+        const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
+        *reinterpret_cast<float2 *>(state + (size_t)ra * VD + col) = make_float2(hs[j][0], hs[j][1]);
+        *reinterpret_cast<float2 *>(state + (size_t)(ra + 8) * VD + col) = make_float2(hs[j][2], hs[j][3]);
+    }
     cluster.sync();  // peers may still read this CTA's ss
 }
 
@@ -541,8 +583,8 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
 size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD) * 4 + 1024; }
 size_t gdn_scan_smem()
 {
-    return (size_t)(3 * PFG_C * PFG_D + PFG_C * PFG_C + PFG_C * SCAN_CB + PFG_D * SCAN_LD +
-                    2 * PFG_C * SCAN_LD) * 4 + 1024;
+    return (size_t)(3 * PFG_C * PFG_D + PFG_C * PFG_C + PFG_C * SCAN_CB + SCAN_CB * HT_LD +
+                    2 * SCAN_CB * DT_LD) * 4 + 1024;
 }
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
@@ -552,8 +594,8 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     const int nchunks = (a.S + PFG_C - 1) / PFG_C;
     const int CD = 2 * (a.KHin ? a.KHin : a.KH) * PFG_D + (a.VHin ? a.VHin : a.VH) * PFG_D;
     cudaError_t e;
-    if (bf16) gdn_pf_prologue_kernel<__nv_bfloat16><<<dim3(a.S, a.KH), PFG_D, 0, st>>>(a);
-    else gdn_pf_prologue_kernel<float><<<dim3(a.S, a.KH), PFG_D, 0, st>>>(a);
+    if (bf16) gdn_pf_prologue_kernel<__nv_bfloat16><<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), PFG_D, 0, st>>>(a);
+    else gdn_pf_prologue_kernel<float><<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), PFG_D, 0, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (bf16) gdn_pf_hist_kernel<__nv_bfloat16><<<(3 * CD + 255) / 256, 256, 0, st>>>(a);
     else gdn_pf_hist_kernel<float><<<(3 * CD + 255) / 256, 256, 0, st>>>(a);
@@ -565,7 +607,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     auto scan = [&](auto kern) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_scan_smem());
         if (e2 != cudaSuccess) return e2;
-        kern<<<a.VH * 4, 128, gdn_scan_smem(), st>>>(m.W, m.U, m.Q, m.M, m.K, a);
+        kern<<<a.VH * 4, SCAN_WARPS * 32, gdn_scan_smem(), st>>>(m.W, m.U, m.Q, m.M, m.K, a);
         return cudaGetLastError();
     };
     return bf16 ? scan(gdn_pf_scan_kernel<__nv_bfloat16, __nv_bfloat16>)
