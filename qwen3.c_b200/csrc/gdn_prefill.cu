@@ -160,7 +160,7 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
             const float xv = to_f32(x[(size_t)s * CD + ch[c]]);
             float a = 0.f;
             a += w[c].x * h0[c]; a += w[c].y * h1[c]; a += w[c].z * h2[c]; a += w[c].w * xv;
-            out[c] = siluf_(a);
+            out[c] = __fdividef(a, 1.f + __expf(-a));  // silu (fast exp / divide)
             h0[c] = h1[c]; h1[c] = h2[c]; h2[c] = xv;
         }
         float sq = out[0] * out[0], sk = out[1] * out[1];
@@ -293,22 +293,23 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_expect_tx(&bar_v, PFG_C * PFG_D * 4);
         for (int c = 0; c < 4; ++c) tma_load_3d(sQV + c * PFG_C * 32, &tmV, 32 * c, s0, h, &bar_v);
     }
-    // T = (I + A)^-1 by forward substitution, one column per thread
-    if (tid < PFG_C) {
-        const int c = tid;
+    // T = (I + A)^-1 by forward substitution: column c = tid/2, the two
+    // threads of a column split each row's dot product by the parity of j
+    // and combine it with one shuffle (same warp, so no block barrier).
+    {
+        const int c = tid >> 1, hp = tid & 1;
         for (int i = 0; i < PFG_C; ++i) {
-            // four independent partial sums shorten the dependent FMA chain
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            int j = c;
-            for (; j + 3 < i; j += 4) {
+            float a0 = 0.f, a1 = 0.f;
+            int j = c + hp;
+            for (; j + 2 < i; j += 4) {
                 a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
-                a1 += sA[i * PREP_LD + j + 1] * sT[(j + 1) * PREP_LD + c];
-                a2 += sA[i * PREP_LD + j + 2] * sT[(j + 2) * PREP_LD + c];
-                a3 += sA[i * PREP_LD + j + 3] * sT[(j + 3) * PREP_LD + c];
+                a1 += sA[i * PREP_LD + j + 2] * sT[(j + 2) * PREP_LD + c];
             }
-            for (; j < i; ++j) a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
-            const float acc = ((i == c) ? 1.f : 0.f) - ((a0 + a1) + (a2 + a3));
-            sT[i * PREP_LD + c] = i < c ? 0.f : acc;
+            for (; j < i; j += 2) a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
+            float part = a0 + a1;
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            if (hp == 0) sT[i * PREP_LD + c] = i < c ? 0.f : ((i == c) ? 1.f : 0.f) - part;
+            __syncwarp();
         }
     }
     __syncthreads();
