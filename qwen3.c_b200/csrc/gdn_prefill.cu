@@ -223,6 +223,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     float *sK = sQV + PFG_C * PFG_D;            // K chunk
     float *sA = sK + PFG_C * PFG_D;             // [64][68] strictly lower A
     float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1
+    float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
     __shared__ float G[PFG_C], bet[PFG_C];
     __shared__ __align__(8) uint64_t bar_qk, bar_v;
 
@@ -293,23 +294,44 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_expect_tx(&bar_v, PFG_C * PFG_D * 4);
         for (int c = 0; c < 4; ++c) tma_load_3d(sQV + c * PFG_C * 32, &tmV, 32 * c, s0, h, &bar_v);
     }
-    // T = (I + A)^-1 by forward substitution: column c = tid/2, the two
-    // threads of a column split each row's dot product by the parity of j
-    // and combine it with one shuffle (same warp, so no block barrier).
+    // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
+    // diagonal blocks by forward substitution (one column per thread), then
+    // T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one block diagonal at a time.
     {
-        const int c = tid >> 1, hp = tid & 1;
-        for (int i = 0; i < PFG_C; ++i) {
-            float a0 = 0.f, a1 = 0.f;
-            int j = c + hp;
-            for (; j + 2 < i; j += 4) {
-                a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
-                a1 += sA[i * PREP_LD + j + 2] * sT[(j + 2) * PREP_LD + c];
+        for (int e = tid; e < PFG_C * PFG_C; e += 128) sT[(e >> 6) * PREP_LD + (e & 63)] = 0.f;
+        __syncthreads();
+        if (tid < 64) {
+            const int o = (tid >> 4) * 16, c = tid & 15;
+            for (int i = c; i < 16; ++i) {
+                float acc = (i == c) ? 1.f : 0.f;
+                for (int j = c; j < i; ++j) acc -= sA[(o + i) * PREP_LD + o + j] * sT[(o + j) * PREP_LD + o + c];
+                sT[(o + i) * PREP_LD + o + c] = acc;
             }
-            for (; j < i; j += 2) a0 += sA[i * PREP_LD + j] * sT[j * PREP_LD + c];
-            float part = a0 + a1;
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            if (hp == 0) sT[i * PREP_LD + c] = i < c ? 0.f : ((i == c) ? 1.f : 0.f) - part;
-            __syncwarp();
+        }
+        __syncthreads();
+        for (int dist = 1; dist < 4; ++dist) {
+            const int nblk = 4 - dist;                 // blocks (p, p - dist), p = dist..3
+            // X_p = sum_{r=q}^{p-1} A_pr T_rq
+            for (int e = tid; e < nblk * 256; e += 128) {
+                const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
+                const int pr = (dist + bi) * 16, q = bi * 16;
+                float acc = 0.f;
+                for (int r = q; r < pr; r += 16)
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) acc += sA[(pr + i) * PREP_LD + r + k] * sT[(r + k) * PREP_LD + q + j];
+                sX[e] = acc;
+            }
+            __syncthreads();
+            // T_pq = -T_pp X_p
+            for (int e = tid; e < nblk * 256; e += 128) {
+                const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
+                const int pr = (dist + bi) * 16, q = bi * 16;
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) acc += sT[(pr + i) * PREP_LD + pr + k] * sX[(bi << 8) + (k << 4) + j];
+                sT[(pr + i) * PREP_LD + q + j] = -acc;
+            }
+            __syncthreads();
         }
     }
     __syncthreads();
@@ -581,7 +603,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
 }
 
 // ---------------------------------------------------------------- launch
-size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD) * 4 + 1024; }
+size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD + 3 * 256) * 4 + 1024; }
 size_t gdn_scan_smem()
 {
     return (size_t)(3 * PFG_C * PFG_D + PFG_C * PFG_C + PFG_C * SCAN_CB + SCAN_CB * HT_LD +
