@@ -58,7 +58,7 @@ struct GdnLayer {
 
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
-            S_GQ, S_GK, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_COUNT };
+            S_GQ, S_GK, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -406,7 +406,9 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.W = (float *)scratch(S_GW, (size_t)nch * VH * 64 * 128 * 4);
     p.U = (float *)scratch(S_GU, (size_t)nch * VH * 64 * 128 * 4);
     p.M = (float *)scratch(S_GM, (size_t)nch * VH * 64 * 64 * 4);
-    if (!p.Qh || !p.Kh || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M) return 0;
+    p.Dt = (float *)scratch(S_GDT, (size_t)nch * VH * 128 * 64 * 4);
+    p.QH = (float *)scratch(S_GQH, (size_t)nch * VH * 64 * 128 * 4);
+    if (!p.Qh || !p.Kh || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
     p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
     GdnPrefillMaps m;
@@ -414,12 +416,13 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
         !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
         !make_f32_3d(&m.W, p.W, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||
-        !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64))
+        !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64) ||
+        !make_f32_3d(&m.Dt, p.Dt, 64, 128, nch * VH, 32, 128))
         return 0;
     kt_mark(COLI_K_GDN_PREFILL);
     CK(launch_gdn_prefill(p, m, dtype, stream()));
     kt_mark(COLI_K_GDN_PREFILL);
-    g_launches += 4;
+    g_launches += 5;
     return 1;
 }
 

@@ -23,14 +23,13 @@
 //   gdn_pf_prep_kernel      per (chunk, V head), fully parallel: K K^T and
 //                           Q K^T on tf32 mma.sync, T by forward substitution
 //                           in fp32, then W, U and the decay-masked M.
-//   gdn_pf_scan_kernel      per (V head, 32-column block of the state), a
-//                           cluster of the 4 column blocks of a head; walks
+//   gdn_pf_scan_kernel      per (V head, 32-column block of the state): walks
 //                           the chunks in order with the state slice in mma
-//                           accumulators; the gated-RMSNorm statistic goes
-//                           through distributed shared memory. Operands
-//                           arrive by TMA (128B swizzle, no multicast), each
-//                           with its own barrier, so the next chunk's loads
-//                           overlap the current chunk's later phases.
+//                           accumulators, producing D and diag(gamma) Q S0 of
+//                           every chunk. Operands arrive by TMA (128B swizzle,
+//                           no multicast), one barrier per operand group.
+//   gdn_pf_out_kernel       per (chunk, V head), fully parallel: Y = QH + M D,
+//                           gated RMSNorm over the head's 128 columns, y.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -103,6 +102,15 @@ __device__ __forceinline__ void ldb_sw(uint32_t tile, int n0, int ks, int lane, 
     const int mat = (lane >> 3) & 1, row = n0 + (lane & 7);
     const int chunk = ((ks & 3) << 1) + mat;
     ldsm_x2(tile + (ks >> 2) * (PFG_C * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1);
+}
+
+// Same for a swizzled tile of `rows` rows (regions rows x 128 bytes).
+__device__ __forceinline__ void ldb_sw_rows(uint32_t tile, int rows, int n0, int ks, int lane, uint32_t &b0,
+                                            uint32_t &b1)
+{
+    const int mat = (lane >> 3) & 1, row = n0 + (lane & 7);
+    const int chunk = ((ks & 3) << 1) + mat;
+    ldsm_x2(tile + (ks >> 2) * (rows * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1);
 }
 
 // Inclusive cumulative sum of the log decay of one chunk (one warp, 2 rows/lane).
@@ -383,49 +391,47 @@ constexpr int SCAN_WARPS = 16;
 constexpr int HT_LD = 132;    // row stride (floats) of h^T [dv][dk]: 16B rows, conflict-free ldmatrix
 constexpr int DT_LD = 68;     // row stride (floats) of D^T [dv][token]
 
-// 16 warps share each chunk's products so every SM sub-partition interleaves
-// four warps: in phases (a) and (b) warp w owns token rows 16(w&3).. and state
-// columns 8(w>>2)..; in phase (c) it owns dk rows 16(w&7).. and columns
-// 16(w>>3)... Operand fragments come from shared memory with ldmatrix.
-template <typename TI, typename TO>
-__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(SCAN_WARPS * 32, 1)
+// The sequential part: per (V head, 32-column block of the state) the chunks
+// are walked in order with the fp32 state slice in mma accumulators. Per chunk
+//   (a) D = U - W h and QH = diag(gamma) Q h (one pass, shared h fragments),
+//   (c) h = gamma_C h + K^T (e^{G_C-G} D);
+// D (transposed) and QH go to scratch, and gdn_pf_out_kernel turns them into
+// the outputs in parallel over chunks. 16 warps share each chunk: in (a) warp
+// w owns token rows 16(w&3).. and columns 8(w>>2)..; in (c) dk rows 16(w&7)..
+// and columns 16(w>>3)... Operands arrive by TMA, one barrier per operand
+// group, so the next chunk's loads overlap the current chunk's work.
+__global__ void __launch_bounds__(SCAN_WARPS * 32, 1)
 gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmU,
-                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmM,
-                   const __grid_constant__ CUtensorMap tmK, GdnPrefillArgs p)
+                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   GdnPrefillArgs p)
 {
-    cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *sW = base;                         // [64 x 128] swizzled
     float *sQ = sW + PFG_C * PFG_D;           // [64 x 128]
     float *sK = sQ + PFG_C * PFG_D;           // [64 x 128]
-    float *sM = sK + PFG_C * PFG_D;           // [64 x 64]
-    float *sU = sM + PFG_C * PFG_C;           // [64 x 32]
+    float *sU = sK + PFG_C * PFG_D;           // [64 x 32]
     float *sHt = sU + PFG_C * SCAN_CB;        // h^T as [dv 32][HT_LD]
     float *sD = sHt + SCAN_CB * HT_LD;        // D^T as [dv 32][DT_LD]
     float *sDt = sD + SCAN_CB * DT_LD;        // (e^{G_C - G} D)^T as [dv 32][DT_LD]
     __shared__ float G[2][PFG_C];
-    __shared__ float ss[2][PFG_C];
-    __shared__ float ssp[4][PFG_C];
-    __shared__ __align__(8) uint64_t bar_wu, bar_qm, bar_k;
+    __shared__ __align__(8) uint64_t bar_wu, bar_q, bar_k;
 
     const int cblk = blockIdx.x & 3, h = blockIdx.x >> 2, kh = h >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
     const int S = p.S, nchunks = (S + PFG_C - 1) / PFG_C;
     const int VD = PFG_D, VH = p.VH;
-    const int VHin = p.VHin ? p.VHin : VH, vg = 2 * p.kh0 + h;  // V head in the input layout
-    const uint32_t aW = smem_u32(sW), aQ = smem_u32(sQ), aM = smem_u32(sM);
-    const uint32_t aHt = smem_u32(sHt), aD = smem_u32(sD), aDt = smem_u32(sDt);
+    const uint32_t aW = smem_u32(sW), aQ = smem_u32(sQ);
+    const uint32_t aHt = smem_u32(sHt), aDt = smem_u32(sDt);
 
     auto load_wu = [&](int n) {
         mbar_expect_tx(&bar_wu, (PFG_C * PFG_D + PFG_C * SCAN_CB) * 4);
         for (int c = 0; c < 4; ++c) tma_load_3d(sW + c * PFG_C * 32, &tmW, 32 * c, 0, n * VH + h, &bar_wu);
         tma_load_3d(sU, &tmU, 32 * cblk, 0, n * VH + h, &bar_wu);
     };
-    auto load_qm = [&](int n) {
-        mbar_expect_tx(&bar_qm, (PFG_C * PFG_D + PFG_C * PFG_C) * 4);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sQ + c * PFG_C * 32, &tmQ, 32 * c, n * PFG_C, kh, &bar_qm);
-        for (int c = 0; c < 2; ++c) tma_load_3d(sM + c * PFG_C * 32, &tmM, 32 * c, 0, n * VH + h, &bar_qm);
+    auto load_q = [&](int n) {
+        mbar_expect_tx(&bar_q, PFG_C * PFG_D * 4);
+        for (int c = 0; c < 4; ++c) tma_load_3d(sQ + c * PFG_C * 32, &tmQ, 32 * c, n * PFG_C, kh, &bar_q);
     };
     auto load_k = [&](int n) {
         mbar_expect_tx(&bar_k, PFG_C * PFG_D * 4);
@@ -433,18 +439,18 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     };
 
     if (tid == 0) {
-        mbar_init(&bar_wu, 1); mbar_init(&bar_qm, 1); mbar_init(&bar_k, 1);
+        mbar_init(&bar_wu, 1); mbar_init(&bar_q, 1); mbar_init(&bar_k, 1);
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) { load_wu(0); load_qm(0); load_k(0); }
+    if (tid == 0) { load_wu(0); load_q(0); load_k(0); }
     if (warp == 0) chunk_cumsum(p.GL + (size_t)h * S, 0, S, lane, G[0]);
 
     // phase (c) ownership: dk rows 16*mt.., state columns 16*nb.. (2 n-tiles)
     const int mt = warp & 7, nb = warp >> 3;
     float hs[2][4];
     float *state = p.state + (size_t)h * PFG_D * VD + cblk * SCAN_CB;
-    auto store_ht = [&]() {  // h (fp32 master, C fragments) -> h^T operand tile
+    auto store_ht = [&]() {  // h (fp32 master, C fragments) -> tf32 h^T operand tile
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
@@ -464,28 +470,17 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     store_ht();
     __syncthreads();
 
-    const int r0 = (warp & 3) * 16;  // phases (a), (b): token rows
-    const int nt = warp >> 2;        // phases (a), (b): state columns 8*nt..
-    // output columns of this thread, and their gated-norm weights
-    const int ocol = cblk * SCAN_CB + nt * 8 + 2 * tq;
-    const float gw0 = p.gnorm[ocol], gw1 = p.gnorm[ocol + 1];
+    const int r0 = (warp & 3) * 16;  // phase (a): token rows
+    const int nt = warp >> 2;        // phase (a): state columns 8*nt..
     // A timed-out wait raises the device error word; the loop still runs to
-    // the end so that every CTA of the cluster meets every cluster barrier.
+    // the end so that every thread meets every barrier.
     for (int n = 0; n < nchunks; ++n) {
         const int par = n & 1;
         const float *Gc = G[par];
-        // silu(z) inputs of this thread's output elements, loaded early so the
-        // global latency hides behind the chunk's products
-        float sz[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int t = n * PFG_C + r0 + g + 8 * (q >> 1);
-            sz[q] = t < S ? to_f32(static_cast<const TI *>(p.z)[(size_t)t * VHin * VD + vg * VD + ocol + (q & 1)])
-                          : 0.f;
-        }
-        // ---- (a) D = U - W h   (accumulated as W h - U, negated below)
+        // ---- (a) D = U - W h (accumulated as W h - U), QH = gamma Q h
         mbar_wait(&bar_wu, par);
-        float d[4];
+        mbar_wait(&bar_q, par);
+        float d[4], q4[4] = {0.f, 0.f, 0.f, 0.f};
         {
             const int col = nt * 8 + 2 * tq;
             d[0] = -sw_ld(sU, PFG_C, r0 + g, col);     d[1] = -sw_ld(sU, PFG_C, r0 + g, col + 1);
@@ -493,13 +488,16 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         }
 #pragma unroll
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            uint32_t a[4], b0, b1;
+            uint32_t a[4], aq[4], b0, b1;
             lda_sw(aW, r0, ks, lane, a);
+            lda_sw(aQ, r0, ks, lane, aq);
             ldb_rm(aHt, HT_LD, nt * 8, ks, lane, b0, b1);
             mma_tf32(d, a[0], a[1], a[2], a[3], b0, b1);
+            mma_tf32(q4, aq[0], aq[1], aq[2], aq[3], b0, b1);
         }
         {
             const float gC = Gc[PFG_C - 1];
+            const float ga = expf(Gc[r0 + g]), gb = expf(Gc[r0 + g + 8]);
             const float sa = expf(gC - Gc[r0 + g]), sb = expf(gC - Gc[r0 + g + 8]);
             const int col = nt * 8 + 2 * tq, ta = r0 + g, tb = ta + 8;
             const float D0 = -d[0], D1 = -d[1], D2 = -d[2], D3 = -d[3];
@@ -507,43 +505,18 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             sD[col * DT_LD + tb] = tf32r(D2);  sD[(col + 1) * DT_LD + tb] = tf32r(D3);
             sDt[col * DT_LD + ta] = tf32r(D0 * sa);  sDt[(col + 1) * DT_LD + ta] = tf32r(D1 * sa);
             sDt[col * DT_LD + tb] = tf32r(D2 * sb);  sDt[(col + 1) * DT_LD + tb] = tf32r(D3 * sb);
+            float *qh = p.QH + ((size_t)n * VH + h) * PFG_C * PFG_D + cblk * SCAN_CB + col;
+            *reinterpret_cast<float2 *>(qh + (size_t)ta * PFG_D) = make_float2(q4[0] * ga, q4[1] * ga);
+            *reinterpret_cast<float2 *>(qh + (size_t)tb * PFG_D) = make_float2(q4[2] * gb, q4[3] * gb);
         }
-        __syncthreads();                                   // D complete; W/U free
-        if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_wu(n + 1); }
-
-        // ---- (b) Y = diag(gamma) Q h + M D
-        mbar_wait(&bar_qm, par);
-        float y[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            uint32_t a[4], b0, b1;
-            lda_sw(aQ, r0, ks, lane, a);
-            ldb_rm(aHt, HT_LD, nt * 8, ks, lane, b0, b1);
-            mma_tf32(y, a[0], a[1], a[2], a[3], b0, b1);
+        __syncthreads();                                   // D complete; W/U/Q free
+        if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_wu(n + 1); load_q(n + 1); }
+        {   // D^T of this block (32 dv rows x 64 tokens) to scratch, coalesced
+            float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB) * PFG_C;
+            const int row = tid >> 4, c4 = (tid & 15) * 4;
+            *reinterpret_cast<float4 *>(dt + row * PFG_C + c4) =
+                *reinterpret_cast<const float4 *>(sD + row * DT_LD + c4);
         }
-        {
-            const float ga = expf(Gc[r0 + g]), gb = expf(Gc[r0 + g + 8]);
-            y[0] *= ga; y[1] *= ga; y[2] *= gb; y[3] *= gb;
-        }
-#pragma unroll
-        for (int ks = 0; ks < PFG_C / 8; ++ks) {
-            uint32_t a[4], b0, b1;
-            lda_sw(aM, r0, ks, lane, a);
-            ldb_rm(aD, DT_LD, nt * 8, ks, lane, b0, b1);
-            mma_tf32(y, a[0], a[1], a[2], a[3], b0, b1);
-        }
-        // partial sum of squares of this warp's 8 columns, per token row
-        {
-            float sa = y[0] * y[0] + y[1] * y[1], sb = y[2] * y[2] + y[3] * y[3];
-            sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
-            sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
-            if (tq == 0) { ssp[nt][r0 + g] = sa; ssp[nt][r0 + g + 8] = sb; }
-        }
-        __syncthreads();                                   // Q/M and h^T reads done; ssp complete
-        if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_qm(n + 1); }
-        if (tid < PFG_C) ss[par][tid] = (ssp[0][tid] + ssp[1][tid]) + (ssp[2][tid] + ssp[3][tid]);
-        __syncthreads();
-        cluster_arrive_release();
 
         // ---- (c) h = gamma_C h + K^T (e^{G_C - G} D)
         mbar_wait(&bar_k, par);
@@ -569,27 +542,9 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             }
         }
         if (warp == 0 && n + 1 < nchunks) chunk_cumsum(p.GL + (size_t)h * S, (n + 1) * PFG_C, S, lane, G[par ^ 1]);
-        __syncthreads();                                   // K, D~ reads done
+        __syncthreads();                                   // K, D reads done
         if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_k(n + 1); }
         store_ht();
-
-        // ---- gated RMSNorm over the head's 128 columns (4 CTAs) and output
-        cluster_wait();
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            const int i = r0 + g + 8 * half, t = n * PFG_C + i;
-            float tot = 0.f;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) tot += *cluster.map_shared_rank(&ss[par][i], r);
-            const float rinv = 1.f / sqrtf(tot / VD + p.eps);
-            if (t < S) {
-                const float o0 = y[2 * half] * rinv * gw0 * siluf_(sz[2 * half]);
-                const float o1 = y[2 * half + 1] * rinv * gw1 * siluf_(sz[2 * half + 1]);
-                TO *dst = static_cast<TO *>(p.y) + (size_t)t * VH * VD + h * VD + ocol;
-                dst[0] = from_f32<TO>(o0);
-                dst[1] = from_f32<TO>(o1);
-            }
-        }
         __syncthreads();                                   // h^T rewritten for the next chunk
     }
     // final state back to HBM
@@ -599,16 +554,93 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         *reinterpret_cast<float2 *>(state + (size_t)ra * VD + col) = make_float2(hs[j][0], hs[j][1]);
         *reinterpret_cast<float2 *>(state + (size_t)(ra + 8) * VD + col) = make_float2(hs[j][2], hs[j][3]);
     }
-    cluster.sync();  // peers may still read this CTA's ss
+}
+
+// ---------------------------------------------------------------- outputs
+// Parallel over (chunk, V head): Y = QH + M D, then the gated RMSNorm over the
+// head's 128 columns (all in this CTA) and y = Y * rsqrt(mean Y^2 + eps) *
+// gnorm * silu(z).
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(128)
+gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmDt,
+                  GdnPrefillArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *sM = base;                    // [64 x 64] swizzled (2 boxes of 32 columns)
+    float *sDT = sM + PFG_C * PFG_C;     // D^T [128 dv x 64 tokens] swizzled (2 boxes of 32 tokens)
+    __shared__ __align__(8) uint64_t bar;
+    const int n = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    const int VH = p.VH, VD = PFG_D, S = p.S;
+    const int VHin = p.VHin ? p.VHin : VH, vg = 2 * p.kh0 + h;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_expect_tx(&bar, (PFG_C * PFG_C + PFG_D * PFG_C) * 4);
+        for (int c = 0; c < 2; ++c) tma_load_3d(sM + c * PFG_C * 32, &tmM, 32 * c, 0, n * VH + h, &bar);
+        for (int c = 0; c < 2; ++c) tma_load_3d(sDT + c * PFG_D * 32, &tmDt, 32 * c, 0, n * VH + h, &bar);
+    }
+    const int r0 = warp * 16, ta = n * PFG_C + r0 + g, tb = ta + 8;
+    float y[16][4];
+    const float *qh = p.QH + ((size_t)n * VH + h) * PFG_C * PFG_D;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+        const int col = nt * 8 + 2 * tq;
+        const float2 u0 = *reinterpret_cast<const float2 *>(qh + (size_t)(r0 + g) * PFG_D + col);
+        const float2 u1 = *reinterpret_cast<const float2 *>(qh + (size_t)(r0 + g + 8) * PFG_D + col);
+        y[nt][0] = u0.x; y[nt][1] = u0.y; y[nt][2] = u1.x; y[nt][3] = u1.y;
+    }
+    __syncthreads();
+    mbar_wait(&bar, 0);
+    const uint32_t aM = smem_u32(sM), aD = smem_u32(sDT);
+#pragma unroll
+    for (int ks = 0; ks < PFG_C / 8; ++ks) {
+        uint32_t a[4];
+        lda_sw(aM, r0, ks, lane, a);
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) {
+            uint32_t b0, b1;
+            ldb_sw_rows(aD, PFG_D, nt * 8, ks, lane, b0, b1);
+            mma_tf32(y[nt], a[0], a[1], a[2], a[3], b0, b1);
+        }
+    }
+    float sa = 0.f, sb = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+        sa += y[nt][0] * y[nt][0] + y[nt][1] * y[nt][1];
+        sb += y[nt][2] * y[nt][2] + y[nt][3] * y[nt][3];
+    }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    const float ra_ = 1.f / sqrtf(sa / VD + p.eps), rb_ = 1.f / sqrtf(sb / VD + p.eps);
+    const TI *z = static_cast<const TI *>(p.z);
+    TO *out = static_cast<TO *>(p.y);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int col = nt * 8 + 2 * tq + e;
+            const float gw = p.gnorm[col];
+            if (ta < S) {
+                const float zv = to_f32(z[(size_t)ta * VHin * VD + vg * VD + col]);
+                out[(size_t)ta * VH * VD + h * VD + col] = from_f32<TO>(y[nt][e] * ra_ * gw * siluf_(zv));
+            }
+            if (tb < S) {
+                const float zv = to_f32(z[(size_t)tb * VHin * VD + vg * VD + col]);
+                out[(size_t)tb * VH * VD + h * VD + col] = from_f32<TO>(y[nt][2 + e] * rb_ * gw * siluf_(zv));
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------- launch
 size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD + 3 * 256) * 4 + 1024; }
 size_t gdn_scan_smem()
 {
-    return (size_t)(3 * PFG_C * PFG_D + PFG_C * PFG_C + PFG_C * SCAN_CB + SCAN_CB * HT_LD +
-                    2 * SCAN_CB * DT_LD) * 4 + 1024;
+    return (size_t)(3 * PFG_C * PFG_D + PFG_C * SCAN_CB + SCAN_CB * HT_LD + 2 * SCAN_CB * DT_LD) * 4 + 1024;
 }
+size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + PFG_D * PFG_C) * 4 + 1024; }
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st)
@@ -627,14 +659,17 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     if (e != cudaSuccess) return e;
     gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), 128, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    auto scan = [&](auto kern) -> cudaError_t {
-        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_scan_smem());
+    e = cudaFuncSetAttribute(gdn_pf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_scan_smem());
+    if (e != cudaSuccess) return e;
+    gdn_pf_scan_kernel<<<a.VH * 4, SCAN_WARPS * 32, gdn_scan_smem(), st>>>(m.W, m.U, m.Q, m.K, a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    auto out = [&](auto kern) -> cudaError_t {
+        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_out_smem());
         if (e2 != cudaSuccess) return e2;
-        kern<<<a.VH * 4, SCAN_WARPS * 32, gdn_scan_smem(), st>>>(m.W, m.U, m.Q, m.M, m.K, a);
+        kern<<<dim3(nchunks, a.VH), 128, gdn_out_smem(), st>>>(m.M, m.Dt, a);
         return cudaGetLastError();
     };
-    return bf16 ? scan(gdn_pf_scan_kernel<__nv_bfloat16, __nv_bfloat16>)
-                : scan(gdn_pf_scan_kernel<float, float>);
+    return bf16 ? out(gdn_pf_out_kernel<__nv_bfloat16, __nv_bfloat16>) : out(gdn_pf_out_kernel<float, float>);
 }
 
 }  // namespace coli

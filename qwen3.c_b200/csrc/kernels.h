@@ -89,6 +89,8 @@ struct GdnPrefillArgs {
     float *GL, *BETA;                     // scratch [VH][S]
     float *W, *U;                         // scratch [nchunks][VH][64][128]
     float *M;                             // scratch [nchunks][VH][64][64]
+    float *Dt;                            // scratch [nchunks][VH][128][64] (D transposed)
+    float *QH;                            // scratch [nchunks][VH][64][128] (diag(gamma) Q S0)
     int S, KH, VH;
     float eps;
     // head-sharded prefill: this call owns K heads [kh0, kh0+KH) (V heads
@@ -97,7 +99,7 @@ struct GdnPrefillArgs {
     int kh0, KHin, VHin;
 };
 struct GdnPrefillMaps {
-    CUtensorMap Q, K, V, W, U, M;
+    CUtensorMap Q, K, V, W, U, M, Dt;
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st);
