@@ -16,7 +16,7 @@
 //               with tcgen05.ld, causal mask, online softmax in the log2
 //               domain with lazy rescaling (O is corrected in TMEM only when
 //               the running max grows by more than 2^8), P written to shared
-//               memory in the UMMA K-major layout; final epilogue O / l *
+//               memory (two P buffers) in the UMMA K-major layout; final epilogue O / l *
 //               sigmoid(gate).
 // TMEM: 2 x 64 columns of scores + 256 columns of O (512 allocated).
 // Every wait is bounded (see mbar_wait); no cluster multicast.
@@ -30,30 +30,39 @@ constexpr int PF_BM = 128, PF_BN = 64, PF_HD = 256;
 constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB
 constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 32 KiB per K (or V) tile
 constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 16 KiB
-constexpr int PF_SMEM = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES + 1024;
+constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + 2 * PF_P_BYTES;  // 224 KiB
 constexpr int PF_THREADS = 320;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 struct PfBars {
     uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
-    float mx[2][2][PF_BM];   // per-tile row max of each half (double-buffered)
-    float lsum[2][PF_BM];    // final row sums of each half
+    // per-tile row max of each half (double-buffered by tile parity); after
+    // the loop the buffer the last tile did not use carries the row sums
+    float mx[2][2][PF_BM];
 };
+constexpr int PF_SMEM = PF_DATA + (int)sizeof(PfBars);
+static_assert(PF_SMEM <= 232448, "prefill shared memory exceeds the 227 KiB per-CTA limit");
 
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, GqaPrefillArgs p)
 {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // All shared memory is dynamic (no static __shared__), so the window
+    // starts 1024-byte aligned as the 128B-swizzled TMA boxes and UMMA
+    // descriptors need; checked below rather than padded (the budget is tight).
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw;
     uint8_t *sQ = smem;
     uint8_t *sK = sQ + PF_Q_BYTES;              // [2][32 KiB]
     uint8_t *sV = sK + 2 * PF_KV_BYTES;         // [2][32 KiB]
-    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // 16 KiB, one P tile
-    __shared__ PfBars bars;
+    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // [2][16 KiB] P tiles
+    PfBars &bars = *reinterpret_cast<PfBars *>(sP + 2 * PF_P_BYTES);
+    if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA: nothing has started yet
+        if (threadIdx.x == 0) raise_error(2);
+        return;
+    }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H;
@@ -129,7 +138,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tc::fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_BN / 16; ++kk) {
-                    const uint64_t da = tc::desc_k_sw128(aP + kk * 32);
+                    const uint64_t da = tc::desc_k_sw128(aP + b * PF_P_BYTES + kk * 32);
                     const uint64_t db = tc::desc_mn_sw128(aV + b * PF_KV_BYTES + kk * 16 * 128,
                                                           PF_BN * 128, 1024);
                     tc::mma_bf16(tO, da, db, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
@@ -224,9 +233,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 pk[c] = pack_bf16(p0, p1);
             }
             l += rs;
-            // the single P buffer was last read by PV(i-1)
-            if (i >= 1) mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
-            uint8_t *prow = sP + row * 128;
+            // P buffer b was last read by PV(i-2)
+            if (i >= 2) mbar_wait(&bars.pv_done[b], ((i - 2) >> 1) & 1);
+            uint8_t *prow = sP + b * PF_P_BYTES + row * 128;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int ch = 4 * half + q;
@@ -237,9 +246,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_arrive(&bars.p_full[b]);
         }
         // row sum = both halves' partial sums (same running max)
-        bars.lsum[half][row] = l;
+        bars.mx[nt & 1][half][row] = l;
         asm volatile("bar.sync 1, 256;" ::: "memory");
-        l += bars.lsum[half ^ 1][row];
+        l += bars.mx[nt & 1][half ^ 1][row];
         mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1);
         tc::fence_after();
         {
