@@ -6,17 +6,17 @@
 // sigmoid(gate). The prologue (q/k norm, RoPE, K/V append) runs before this
 // kernel (gqa_prologue_kernel), so the new rows are already in the cache.
 //
-// One CTA = 128 query rows of one Q head. Warp roles (320 threads):
+// One CTA = 128 query rows of one Q head. Warp roles (576 threads):
 //   warp 0      TMA producers (lane 0: Q once, then K; lane 1: V): 64-key
 //               tiles into separate 2-stage K and V rings (128B swizzle).
 //   warp 1      MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
 //               two TMEM score buffers (M=128, N=64, K=256), then
 //               O += P V (M=128, N=256, K=64) with V read MN-major.
-//   warps 2..9  softmax: two threads per query row (TMEM lane), scores read
+//   warps 2..17 softmax: four threads per query row (TMEM lane), scores read
 //               with tcgen05.ld, causal mask, online softmax in the log2
 //               domain with lazy rescaling (O is corrected in TMEM only when
 //               the running max grows by more than 2^8), P written to shared
-//               memory (two P buffers) in the UMMA K-major layout; final epilogue O / l *
+//               memory in the UMMA K-major layout; final epilogue O / l *
 //               sigmoid(gate).
 // TMEM: 2 x 64 columns of scores + 256 columns of O (512 allocated).
 // Every wait is bounded (see mbar_wait); no cluster multicast.
@@ -30,8 +30,8 @@ constexpr int PF_BM = 128, PF_BN = 64, PF_HD = 256;
 constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB
 constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 32 KiB per K (or V) tile
 constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 16 KiB
-constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + 2 * PF_P_BYTES;  // 224 KiB
-constexpr int PF_THREADS = 320;
+constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES;  // 208 KiB
+constexpr int PF_THREADS = 576;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 struct PfBars {
@@ -39,7 +39,7 @@ struct PfBars {
     uint32_t tmem_base;
     // per-tile row max of each half (double-buffered by tile parity); after
     // the loop the buffer the last tile did not use carries the row sums
-    float mx[2][2][PF_BM];
+    float mx[2][4][PF_BM];
 };
 constexpr int PF_SMEM = PF_DATA + (int)sizeof(PfBars);
 static_assert(PF_SMEM <= 232448, "prefill shared memory exceeds the 227 KiB per-CTA limit");
@@ -57,8 +57,8 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint8_t *sQ = smem;
     uint8_t *sK = sQ + PF_Q_BYTES;              // [2][32 KiB]
     uint8_t *sV = sK + 2 * PF_KV_BYTES;         // [2][32 KiB]
-    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // [2][16 KiB] P tiles
-    PfBars &bars = *reinterpret_cast<PfBars *>(sP + 2 * PF_P_BYTES);
+    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // 16 KiB P tile
+    PfBars &bars = *reinterpret_cast<PfBars *>(sP + PF_P_BYTES);
     if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA: nothing has started yet
         if (threadIdx.x == 0) raise_error(2);
         return;
@@ -83,8 +83,8 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_init(&bars.k_empty[i], 1);
             mbar_init(&bars.v_empty[i], 1);
             mbar_init(&bars.s_full[i], 1);
-            mbar_init(&bars.s_free[i], 256);
-            mbar_init(&bars.p_full[i], 256);
+            mbar_init(&bars.s_free[i], 512);
+            mbar_init(&bars.p_full[i], 512);
             mbar_init(&bars.pv_done[i], 1);
         }
         fence_mbar_init();
@@ -138,7 +138,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tc::fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_BN / 16; ++kk) {
-                    const uint64_t da = tc::desc_k_sw128(aP + b * PF_P_BYTES + kk * 32);
+                    const uint64_t da = tc::desc_k_sw128(aP + kk * 32);
                     const uint64_t db = tc::desc_mn_sw128(aV + b * PF_KV_BYTES + kk * 16 * 128,
                                                           PF_BN * 128, 1024);
                     tc::mma_bf16(tO, da, db, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
@@ -167,13 +167,13 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     } else {
         // ------------------------------------------------ softmax + epilogue
-        // Two threads per query row: warps 2-5 take score columns 0-31 and O
-        // columns 0-127, warps 6-9 columns 32-63 and O 128-255 of the same
-        // TMEM lanes. Row maxima are exchanged through shared memory under a
-        // named barrier of the 256 softmax threads. Waits never break out of
+        // Four threads per query row: warp w (2..17) takes score columns
+        // 16q..16q+15 and O columns 64q..64q+63 with q = (w-2)/4, of TMEM lanes
+        // 32(w%4).. Row maxima are exchanged through shared memory under a
+        // named barrier of the 512 softmax threads. Waits never break out of
         // the loop (a time-out raises the error word and the loop runs on), so
         // every thread meets every named barrier.
-        const int half = (warp - 2) >> 2;
+        const int qr = (warp - 2) >> 2;
         const int row = 32 * (warp & 3) + lane;            // TMEM lane == query row in tile
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         const int srow = q0 + row;                         // query row index in [0, S)
@@ -184,21 +184,27 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const int b = i & 1;
             mbar_wait(&bars.s_full[b], (i >> 1) & 1);
             tc::fence_after();
-            float x[32];
-            tc::ld32(tS0 + b * PF_BN + 32 * half + lane_off, x);
+            float x[16];
+            tc::ld16(tS0 + b * PF_BN + 16 * qr + lane_off, x);
             tc::wait_ld();
             tc::fence_before();
             mbar_arrive(&bars.s_free[b]);
-            const int key0 = i * PF_BN + 32 * half;
+            const int key0 = i * PF_BN + 16 * qr;
             float mx = -INFINITY;
+            if (key0 + 15 <= qpos) {                       // tile fully visible to this row
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                x[c] = (key0 + c <= qpos) ? x[c] * sl2 : -INFINITY;
-                mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < 16; ++c) { x[c] *= sl2; mx = fmaxf(mx, x[c]); }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    x[c] = (key0 + c <= qpos) ? x[c] * sl2 : -INFINITY;
+                    mx = fmaxf(mx, x[c]);
+                }
             }
-            bars.mx[b][half][row] = mx;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
-            mx = fmaxf(mx, bars.mx[b][half ^ 1][row]);
+            bars.mx[b][qr][row] = mx;
+            asm volatile("bar.sync 1, 512;" ::: "memory");
+            mx = fmaxf(fmaxf(bars.mx[b][0][row], bars.mx[b][1][row]),
+                       fmaxf(bars.mx[b][2][row], bars.mx[b][3][row]));
             const float mnew = fmaxf(m, mx);
             if (i == 0) {
                 m = mnew;
@@ -210,9 +216,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     tc::fence_after();
                     const float alpha = need ? exp2f(m - mnew) : 1.f;
 #pragma unroll 1
-                    for (int c = 0; c < PF_HD / 64; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         float o[32];
-                        const uint32_t col = tO + 128 * half + 32 * c + lane_off;
+                        const uint32_t col = tO + 64 * qr + 32 * c + lane_off;
                         tc::ld32(col, o);
                         tc::wait_ld();
 #pragma unroll
@@ -225,30 +231,32 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             const float mu = (m == -INFINITY) ? 0.f : m;
             float rs = 0.f;
-            uint32_t pk[16];
+            uint32_t pk[8];
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
+            for (int c = 0; c < 8; ++c) {
                 const float p0 = exp2f(x[2 * c] - mu), p1 = exp2f(x[2 * c + 1] - mu);
                 rs += p0 + p1;
                 pk[c] = pack_bf16(p0, p1);
             }
             l += rs;
-            // P buffer b was last read by PV(i-2)
-            if (i >= 2) mbar_wait(&bars.pv_done[b], ((i - 2) >> 1) & 1);
-            uint8_t *prow = sP + b * PF_P_BYTES + row * 128;
+            // the single P buffer was last read by PV(i-1)
+            if (i >= 1) mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
+            uint8_t *prow = sP + row * 128;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int ch = 4 * half + q;
+            for (int q = 0; q < 2; ++q) {
+                const int ch = 2 * qr + q;
                 *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) =
                     make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
             }
             fence_proxy_async();
             mbar_arrive(&bars.p_full[b]);
         }
-        // row sum = both halves' partial sums (same running max)
-        bars.mx[nt & 1][half][row] = l;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        l += bars.mx[nt & 1][half ^ 1][row];
+        // row sum = the four partial sums (same running max); the buffer the
+        // last tile did not use carries them
+        bars.mx[nt & 1][qr][row] = l;
+        asm volatile("bar.sync 1, 512;" ::: "memory");
+        l = (bars.mx[nt & 1][0][row] + bars.mx[nt & 1][1][row]) +
+            (bars.mx[nt & 1][2][row] + bars.mx[nt & 1][3][row]);
         mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1);
         tc::fence_after();
         {
@@ -257,9 +265,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD;
             TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD;
 #pragma unroll 1
-            for (int c = 0; c < PF_HD / 64; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 float o[32];
-                const int d0 = 128 * half + 32 * c;
+                const int d0 = 64 * qr + 32 * c;
                 tc::ld32(tO + d0 + lane_off, o);
                 tc::wait_ld();
                 if (valid) {
