@@ -58,7 +58,7 @@ struct GdnLayer {
 
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
-            S_GQ, S_GK, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_COUNT };
+            S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -400,6 +400,7 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.y = y;
     p.Qh = (float *)scratch(S_GQ, (size_t)KH * S * 128 * 4);
     p.Kh = (float *)scratch(S_GK, (size_t)KH * S * 128 * 4);
+    p.KT = (float *)scratch(S_GKT, (size_t)KH * nch * 64 * 128 * 4);
     p.Vh = (float *)scratch(S_GV, (size_t)VH * S * 128 * 4);
     p.GL = (float *)scratch(S_GL, (size_t)VH * S * 4);
     p.BETA = (float *)scratch(S_GB, (size_t)VH * S * 4);
@@ -408,16 +409,16 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.M = (float *)scratch(S_GM, (size_t)nch * VH * 64 * 64 * 4);
     p.Dt = (float *)scratch(S_GDT, (size_t)nch * VH * 128 * 64 * 4);
     p.QH = (float *)scratch(S_GQH, (size_t)nch * VH * 64 * 128 * 4);
-    if (!p.Qh || !p.Kh || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
+    if (!p.Qh || !p.Kh || !p.KT || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
     p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
     GdnPrefillMaps m;
     if (!make_f32_3d(&m.Q, p.Qh, 128, S, KH, 32, 64) || !make_f32_3d(&m.K, p.Kh, 128, S, KH, 32, 64) ||
         !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
         !make_f32_3d(&m.W, p.W, 128, 64, nch * VH, 32, 64) ||
-        !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64) ||
-        !make_f32_3d(&m.Dt, p.Dt, 64, 128, nch * VH, 32, 128))
+        !make_f32_3d(&m.Dt, p.Dt, 64, 128, nch * VH, 32, 128) ||
+        !make_f32_3d(&m.KT, p.KT, 64, 128, nch * KH, 32, 128))
         return 0;
     kt_mark(COLI_K_GDN_PREFILL);
     CK(launch_gdn_prefill(p, m, dtype, stream()));

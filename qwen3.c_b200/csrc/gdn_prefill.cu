@@ -18,22 +18,24 @@
 //   gdn_pf_prologue_kernel  per (64-token run, K head): sliding conv4 (history
 //                           carried in from the previous call) + SiLU,
 //                           q/k L2 norm, gates -> Q, K, V (fp32, head-major),
-//                           log-decay and beta per V head.
+//                           K also transposed per chunk, log-decay and beta
+//                           per V head.
 //   gdn_pf_hist_kernel      carries the last 3 pre-conv rows out as history.
 //   gdn_pf_prep_kernel      per (chunk, V head), fully parallel: K K^T and
 //                           Q K^T on tf32 mma.sync, T by forward substitution
 //                           in fp32, then W, U and the decay-masked M.
 //   gdn_pf_scan_kernel      per (V head, 32-column block of the state): walks
-//                           the chunks in order with the state slice in mma
-//                           accumulators, producing D and diag(gamma) Q S0 of
-//                           every chunk. Operands arrive by TMA (128B swizzle,
-//                           no multicast), one barrier per operand group.
+//                           the chunks in order with the state slice in TMEM,
+//                           products on tcgen05 (kind::tf32), producing D and
+//                           diag(gamma) Q S0 of every chunk. Operands arrive by
+//                           TMA (128B swizzle, no multicast) in a 2-stage ring.
 //   gdn_pf_out_kernel       per (chunk, V head), fully parallel: Y = QH + M D,
 //                           gated RMSNorm over the head's 128 columns, y.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc05.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -160,44 +162,67 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
         h0[c] = tap(s_begin - 3); h1[c] = tap(s_begin - 2); h2[c] = tap(s_begin - 1);
     }
     __shared__ float red[2][2][4];
-    for (int s = s_begin; s < s_end; ++s) {
-        const int par = s & 1;
-        float out[4];
+    // K of this chunk also goes out transposed ([dk][64 tokens], tokens past S
+    // zero), the A operand of the scan's state update; 4 tokens per store.
+    float *kt = p.KT + (((size_t)kh * gridDim.x + blockIdx.x) * PFG_D + t) * PFG_C;
+    float xn[4];                                   // next token's inputs, loaded one token ahead
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float xv = to_f32(x[(size_t)s * CD + ch[c]]);
-            float a = 0.f;
-            a += w[c].x * h0[c]; a += w[c].y * h1[c]; a += w[c].z * h2[c]; a += w[c].w * xv;
-            out[c] = __fdividef(a, 1.f + __expf(-a));  // silu (fast exp / divide)
-            h0[c] = h1[c]; h1[c] = h2[c]; h2[c] = xv;
-        }
-        float sq = out[0] * out[0], sk = out[1] * out[1];
+    for (int c = 0; c < 4; ++c) xn[c] = to_f32(x[(size_t)s_begin * CD + ch[c]]);
+    for (int s4 = s_begin; s4 < s_end; s4 += 4) {
+        float kb[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            sq += __shfl_xor_sync(0xffffffffu, sq, o);
-            sk += __shfl_xor_sync(0xffffffffu, sk, o);
-        }
-        if (lane == 0) { red[par][0][warp] = sq; red[par][1][warp] = sk; }
-        __syncthreads();
-        sq = (red[par][0][0] + red[par][0][1]) + (red[par][0][2] + red[par][0][3]);
-        sk = (red[par][1][0] + red[par][1][1]) + (red[par][1][2] + red[par][1][3]);
-        const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
-        const float rk = 1.f / sqrtf(sk + p.eps);
-        p.Qh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[0] * rq);
-        p.Kh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[1] * rk);
+        for (int u = 0; u < 4; ++u) {
+            const int s = s4 + u;
+            kb[u] = 0.f;
+            if (s >= s_end) continue;              // uniform across the CTA
+            const int par = s & 1;
+            float xv[4], out[4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
-            p.Vh[((size_t)vh * S + s) * PFG_D + t] = out[2 + j];
-            if (t == j) {
-                const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
-                const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
-                // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
-                p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
-                p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
+            for (int c = 0; c < 4; ++c) xv[c] = xn[c];
+            if (s + 1 < s_end) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xn[c] = to_f32(x[(size_t)(s + 1) * CD + ch[c]]);
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float a = 0.f;
+                a += w[c].x * h0[c]; a += w[c].y * h1[c]; a += w[c].z * h2[c]; a += w[c].w * xv[c];
+                out[c] = __fdividef(a, 1.f + __expf(-a));  // silu (fast exp / divide)
+                h0[c] = h1[c]; h1[c] = h2[c]; h2[c] = xv[c];
+            }
+            float sq = out[0] * out[0], sk = out[1] * out[1];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                sk += __shfl_xor_sync(0xffffffffu, sk, o);
+            }
+            if (lane == 0) { red[par][0][warp] = sq; red[par][1][warp] = sk; }
+            __syncthreads();
+            sq = (red[par][0][0] + red[par][0][1]) + (red[par][0][2] + red[par][0][3]);
+            sk = (red[par][1][0] + red[par][1][1]) + (red[par][1][2] + red[par][1][3]);
+            const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
+            const float rk = 1.f / sqrtf(sk + p.eps);
+            const float kv = tf32r(out[1] * rk);
+            kb[u] = kv;
+            p.Qh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[0] * rq);
+            p.Kh[((size_t)kh * S + s) * PFG_D + t] = kv;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
+                p.Vh[((size_t)vh * S + s) * PFG_D + t] = out[2 + j];
+                if (t == j) {
+                    const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
+                    const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
+                    // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
+                    p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
+                    p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
+                }
             }
         }
+        *reinterpret_cast<float4 *>(kt + (s4 - s_begin)) = make_float4(kb[0], kb[1], kb[2], kb[3]);
     }
+    for (int i = (s_end - s_begin + 3) & ~3; i < PRO_T; i += 4)
+        *reinterpret_cast<float4 *>(kt + i) = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // New conv history = the last 3 pre-conv rows of the owned channels. Needs
@@ -386,173 +411,208 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 }
 
 // ---------------------------------------------------------------- chunk scan
-constexpr int SCAN_CB = 32;   // state columns per CTA
-constexpr int SCAN_WARPS = 16;
-constexpr int HT_LD = 132;    // row stride (floats) of h^T [dv][dk]: 16B rows, conflict-free ldmatrix
-constexpr int DT_LD = 68;     // row stride (floats) of D^T [dv][token]
+// The sequential part, on the 5th-gen tensor core (tcgen05, kind::tf32). Per
+// (V head, 32-column block of the state) the chunks are walked in order:
+//   (a) P = [W; Q] h            M = 128 (64 W rows over 64 Q rows), N = 32, K = 128
+//   (e) D = U - P_W: D^T to scratch, D' = e^{G_C-G} D to shared memory;
+//       QH = diag(gamma) P_Q to scratch
+//   (c) h = gamma_C h + K^T D'  M = 128 (dk), N = 32, K = 64 tokens
+// The fp32 state h lives in TMEM (32 columns). The epilogue warps copy it, tf32
+// rounded, into shared memory as the B operand of (a) and scale it by gamma_C
+// in TMEM before (c) accumulates onto it. Every operand is a K-major
+// 128B-swizzled tile: W, Q and K^T (written transposed per chunk by the
+// prologue) arrive by TMA in a 2-stage ring, h^T and D'^T are written by the
+// epilogue threads. gdn_pf_out_kernel then turns D and QH into the outputs,
+// parallel over chunks.
+// Warp roles: 0 = TMA producer, 1 = TMEM owner and MMA issuer, 2..5 =
+// epilogue (TMEM lane quarter = warp % 4: quarters 0/1 hold the W rows, i.e.
+// tokens 0-31 / 32-63, quarters 2/3 the Q rows; in (c) lane = dk row).
+constexpr int SCAN_CB = 32;                   // state columns per CTA
+constexpr int SCAN_THREADS = 192;
+constexpr uint32_t SC_A_BYTES = 4 * 16384;    // [W; Q]: 4 k-atoms x (128 rows x 128 B)
+constexpr uint32_t SC_K_BYTES = 2 * 16384;    // K^T: 2 k-atoms x (128 dk rows x 128 B)
+constexpr uint32_t SC_BH_BYTES = 4 * 4096;    // h^T: 4 k-atoms x (32 rows x 128 B)
+constexpr uint32_t SC_BD_BYTES = 2 * 4096;    // D'^T: 2 k-atoms x (32 rows x 128 B)
+constexpr uint32_t SC_SMEM = 2 * SC_A_BYTES + 2 * SC_K_BYTES + SC_BH_BYTES + SC_BD_BYTES;
 
-// The sequential part: per (V head, 32-column block of the state) the chunks
-// are walked in order with the fp32 state slice in mma accumulators. Per chunk
-//   (a) D = U - W h and QH = diag(gamma) Q h (one pass, shared h fragments),
-//   (c) h = gamma_C h + K^T (e^{G_C-G} D);
-// D (transposed) and QH go to scratch, and gdn_pf_out_kernel turns them into
-// the outputs in parallel over chunks. 16 warps share each chunk: in (a) warp
-// w owns token rows 16(w&3).. and columns 8(w>>2)..; in (c) dk rows 16(w&7)..
-// and columns 16(w>>3)... Operands arrive by TMA, one barrier per operand
-// group, so the next chunk's loads overlap the current chunk's work.
-__global__ void __launch_bounds__(SCAN_WARPS * 32, 1)
-gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmU,
-                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   GdnPrefillArgs p)
+// Byte offset of element (row r, k) in a K-major 128B-swizzled fp32 tile with
+// `rows` rows per k-atom (32 fp32 of k per 128 B row, 8-row groups 1 KiB apart).
+__device__ __forceinline__ uint32_t kmaj_off(int rows, int r, int k)
+{
+    return (uint32_t)((k >> 5) * rows * 128 + r * 128 + ((((k & 31) >> 2) ^ (r & 7)) << 4) + (k & 3) * 4);
+}
+
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
+gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmKT, GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
-    float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *sW = base;                         // [64 x 128] swizzled
-    float *sQ = sW + PFG_C * PFG_D;           // [64 x 128]
-    float *sK = sQ + PFG_C * PFG_D;           // [64 x 128]
-    float *sU = sK + PFG_C * PFG_D;           // [64 x 32]
-    float *sHt = sU + PFG_C * SCAN_CB;        // h^T as [dv 32][HT_LD]
-    float *sD = sHt + SCAN_CB * HT_LD;        // D^T as [dv 32][DT_LD]
-    float *sDt = sD + SCAN_CB * DT_LD;        // (e^{G_C - G} D)^T as [dv 32][DT_LD]
-    __shared__ float G[2][PFG_C];
-    __shared__ __align__(8) uint64_t bar_wu, bar_q, bar_k;
+    uint8_t *sA = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sK = sA + 2 * SC_A_BYTES;
+    uint8_t *sBh = sK + 2 * SC_K_BYTES;
+    uint8_t *sBd = sBh + SC_BH_BYTES;
+    __shared__ __align__(8) uint64_t a_full[2], a_empty[2], k_full[2], k_empty[2];
+    __shared__ __align__(8) uint64_t h_ready, a_done, d_ready, c_done;
+    __shared__ uint32_t tmem_base;
 
     const int cblk = blockIdx.x & 3, h = blockIdx.x >> 2, kh = h >> 1;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
-    const int S = p.S, nchunks = (S + PFG_C - 1) / PFG_C;
-    const int VD = PFG_D, VH = p.VH;
-    const uint32_t aW = smem_u32(sW), aQ = smem_u32(sQ);
-    const uint32_t aHt = smem_u32(sHt), aDt = smem_u32(sDt);
-
-    auto load_wu = [&](int n) {
-        mbar_expect_tx(&bar_wu, (PFG_C * PFG_D + PFG_C * SCAN_CB) * 4);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sW + c * PFG_C * 32, &tmW, 32 * c, 0, n * VH + h, &bar_wu);
-        tma_load_3d(sU, &tmU, 32 * cblk, 0, n * VH + h, &bar_wu);
-    };
-    auto load_q = [&](int n) {
-        mbar_expect_tx(&bar_q, PFG_C * PFG_D * 4);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sQ + c * PFG_C * 32, &tmQ, 32 * c, n * PFG_C, kh, &bar_q);
-    };
-    auto load_k = [&](int n) {
-        mbar_expect_tx(&bar_k, PFG_C * PFG_D * 4);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sK + c * PFG_C * 32, &tmK, 32 * c, n * PFG_C, kh, &bar_k);
-    };
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = p.S, nch = (S + PFG_C - 1) / PFG_C, VH = p.VH;
 
     if (tid == 0) {
-        mbar_init(&bar_wu, 1); mbar_init(&bar_q, 1); mbar_init(&bar_k, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1);
+            mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
+        }
+        mbar_init(&h_ready, 128); mbar_init(&a_done, 1); mbar_init(&d_ready, 64); mbar_init(&c_done, 1);
         fence_mbar_init();
     }
+    if (warp == 1) tc::alloc(&tmem_base, 64);
+    tc::fence_before();
     __syncthreads();
-    if (tid == 0) { load_wu(0); load_q(0); load_k(0); }
-    if (warp == 0) chunk_cumsum(p.GL + (size_t)h * S, 0, S, lane, G[0]);
+    tc::fence_after();
+    const uint32_t tP = tmem_base, tH = tmem_base + 32;
 
-    // phase (c) ownership: dk rows 16*mt.., state columns 16*nb.. (2 n-tiles)
-    const int mt = warp & 7, nb = warp >> 3;
-    float hs[2][4];
-    float *state = p.state + (size_t)h * PFG_D * VD + cblk * SCAN_CB;
-    auto store_ht = [&]() {  // h (fp32 master, C fragments) -> tf32 h^T operand tile
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
-            sHt[col * HT_LD + ra] = tf32r(hs[j][0]);
-            sHt[(col + 1) * HT_LD + ra] = tf32r(hs[j][1]);
-            sHt[col * HT_LD + ra + 8] = tf32r(hs[j][2]);
-            sHt[(col + 1) * HT_LD + ra + 8] = tf32r(hs[j][3]);
-        }
-    };
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
-        const float2 x0 = *reinterpret_cast<const float2 *>(state + (size_t)ra * VD + col);
-        const float2 x1 = *reinterpret_cast<const float2 *>(state + (size_t)(ra + 8) * VD + col);
-        hs[j][0] = x0.x; hs[j][1] = x0.y; hs[j][2] = x1.x; hs[j][3] = x1.y;
-    }
-    store_ht();
-    __syncthreads();
-
-    const int r0 = (warp & 3) * 16;  // phase (a): token rows
-    const int nt = warp >> 2;        // phase (a): state columns 8*nt..
-    // A timed-out wait raises the device error word; the loop still runs to
-    // the end so that every thread meets every barrier.
-    for (int n = 0; n < nchunks; ++n) {
-        const int par = n & 1;
-        const float *Gc = G[par];
-        // ---- (a) D = U - W h (accumulated as W h - U), QH = gamma Q h
-        mbar_wait(&bar_wu, par);
-        mbar_wait(&bar_q, par);
-        float d[4], q4[4] = {0.f, 0.f, 0.f, 0.f};
-        {
-            const int col = nt * 8 + 2 * tq;
-            d[0] = -sw_ld(sU, PFG_C, r0 + g, col);     d[1] = -sw_ld(sU, PFG_C, r0 + g, col + 1);
-            d[2] = -sw_ld(sU, PFG_C, r0 + g + 8, col); d[3] = -sw_ld(sU, PFG_C, r0 + g + 8, col + 1);
-        }
-#pragma unroll
-        for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            uint32_t a[4], aq[4], b0, b1;
-            lda_sw(aW, r0, ks, lane, a);
-            lda_sw(aQ, r0, ks, lane, aq);
-            ldb_rm(aHt, HT_LD, nt * 8, ks, lane, b0, b1);
-            mma_tf32(d, a[0], a[1], a[2], a[3], b0, b1);
-            mma_tf32(q4, aq[0], aq[1], aq[2], aq[3], b0, b1);
-        }
-        {
-            const float gC = Gc[PFG_C - 1];
-            const float ga = expf(Gc[r0 + g]), gb = expf(Gc[r0 + g + 8]);
-            const float sa = expf(gC - Gc[r0 + g]), sb = expf(gC - Gc[r0 + g + 8]);
-            const int col = nt * 8 + 2 * tq, ta = r0 + g, tb = ta + 8;
-            const float D0 = -d[0], D1 = -d[1], D2 = -d[2], D3 = -d[3];
-            sD[col * DT_LD + ta] = tf32r(D0);  sD[(col + 1) * DT_LD + ta] = tf32r(D1);
-            sD[col * DT_LD + tb] = tf32r(D2);  sD[(col + 1) * DT_LD + tb] = tf32r(D3);
-            sDt[col * DT_LD + ta] = tf32r(D0 * sa);  sDt[(col + 1) * DT_LD + ta] = tf32r(D1 * sa);
-            sDt[col * DT_LD + tb] = tf32r(D2 * sb);  sDt[(col + 1) * DT_LD + tb] = tf32r(D3 * sb);
-            float *qh = p.QH + ((size_t)n * VH + h) * PFG_C * PFG_D + cblk * SCAN_CB + col;
-            *reinterpret_cast<float2 *>(qh + (size_t)ta * PFG_D) = make_float2(q4[0] * ga, q4[1] * ga);
-            *reinterpret_cast<float2 *>(qh + (size_t)tb * PFG_D) = make_float2(q4[2] * gb, q4[3] * gb);
-        }
-        __syncthreads();                                   // D complete; W/U/Q free
-        if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_wu(n + 1); load_q(n + 1); }
-        {   // D^T of this block (32 dv rows x 64 tokens) to scratch, coalesced
-            float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB) * PFG_C;
-            const int row = tid >> 4, c4 = (tid & 15) * 4;
-            *reinterpret_cast<float4 *>(dt + row * PFG_C + c4) =
-                *reinterpret_cast<const float4 *>(sD + row * DT_LD + c4);
-        }
-
-        // ---- (c) h = gamma_C h + K^T (e^{G_C - G} D)
-        mbar_wait(&bar_k, par);
-        {
-            const float gam = expf(Gc[PFG_C - 1]);
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) hs[j][e] *= gam;
-        }
-#pragma unroll
-        for (int ks = 0; ks < PFG_C / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;   // token index (k dimension)
-            const int ra = mt * 16 + g;                // dk row
-            // K was rounded to tf32 by the prologue: pass its bits as they are
-            const uint32_t a0 = __float_as_uint(sw_ld(sK, PFG_C, c0, ra)), a1 = __float_as_uint(sw_ld(sK, PFG_C, c0, ra + 8));
-            const uint32_t a2 = __float_as_uint(sw_ld(sK, PFG_C, c1, ra)), a3 = __float_as_uint(sw_ld(sK, PFG_C, c1, ra + 8));
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                uint32_t b0, b1;
-                ldb_rm(aDt, DT_LD, (2 * nb + j) * 8, ks, lane, b0, b1);
-                mma_tf32(hs[j], a0, a1, a2, a3, b0, b1);
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int n = 0; n < nch; ++n) {
+                const int s = n & 1;
+                if (n >= 2) mbar_wait(&a_empty[s], ((n >> 1) + 1) & 1);
+                uint8_t *a = sA + s * SC_A_BYTES;
+                mbar_expect_tx(&a_full[s], SC_A_BYTES);
+                for (int c = 0; c < 4; ++c) {
+                    tma_load_3d(a + c * 16384, &tmW, 32 * c, 0, n * VH + h, &a_full[s]);
+                    tma_load_3d(a + c * 16384 + 8192, &tmQ, 32 * c, n * PFG_C, kh, &a_full[s]);
+                }
+                if (n >= 2) mbar_wait(&k_empty[s], ((n >> 1) + 1) & 1);
+                uint8_t *k = sK + s * SC_K_BYTES;
+                mbar_expect_tx(&k_full[s], SC_K_BYTES);
+                for (int c = 0; c < 2; ++c) tma_load_3d(k + c * 16384, &tmKT, 32 * c, 0, kh * nch + n, &k_full[s]);
             }
         }
-        if (warp == 0 && n + 1 < nchunks) chunk_cumsum(p.GL + (size_t)h * S, (n + 1) * PFG_C, S, lane, G[par ^ 1]);
-        __syncthreads();                                   // K, D reads done
-        if (tid == 0 && n + 1 < nchunks) { fence_proxy_async(); load_k(n + 1); }
-        store_ht();
-        __syncthreads();                                   // h^T rewritten for the next chunk
-    }
-    // final state back to HBM
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_tf32(128, SCAN_CB);
+            const uint32_t aA = smem_u32(sA), aK = smem_u32(sK), aBh = smem_u32(sBh), aBd = smem_u32(sBd);
+            for (int n = 0; n < nch; ++n) {
+                const int s = n & 1;
+                const uint32_t ph = (n >> 1) & 1;
+                mbar_wait(&a_full[s], ph);
+                mbar_wait(&h_ready, n & 1);
+                tc::fence_after();
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int ra = mt * 16 + g, col = (2 * nb + j) * 8 + 2 * tq;
-        *reinterpret_cast<float2 *>(state + (size_t)ra * VD + col) = make_float2(hs[j][0], hs[j][1]);
-        *reinterpret_cast<float2 *>(state + (size_t)(ra + 8) * VD + col) = make_float2(hs[j][2], hs[j][3]);
+                for (int ks = 0; ks < PFG_D / 8; ++ks)
+                    tc::mma_tf32(tP, tc::desc_k_sw128(aA + s * SC_A_BYTES + (ks >> 2) * 16384 + (ks & 3) * 32),
+                                 tc::desc_k_sw128(aBh + (ks >> 2) * 4096 + (ks & 3) * 32), idesc, ks > 0);
+                tc::commit(&a_done);
+                tc::commit(&a_empty[s]);
+                mbar_wait(&k_full[s], ph);
+                mbar_wait(&d_ready, n & 1);
+                tc::fence_after();
+#pragma unroll
+                for (int ks = 0; ks < PFG_C / 8; ++ks)
+                    tc::mma_tf32(tH, tc::desc_k_sw128(aK + s * SC_K_BYTES + (ks >> 2) * 16384 + (ks & 3) * 32),
+                                 tc::desc_k_sw128(aBd + (ks >> 2) * 4096 + (ks & 3) * 32), idesc, 1);
+                tc::commit(&c_done);
+                tc::commit(&k_empty[s]);
+            }
+        }
+    } else {
+        const int q = warp & 3, half = q & 1;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const int r = q * 32 + lane;               // dk row in (c) / TMEM lane
+        const int t = half * 32 + lane;            // token within the chunk in (e)
+        const float *gl = p.GL + (size_t)h * S;
+        float gl_lo = lane < S ? gl[lane] : 0.f, gl_hi = lane + 32 < S ? gl[lane + 32] : 0.f;
+        float hv[32], u[32], pv[32];
+        float *st = p.state + ((size_t)h * PFG_D + r) * PFG_D + cblk * SCAN_CB;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = reinterpret_cast<const float4 *>(st)[i];
+            hv[4 * i] = v.x; hv[4 * i + 1] = v.y; hv[4 * i + 2] = v.z; hv[4 * i + 3] = v.w;
+        }
+        for (int n = 0; n < nch; ++n) {
+            // inclusive cumulative log decay of this chunk: G_t for this
+            // thread's token, G_C for the whole chunk
+            float slo = gl_lo, shi = gl_hi;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float a = __shfl_up_sync(0xffffffffu, slo, o), b = __shfl_up_sync(0xffffffffu, shi, o);
+                if (lane >= o) { slo += a; shi += b; }
+            }
+            const float tot_lo = __shfl_sync(0xffffffffu, slo, 31);
+            const float GC = tot_lo + __shfl_sync(0xffffffffu, shi, 31);
+            const float Gt = half ? tot_lo + shi : slo;
+            if (n + 1 < nch) {
+                const int t0 = (n + 1) * PFG_C + lane;
+                gl_lo = t0 < S ? gl[t0] : 0.f;
+                gl_hi = t0 + 32 < S ? gl[t0 + 32] : 0.f;
+            }
+            if (q < 2) {
+                const float *ur = p.U + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 v = reinterpret_cast<const float4 *>(ur)[i];
+                    u[4 * i] = v.x; u[4 * i + 1] = v.y; u[4 * i + 2] = v.z; u[4 * i + 3] = v.w;
+                }
+            }
+            // ---- h -> h^T (tf32) for (a); gamma_C h back into TMEM for (c)
+            if (n > 0) {
+                mbar_wait(&c_done, (n - 1) & 1);
+                tc::fence_after();
+                tc::ld32(tH + lane_off, hv);
+                tc::wait_ld();
+            }
+#pragma unroll
+            for (int j = 0; j < SCAN_CB; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(SCAN_CB, j, r)) = tf32r(hv[j]);
+            const float gC = expf(GC);
+#pragma unroll
+            for (int j = 0; j < SCAN_CB; ++j) hv[j] *= gC;
+            tc::st32(tH + lane_off, hv);
+            tc::wait_st();
+            fence_proxy_async();                    // h^T visible to the tensor core
+            tc::fence_before();
+            mbar_arrive(&h_ready);
+            // ---- P = [W; Q] h is in TMEM
+            mbar_wait(&a_done, n & 1);
+            tc::fence_after();
+            tc::ld32(tP + lane_off, pv);
+            tc::wait_ld();
+            if (q < 2) {
+                const float sc = expf(GC - Gt);
+                float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB) * PFG_C + t;
+#pragma unroll
+                for (int j = 0; j < SCAN_CB; ++j) {
+                    const float d = u[j] - pv[j];
+                    dt[j * PFG_C] = tf32r(d);
+                    *reinterpret_cast<float *>(sBd + kmaj_off(SCAN_CB, j, t)) = tf32r(d * sc);
+                }
+                fence_proxy_async();                // D'^T visible to the tensor core
+                tc::fence_before();
+                mbar_arrive(&d_ready);
+            } else {
+                const float gt = expf(Gt);
+                float *qh = p.QH + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB;
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    reinterpret_cast<float4 *>(qh)[i] =
+                        make_float4(pv[4 * i] * gt, pv[4 * i + 1] * gt, pv[4 * i + 2] * gt, pv[4 * i + 3] * gt);
+            }
+        }
+        // final state back to HBM
+        mbar_wait(&c_done, (nch - 1) & 1);
+        tc::fence_after();
+        tc::ld32(tH + lane_off, hv);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            reinterpret_cast<float4 *>(st)[i] = make_float4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+        tc::fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after();
+        tc::dealloc(tmem_base, 64);
     }
 }
 
@@ -636,10 +696,7 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
 
 // ---------------------------------------------------------------- launch
 size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD + 3 * 256) * 4 + 1024; }
-size_t gdn_scan_smem()
-{
-    return (size_t)(3 * PFG_C * PFG_D + PFG_C * SCAN_CB + SCAN_CB * HT_LD + 2 * SCAN_CB * DT_LD) * 4 + 1024;
-}
+size_t gdn_scan_smem() { return (size_t)SC_SMEM + 1024; }
 size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + PFG_D * PFG_C) * 4 + 1024; }
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
@@ -661,7 +718,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(gdn_pf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_scan_smem());
     if (e != cudaSuccess) return e;
-    gdn_pf_scan_kernel<<<a.VH * 4, SCAN_WARPS * 32, gdn_scan_smem(), st>>>(m.W, m.U, m.Q, m.K, a);
+    gdn_pf_scan_kernel<<<a.VH * 4, SCAN_THREADS, gdn_scan_smem(), st>>>(m.W, m.Q, m.KT, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     auto out = [&](auto kern) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_out_smem());

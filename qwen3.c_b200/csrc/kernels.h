@@ -85,6 +85,7 @@ struct GdnPrefillArgs {
     float *state;                         // [VH][KD][VD] of the request (in/out)
     void *y;                              // [S][VH*VD]
     float *Qh, *Kh;                       // scratch [KH][S][128]
+    float *KT;                            // scratch [KH][nchunks][128][64] (K^T per chunk)
     float *Vh;                            // scratch [VH][S][128]
     float *GL, *BETA;                     // scratch [VH][S]
     float *W, *U;                         // scratch [nchunks][VH][64][128]
@@ -99,7 +100,7 @@ struct GdnPrefillArgs {
     int kh0, KHin, VHin;
 };
 struct GdnPrefillMaps {
-    CUtensorMap Q, K, V, W, U, M, Dt;
+    CUtensorMap Q, K, V, W, M, Dt, KT;
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st);

@@ -1,5 +1,5 @@
 // Blackwell 5th-gen tensor core (tcgen05) helpers: TMEM allocation, shared
-// memory matrix descriptors, the kind::f16 MMA with fp32 accumulation in
+// memory matrix descriptors, the kind::f16 and kind::tf32 MMAs with fp32 accumulation in
 // TMEM, commit-to-mbarrier, and TMEM <-> register moves. Written for
 // cta_group::1 (one CTA per MMA); no cluster multicast anywhere.
 //
@@ -8,9 +8,9 @@
 //   smem descriptor: [0,14) start>>4, [16,30) leading byte offset>>4,
 //     [32,46) stride byte offset>>4, [46,48) version = 1, [49,52) base offset,
 //     [52] lbo mode, [61,64) swizzle (2 = 128B).
-//   instr descriptor (kind::f16): [4,6) D format (1 = f32), [7,10) A format,
-//     [10,13) B format (1 = bf16), [15] A major, [16] B major (0 = K, 1 = MN),
-//     [17,23) N>>3, [24,29) M>>4.
+//   instr descriptor (kind::f16 / kind::tf32): [4,6) D format (1 = f32),
+//     [7,10) A format, [10,13) B format (1 = bf16; 2 = tf32 under kind::tf32),
+//     [15] A major, [16] B major (0 = K, 1 = MN), [17,23) N>>3, [24,29) M>>4.
 #pragma once
 #include <stdint.h>
 
@@ -49,6 +49,24 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
 {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
            ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::tf32 instruction descriptor: tf32 A/B (format 2), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N)
+{
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] . B[smem]^T in tf32 (K = 8 per instruction); one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate),
+          "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
 // D[tmem] (+)= A[smem] . B[smem]^T ; issued by one thread.
