@@ -44,15 +44,12 @@ namespace coli {
 constexpr int PFG_C = 64, PFG_D = 128;
 
 // ---------------------------------------------------------------- tf32 MMA
-// fp32 -> tf32 with round-to-nearest. Operands that reach the MMA straight
-// from shared memory (ldmatrix) are rounded once where they are produced
-// (tf32r), since the MMA itself would truncate the low mantissa bits.
-__device__ __forceinline__ uint32_t f2tf32(float x)
-{
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// fp32 -> tf32, round to nearest with ties away from zero (the rounding of
+// cvt.rna.tf32.f32): add half a tf32 ulp (bit 12) to the magnitude bits and
+// clear the 13 low mantissa bits; a carry moves into the exponent as it
+// should. Operands that reach the MMA straight from shared memory are rounded
+// once where they are produced (tf32r), since the MMA itself would truncate.
+__device__ __forceinline__ uint32_t f2tf32(float x) { return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u; }
 __device__ __forceinline__ float tf32r(float x) { return __uint_as_float(f2tf32(x)); }
 // D[16x8] += A[16x8] . B[8x8] in tf32 with fp32 accumulation.
 __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -424,11 +421,14 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 // prologue) arrive by TMA in a 2-stage ring, h^T and D'^T are written by the
 // epilogue threads. gdn_pf_out_kernel then turns D and QH into the outputs,
 // parallel over chunks.
-// Warp roles: 0 = TMA producer, 1 = TMEM owner and MMA issuer, 2..5 =
-// epilogue (TMEM lane quarter = warp % 4: quarters 0/1 hold the W rows, i.e.
-// tokens 0-31 / 32-63, quarters 2/3 the Q rows; in (c) lane = dk row).
+// Warp roles: 0 = TMA producer, 1 = TMEM owner and MMA issuer, then the
+// epilogue warps, 32 / SCAN_EC per TMEM lane quarter (warp % 4), SCAN_EC
+// columns each; quarters 0/1 hold the W rows (tokens 0-31 / 32-63), quarters
+// 2/3 the Q rows; for h, lane = dk row.
 constexpr int SCAN_CB = 32;                   // state columns per CTA
-constexpr int SCAN_THREADS = 192;
+constexpr int SCAN_EC = 8;                    // state columns per epilogue thread
+constexpr int SCAN_EPI = 4 * (SCAN_CB / SCAN_EC) * 32;  // epilogue threads
+constexpr int SCAN_THREADS = 64 + SCAN_EPI;
 constexpr uint32_t SC_A_BYTES = 4 * 16384;    // [W; Q]: 4 k-atoms x (128 rows x 128 B)
 constexpr uint32_t SC_K_BYTES = 2 * 16384;    // K^T: 2 k-atoms x (128 dk rows x 128 B)
 constexpr uint32_t SC_BH_BYTES = 4 * 4096;    // h^T: 4 k-atoms x (32 rows x 128 B)
@@ -452,7 +452,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     uint8_t *sBh = sK + 2 * SC_K_BYTES;
     uint8_t *sBd = sBh + SC_BH_BYTES;
     __shared__ __align__(8) uint64_t a_full[2], a_empty[2], k_full[2], k_empty[2];
-    __shared__ __align__(8) uint64_t h_ready, a_done, d_ready, c_done;
+    __shared__ __align__(8) uint64_t h_ready, hs_ready, a_done, d_ready, c_done;
     __shared__ uint32_t tmem_base;
 
     const int cblk = blockIdx.x & 3, h = blockIdx.x >> 2, kh = h >> 1;
@@ -464,7 +464,8 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1);
             mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
         }
-        mbar_init(&h_ready, 128); mbar_init(&a_done, 1); mbar_init(&d_ready, 64); mbar_init(&c_done, 1);
+        mbar_init(&h_ready, SCAN_EPI); mbar_init(&hs_ready, SCAN_EPI); mbar_init(&a_done, 1);
+        mbar_init(&d_ready, SCAN_EPI / 2); mbar_init(&c_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) tc::alloc(&tmem_base, 64);
@@ -508,6 +509,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 tc::commit(&a_empty[s]);
                 mbar_wait(&k_full[s], ph);
                 mbar_wait(&d_ready, n & 1);
+                mbar_wait(&hs_ready, n & 1);
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < PFG_C / 8; ++ks)
@@ -518,16 +520,24 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             }
         }
     } else {
-        const int q = warp & 3, half = q & 1;
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const int q = warp & 3, half = q & 1, c0 = ((warp - 2) >> 2) * SCAN_EC;  // lane quarter, first column
+        const uint32_t lane_off = ((uint32_t)(q * 32) << 16) + c0;
         const int r = q * 32 + lane;               // dk row in (c) / TMEM lane
         const int t = half * 32 + lane;            // token within the chunk in (e)
         const float *gl = p.GL + (size_t)h * S;
         float gl_lo = lane < S ? gl[lane] : 0.f, gl_hi = lane + 32 < S ? gl[lane + 32] : 0.f;
-        float hv[32], u[32], pv[32];
-        float *st = p.state + ((size_t)h * PFG_D + r) * PFG_D + cblk * SCAN_CB;
+        float hv[SCAN_EC], u[SCAN_EC], pv[SCAN_EC];
+        float4 un[SCAN_EC / 4];
+        auto load_u = [&](int n) {
+            const float4 *ur = reinterpret_cast<const float4 *>(
+                p.U + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB + c0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < SCAN_EC / 4; ++i) un[i] = ur[i];
+        };
+        if (q < 2) load_u(0);
+        float *st = p.state + ((size_t)h * PFG_D + r) * PFG_D + cblk * SCAN_CB + c0;
+#pragma unroll
+        for (int i = 0; i < SCAN_EC / 4; ++i) {
             const float4 v = reinterpret_cast<const float4 *>(st)[i];
             hv[4 * i] = v.x; hv[4 * i + 1] = v.y; hv[4 * i + 2] = v.z; hv[4 * i + 3] = v.w;
         }
@@ -543,69 +553,72 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             const float tot_lo = __shfl_sync(0xffffffffu, slo, 31);
             const float GC = tot_lo + __shfl_sync(0xffffffffu, shi, 31);
             const float Gt = half ? tot_lo + shi : slo;
+            // decay factors of this chunk: gamma_C for h, e^{G_C-G_t} for D', gamma_t for QH
+            const float gC = expf(GC), sc = q < 2 ? expf(GC - Gt) : expf(Gt);
+            asm volatile("" ::"f"(gC), "f"(sc));   // keep them here, off the critical path
             if (n + 1 < nch) {
                 const int t0 = (n + 1) * PFG_C + lane;
                 gl_lo = t0 < S ? gl[t0] : 0.f;
                 gl_hi = t0 + 32 < S ? gl[t0 + 32] : 0.f;
             }
-            if (q < 2) {
-                const float *ur = p.U + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB;
+            if (q < 2) {   // this chunk's U; the next chunk's loads are issued a chunk ahead
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float4 v = reinterpret_cast<const float4 *>(ur)[i];
-                    u[4 * i] = v.x; u[4 * i + 1] = v.y; u[4 * i + 2] = v.z; u[4 * i + 3] = v.w;
+                for (int i = 0; i < SCAN_EC / 4; ++i) {
+                    u[4 * i] = un[i].x; u[4 * i + 1] = un[i].y; u[4 * i + 2] = un[i].z; u[4 * i + 3] = un[i].w;
                 }
+                if (n + 1 < nch) load_u(n + 1);
             }
             // ---- h -> h^T (tf32) for (a); gamma_C h back into TMEM for (c)
             if (n > 0) {
                 mbar_wait(&c_done, (n - 1) & 1);
                 tc::fence_after();
-                tc::ld32(tH + lane_off, hv);
+                tc::ldn<SCAN_EC>(tH + lane_off, hv);
                 tc::wait_ld();
             }
 #pragma unroll
-            for (int j = 0; j < SCAN_CB; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(SCAN_CB, j, r)) = tf32r(hv[j]);
-            const float gC = expf(GC);
-#pragma unroll
-            for (int j = 0; j < SCAN_CB; ++j) hv[j] *= gC;
-            tc::st32(tH + lane_off, hv);
-            tc::wait_st();
+            for (int j = 0; j < SCAN_EC; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(SCAN_CB, c0 + j, r)) = tf32r(hv[j]);
             fence_proxy_async();                    // h^T visible to the tensor core
             tc::fence_before();
-            mbar_arrive(&h_ready);
+            mbar_arrive(&h_ready);                  // (a) may start
+#pragma unroll
+            for (int j = 0; j < SCAN_EC; ++j) hv[j] *= gC;
+            tc::stn<SCAN_EC>(tH + lane_off, hv);
+            tc::wait_st();
+            tc::fence_before();
+            mbar_arrive(&hs_ready);                 // gamma_C h in place for (c)
             // ---- P = [W; Q] h is in TMEM
             mbar_wait(&a_done, n & 1);
             tc::fence_after();
-            tc::ld32(tP + lane_off, pv);
+            tc::ldn<SCAN_EC>(tP + lane_off, pv);
             tc::wait_ld();
             if (q < 2) {
-                const float sc = expf(GC - Gt);
-                float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB) * PFG_C + t;
+                float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB + c0) * PFG_C + t;
 #pragma unroll
-                for (int j = 0; j < SCAN_CB; ++j) {
-                    const float d = u[j] - pv[j];
-                    dt[j * PFG_C] = tf32r(d);
-                    *reinterpret_cast<float *>(sBd + kmaj_off(SCAN_CB, j, t)) = tf32r(d * sc);
+                for (int j = 0; j < SCAN_EC; ++j) {
+                    pv[j] = u[j] - pv[j];           // D
+                    *reinterpret_cast<float *>(sBd + kmaj_off(SCAN_CB, c0 + j, t)) = tf32r(pv[j] * sc);
                 }
                 fence_proxy_async();                // D'^T visible to the tensor core
                 tc::fence_before();
                 mbar_arrive(&d_ready);
-            } else {
-                const float gt = expf(Gt);
-                float *qh = p.QH + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB;
+                // D^T for the output kernel, off the critical path
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
+                for (int j = 0; j < SCAN_EC; ++j) dt[j * PFG_C] = tf32r(pv[j]);
+            } else {
+                float *qh = p.QH + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB + c0;
+#pragma unroll
+                for (int i = 0; i < SCAN_EC / 4; ++i)
                     reinterpret_cast<float4 *>(qh)[i] =
-                        make_float4(pv[4 * i] * gt, pv[4 * i + 1] * gt, pv[4 * i + 2] * gt, pv[4 * i + 3] * gt);
+                        make_float4(pv[4 * i] * sc, pv[4 * i + 1] * sc, pv[4 * i + 2] * sc, pv[4 * i + 3] * sc);
             }
         }
         // final state back to HBM
         mbar_wait(&c_done, (nch - 1) & 1);
         tc::fence_after();
-        tc::ld32(tH + lane_off, hv);
+        tc::ldn<SCAN_EC>(tH + lane_off, hv);
         tc::wait_ld();
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < SCAN_EC / 4; ++i)
             reinterpret_cast<float4 *>(st)[i] = make_float4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
         tc::fence_before();
     }

@@ -161,5 +161,46 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16])
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void st16(uint32_t taddr, const float (&v)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+          "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
+          "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+          "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+          "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+          "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+// 8 consecutive fp32 columns of this thread's TMEM lane (load / store).
+__device__ __forceinline__ void ld8(uint32_t taddr, float (&v)[8])
+{
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                   "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void st8(uint32_t taddr, const float (&v)[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+                   "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
+                   "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+                 : "memory");
+}
+// Column-count dispatch for templated epilogues.
+template <int N> __device__ __forceinline__ void ldn(uint32_t taddr, float (&v)[N]);
+template <> __device__ __forceinline__ void ldn<8>(uint32_t taddr, float (&v)[8]) { ld8(taddr, v); }
+template <> __device__ __forceinline__ void ldn<16>(uint32_t taddr, float (&v)[16]) { ld16(taddr, v); }
+template <> __device__ __forceinline__ void ldn<32>(uint32_t taddr, float (&v)[32]) { ld32(taddr, v); }
+template <int N> __device__ __forceinline__ void stn(uint32_t taddr, const float (&v)[N]);
+template <> __device__ __forceinline__ void stn<8>(uint32_t taddr, const float (&v)[8]) { st8(taddr, v); }
+template <> __device__ __forceinline__ void stn<16>(uint32_t taddr, const float (&v)[16]) { st16(taddr, v); }
+template <> __device__ __forceinline__ void stn<32>(uint32_t taddr, const float (&v)[32]) { st32(taddr, v); }
 }  // namespace tc
 }  // namespace coli
