@@ -58,7 +58,7 @@ struct GdnLayer {
 
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
-            S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_COUNT };
+            S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_GHS, S_GXS, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -409,6 +409,20 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.M = (float *)scratch(S_GM, (size_t)nch * VH * 64 * 64 * 4);
     p.Dt = (float *)scratch(S_GDT, (size_t)nch * VH * 128 * 64 * 4);
     p.QH = (float *)scratch(S_GQH, (size_t)nch * VH * 64 * 128 * 4);
+    // Few heads per GPU leave the sequential chunk walk latency bound: split it
+    // into segments when the segment-map pass (4 CTAs per head and segment)
+    // still fits one wave.
+    int nseg = 1;
+    const int maxseg = 1 + G.num_sms / (4 * VH);
+    if (maxseg >= 3) nseg = std::min(maxseg, nch / 8);
+    if (nseg < 3) nseg = 1;
+    p.seglen = (nch + nseg - 1) / nseg;
+    p.nseg = (nch + p.seglen - 1) / p.seglen;
+    if (p.nseg > 1) {
+        p.Hs = (float *)scratch(S_GHS, (size_t)p.nseg * VH * 128 * 128 * 4);
+        p.XS = (float *)scratch(S_GXS, (size_t)(p.nseg - 1) * VH * 128 * 256 * 4);
+        if (!p.Hs || !p.XS) return 0;
+    }
     if (!p.Qh || !p.Kh || !p.KT || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
     p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
@@ -417,13 +431,15 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
         !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
         !make_f32_3d(&m.W, p.W, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64) ||
+        !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.Dt, p.Dt, 64, 128, nch * VH, 32, 128) ||
+        !make_f32_3d(&m.QH, p.QH, 64, 128, nch * VH, 32, 128) ||
         !make_f32_3d(&m.KT, p.KT, 64, 128, nch * KH, 32, 128))
         return 0;
     kt_mark(COLI_K_GDN_PREFILL);
     CK(launch_gdn_prefill(p, m, dtype, stream()));
     kt_mark(COLI_K_GDN_PREFILL);
-    g_launches += 5;
+    g_launches += 5 + (p.nseg > 1 ? 2 : 0);
     return 1;
 }
 

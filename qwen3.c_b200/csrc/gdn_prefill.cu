@@ -24,11 +24,15 @@
 //   gdn_pf_prep_kernel      per (chunk, V head), fully parallel: K K^T and
 //                           Q K^T on tf32 mma.sync, T by forward substitution
 //                           in fp32, then W, U and the decay-masked M.
-//   gdn_pf_scan_kernel      per (V head, 32-column block of the state): walks
-//                           the chunks in order with the state slice in TMEM,
-//                           products on tcgen05 (kind::tf32), producing D and
-//                           diag(gamma) Q S0 of every chunk. Operands arrive by
-//                           TMA (128B swizzle, no multicast) in a 2-stage ring.
+//   gdn_pf_scan_kernel      per (V head, 64-column block of the state, segment
+//                           of chunks): walks the chunks in order with the
+//                           state slice in TMEM, products on tcgen05
+//                           (kind::tf32), producing D and diag(gamma) Q S0 of
+//                           every chunk. Operands arrive by TMA (128B swizzle,
+//                           no multicast). With several segments a first
+//                           pass of the same kernel computes each segment's
+//                           affine state map and gdn_pf_combine_kernel chains
+//                           the segment start states.
 //   gdn_pf_out_kernel       per (chunk, V head), fully parallel: Y = QH + M D,
 //                           gated RMSNorm over the head's 128 columns, y.
 #include <cooperative_groups.h>
@@ -409,31 +413,47 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
 // ---------------------------------------------------------------- chunk scan
 // The sequential part, on the 5th-gen tensor core (tcgen05, kind::tf32). Per
-// (V head, 32-column block of the state) the chunks are walked in order:
-//   (a) P = [W; Q] h            M = 128 (64 W rows over 64 Q rows), N = 32, K = 128
+// (V head, 64-column block of the state) the chunks are walked in order:
+//   (a) P = [W; Q] h            M = 128 (64 W rows over 64 Q rows), N = 64, K = 128
 //   (e) D = U - P_W: D^T to scratch, D' = e^{G_C-G} D to shared memory;
-//       QH = diag(gamma) P_Q to scratch
-//   (c) h = gamma_C h + K^T D'  M = 128 (dk), N = 32, K = 64 tokens
-// The fp32 state h lives in TMEM (32 columns). The epilogue warps copy it, tf32
+//       QH = diag(gamma) P_Q to scratch (transposed, like D, so that the
+//       stores of a warp are contiguous)
+//   (c) h = gamma_C h + K^T D'  M = 128 (dk), N = 64, K = 64 tokens
+// The fp32 state h lives in TMEM (64 columns). The epilogue warps copy it, tf32
 // rounded, into shared memory as the B operand of (a) and scale it by gamma_C
 // in TMEM before (c) accumulates onto it. Every operand is a K-major
-// 128B-swizzled tile: W, Q and K^T (written transposed per chunk by the
-// prologue) arrive by TMA in a 2-stage ring, h^T and D'^T are written by the
-// epilogue threads. gdn_pf_out_kernel then turns D and QH into the outputs,
-// parallel over chunks.
-// Warp roles: 0 = TMA producer, 1 = TMEM owner and MMA issuer, then the
-// epilogue warps, 32 / SCAN_EC per TMEM lane quarter (warp % 4), SCAN_EC
-// columns each; quarters 0/1 hold the W rows (tokens 0-31 / 32-63), quarters
-// 2/3 the Q rows; for h, lane = dk row.
-constexpr int SCAN_CB = 32;                   // state columns per CTA
-constexpr int SCAN_EC = 8;                    // state columns per epilogue thread
-constexpr int SCAN_EPI = 4 * (SCAN_CB / SCAN_EC) * 32;  // epilogue threads
+// 128B-swizzled tile: W, Q (2-stage ring) and K^T (written transposed per
+// chunk by the prologue; one stage, reloaded as soon as (c) has read it)
+// arrive by TMA, as does U, h^T and D'^T are written by the epilogue threads.
+// gdn_pf_out_kernel then turns D and QH into the outputs, parallel over chunks.
+//
+// Segments. A tcgen05.mma costs about the same for N = 32 as for N = 64, and
+// the recurrence walks every chunk, so with few heads per GPU the scan is
+// latency bound. The chunks are then split into `nseg` segments walked in
+// parallel. The state after a segment is affine in the state before it,
+// S_end = Phi S_start + Psi, and Phi (U taken as 0, start I) and Psi (start 0)
+// obey the very recurrence above, so the TRANS pass runs this kernel on the
+// 128 x 256 matrix [Phi | Psi] of every segment but the last, without outputs;
+// gdn_pf_combine_kernel chains the segment start states in fp32, and the
+// replay pass then produces every segment's outputs from its start state.
+// Warp roles: 0 = TMA producer, 1 = TMEM owner and MMA issuer, then 16
+// epilogue warps, 4 per TMEM lane quarter (warp % 4) with 16 columns each;
+// quarters 0/1 hold the W rows (tokens 0-31 / 32-63), quarters 2/3 the Q
+// rows; for h, lane = dk row.
+// State columns per CTA: 32 for a single walk over many heads (more CTAs),
+// 64 for segmented walks (fewer CTAs per segment); 4 epilogue warps per TMEM
+// lane quarter with NC / 4 columns each either way.
+constexpr int SCAN_EPI = 512;                 // epilogue threads
 constexpr int SCAN_THREADS = 64 + SCAN_EPI;
 constexpr uint32_t SC_A_BYTES = 4 * 16384;    // [W; Q]: 4 k-atoms x (128 rows x 128 B)
 constexpr uint32_t SC_K_BYTES = 2 * 16384;    // K^T: 2 k-atoms x (128 dk rows x 128 B)
-constexpr uint32_t SC_BH_BYTES = 4 * 4096;    // h^T: 4 k-atoms x (32 rows x 128 B)
-constexpr uint32_t SC_BD_BYTES = 2 * 4096;    // D'^T: 2 k-atoms x (32 rows x 128 B)
-constexpr uint32_t SC_SMEM = 2 * SC_A_BYTES + 2 * SC_K_BYTES + SC_BH_BYTES + SC_BD_BYTES;
+template <int NC> struct ScanSmem {
+    static constexpr uint32_t BH = 4 * NC * 128;          // h^T: 4 k-atoms x (NC rows x 128 B)
+    static constexpr uint32_t BD = 2 * NC * 128;          // D'^T: 2 k-atoms x (NC rows x 128 B)
+    static constexpr uint32_t U = (NC / 32) * PFG_C * 128; // U: 32-column boxes x 64 tokens
+    static constexpr uint32_t TOTAL = 2 * SC_A_BYTES + SC_K_BYTES + BH + BD + U;
+    static_assert(TOTAL + 1024 <= 232448, "scan shared memory");
+};
 
 // Byte offset of element (row r, k) in a K-major 128B-swizzled fp32 tile with
 // `rows` rows per k-atom (32 fp32 of k per 128 B row, 8-row groups 1 KiB apart).
@@ -442,106 +462,128 @@ __device__ __forceinline__ uint32_t kmaj_off(int rows, int r, int k)
     return (uint32_t)((k >> 5) * rows * 128 + r * 128 + ((((k & 31) >> 2) ^ (r & 7)) << 4) + (k & 3) * 4);
 }
 
+// Grid: blockIdx.x = (seg * VH + h) * NB + blk, NB = 128 / NC state blocks
+// (replay) or 256 / NC blocks of [Phi | Psi] (TRANS, segments 0 .. nseg-2).
+template <bool TRANS, int NC>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
 gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQ,
-                   const __grid_constant__ CUtensorMap tmKT, GdnPrefillArgs p)
+                   const __grid_constant__ CUtensorMap tmKT, const __grid_constant__ CUtensorMap tmU,
+                   GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sA = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sK = sA + 2 * SC_A_BYTES;
-    uint8_t *sBh = sK + 2 * SC_K_BYTES;
-    uint8_t *sBd = sBh + SC_BH_BYTES;
-    __shared__ __align__(8) uint64_t a_full[2], a_empty[2], k_full[2], k_empty[2];
+    uint8_t *sBh = sK + SC_K_BYTES;
+    uint8_t *sBd = sBh + ScanSmem<NC>::BH;
+    uint8_t *sU = sBd + ScanSmem<NC>::BD;
+    __shared__ __align__(8) uint64_t a_full[2], a_empty[2], k_full, k_empty, u_full, u_empty;
     __shared__ __align__(8) uint64_t h_ready, hs_ready, a_done, d_ready, c_done;
     __shared__ uint32_t tmem_base;
 
-    const int cblk = blockIdx.x & 3, h = blockIdx.x >> 2, kh = h >> 1;
+    constexpr int EC = NC / 4, NB = (TRANS ? 256 : 128) / NC;
+    const int VH = p.VH;
+    const int blk = blockIdx.x % NB, h = (blockIdx.x / NB) % VH, seg = blockIdx.x / (NB * VH);
+    const int kh = h >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int S = p.S, nch = (S + PFG_C - 1) / PFG_C, VH = p.VH;
+    const int S = p.S, nch = (S + PFG_C - 1) / PFG_C;
+    const int n0 = seg * p.seglen, n1 = min(nch, n0 + p.seglen), cnt = n1 - n0;
+    // TRANS: the first half of the blocks is Phi (U taken as 0, no Q), the second Psi
+    const bool phi = TRANS && blk < NB / 2;
+    const int col = (TRANS ? blk % (NB / 2) : blk) * NC;  // first state column (of Phi / Psi in TRANS)
+    const uint32_t a_bytes = TRANS ? SC_A_BYTES / 2 : SC_A_BYTES;
 
     if (tid == 0) {
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1);
-            mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
-        }
+        for (int s = 0; s < 2; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
+        mbar_init(&k_full, 1); mbar_init(&k_empty, 1);
+        mbar_init(&u_full, 1); mbar_init(&u_empty, SCAN_EPI / 64);  // one arrival per W-row warp
         mbar_init(&h_ready, SCAN_EPI); mbar_init(&hs_ready, SCAN_EPI); mbar_init(&a_done, 1);
         mbar_init(&d_ready, SCAN_EPI / 2); mbar_init(&c_done, 1);
         fence_mbar_init();
     }
-    if (warp == 1) tc::alloc(&tmem_base, 64);
+    if (warp == 1) tc::alloc(&tmem_base, 2 * NC);
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
-    const uint32_t tP = tmem_base, tH = tmem_base + 32;
+    const uint32_t tP = tmem_base, tH = tmem_base + NC;
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int n = 0; n < nch; ++n) {
-                const int s = n & 1;
-                if (n >= 2) mbar_wait(&a_empty[s], ((n >> 1) + 1) & 1);
+            for (int i = 0; i < cnt; ++i) {
+                const int n = n0 + i, s = i & 1;
+                if (i >= 2) mbar_wait(&a_empty[s], ((i >> 1) + 1) & 1);
                 uint8_t *a = sA + s * SC_A_BYTES;
-                mbar_expect_tx(&a_full[s], SC_A_BYTES);
+                mbar_expect_tx(&a_full[s], a_bytes);
                 for (int c = 0; c < 4; ++c) {
                     tma_load_3d(a + c * 16384, &tmW, 32 * c, 0, n * VH + h, &a_full[s]);
-                    tma_load_3d(a + c * 16384 + 8192, &tmQ, 32 * c, n * PFG_C, kh, &a_full[s]);
+                    if (!TRANS) tma_load_3d(a + c * 16384 + 8192, &tmQ, 32 * c, n * PFG_C, kh, &a_full[s]);
                 }
-                if (n >= 2) mbar_wait(&k_empty[s], ((n >> 1) + 1) & 1);
-                uint8_t *k = sK + s * SC_K_BYTES;
-                mbar_expect_tx(&k_full[s], SC_K_BYTES);
-                for (int c = 0; c < 2; ++c) tma_load_3d(k + c * 16384, &tmKT, 32 * c, 0, kh * nch + n, &k_full[s]);
+                if (i >= 1) mbar_wait(&k_empty, (i + 1) & 1);
+                mbar_expect_tx(&k_full, SC_K_BYTES);
+                for (int c = 0; c < 2; ++c) tma_load_3d(sK + c * 16384, &tmKT, 32 * c, 0, kh * nch + n, &k_full);
+                if (!phi) {
+                    if (i >= 1) mbar_wait(&u_empty, (i + 1) & 1);
+                    mbar_expect_tx(&u_full, ScanSmem<NC>::U);
+                    for (int c = 0; c < NC / 32; ++c)
+                        tma_load_3d(sU + c * PFG_C * 128, &tmU, col + 32 * c, 0, n * VH + h, &u_full);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(128, SCAN_CB);
+            constexpr uint32_t idesc = tc::idesc_tf32(128, NC);
             const uint32_t aA = smem_u32(sA), aK = smem_u32(sK), aBh = smem_u32(sBh), aBd = smem_u32(sBd);
-            for (int n = 0; n < nch; ++n) {
-                const int s = n & 1;
-                const uint32_t ph = (n >> 1) & 1;
-                mbar_wait(&a_full[s], ph);
-                mbar_wait(&h_ready, n & 1);
+            for (int i = 0; i < cnt; ++i) {
+                const int s = i & 1;
+                mbar_wait(&a_full[s], (i >> 1) & 1);
+                mbar_wait(&h_ready, i & 1);
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < PFG_D / 8; ++ks)
                     tc::mma_tf32(tP, tc::desc_k_sw128(aA + s * SC_A_BYTES + (ks >> 2) * 16384 + (ks & 3) * 32),
-                                 tc::desc_k_sw128(aBh + (ks >> 2) * 4096 + (ks & 3) * 32), idesc, ks > 0);
+                                 tc::desc_k_sw128(aBh + (ks >> 2) * (NC * 128) + (ks & 3) * 32), idesc, ks > 0);
                 tc::commit(&a_done);
                 tc::commit(&a_empty[s]);
-                mbar_wait(&k_full[s], ph);
-                mbar_wait(&d_ready, n & 1);
-                mbar_wait(&hs_ready, n & 1);
+                mbar_wait(&k_full, i & 1);
+                mbar_wait(&d_ready, i & 1);
+                mbar_wait(&hs_ready, i & 1);
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < PFG_C / 8; ++ks)
-                    tc::mma_tf32(tH, tc::desc_k_sw128(aK + s * SC_K_BYTES + (ks >> 2) * 16384 + (ks & 3) * 32),
-                                 tc::desc_k_sw128(aBd + (ks >> 2) * 4096 + (ks & 3) * 32), idesc, 1);
+                    tc::mma_tf32(tH, tc::desc_k_sw128(aK + (ks >> 2) * 16384 + (ks & 3) * 32),
+                                 tc::desc_k_sw128(aBd + (ks >> 2) * (NC * 128) + (ks & 3) * 32), idesc, 1);
                 tc::commit(&c_done);
-                tc::commit(&k_empty[s]);
+                tc::commit(&k_empty);
             }
         }
     } else {
-        const int q = warp & 3, half = q & 1, c0 = ((warp - 2) >> 2) * SCAN_EC;  // lane quarter, first column
+        const int q = warp & 3, half = q & 1, c0 = ((warp - 2) >> 2) * EC;  // lane quarter, first column
         const uint32_t lane_off = ((uint32_t)(q * 32) << 16) + c0;
-        const int r = q * 32 + lane;               // dk row in (c) / TMEM lane
+        const int r = q * 32 + lane;               // dk row of h / TMEM lane
         const int t = half * 32 + lane;            // token within the chunk in (e)
+        const int cl = col + c0;                   // this thread's first state column
         const float *gl = p.GL + (size_t)h * S;
-        float gl_lo = lane < S ? gl[lane] : 0.f, gl_hi = lane + 32 < S ? gl[lane + 32] : 0.f;
-        float hv[SCAN_EC], u[SCAN_EC], pv[SCAN_EC];
-        float4 un[SCAN_EC / 4];
-        auto load_u = [&](int n) {
-            const float4 *ur = reinterpret_cast<const float4 *>(
-                p.U + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB + c0);
-#pragma unroll
-            for (int i = 0; i < SCAN_EC / 4; ++i) un[i] = ur[i];
-        };
-        if (q < 2) load_u(0);
-        float *st = p.state + ((size_t)h * PFG_D + r) * PFG_D + cblk * SCAN_CB + c0;
-#pragma unroll
-        for (int i = 0; i < SCAN_EC / 4; ++i) {
-            const float4 v = reinterpret_cast<const float4 *>(st)[i];
-            hv[4 * i] = v.x; hv[4 * i + 1] = v.y; hv[4 * i + 2] = v.z; hv[4 * i + 3] = v.w;
+        float gl_lo, gl_hi;
+        {
+            const int t0 = n0 * PFG_C + lane;
+            gl_lo = t0 < S ? gl[t0] : 0.f;
+            gl_hi = t0 + 32 < S ? gl[t0 + 32] : 0.f;
         }
-        for (int n = 0; n < nch; ++n) {
+        float hv[EC], pv[EC];
+        // start state
+        if (TRANS) {
+#pragma unroll
+            for (int j = 0; j < EC; ++j) hv[j] = (phi && r == cl + j) ? 1.f : 0.f;
+        } else {
+            const float *src = (p.nseg > 1 ? p.Hs + ((size_t)seg * VH + h) * PFG_D * PFG_D
+                                           : p.state + (size_t)h * PFG_D * PFG_D) + (size_t)r * PFG_D + cl;
+#pragma unroll
+            for (int i = 0; i < EC / 4; ++i) {
+                const float4 v = reinterpret_cast<const float4 *>(src)[i];
+                hv[4 * i] = v.x; hv[4 * i + 1] = v.y; hv[4 * i + 2] = v.z; hv[4 * i + 3] = v.w;
+            }
+        }
+        for (int i = 0; i < cnt; ++i) {
+            const int n = n0 + i;
             // inclusive cumulative log decay of this chunk: G_t for this
             // thread's token, G_C for the whole chunk
             float slo = gl_lo, shi = gl_hi;
@@ -556,78 +598,169 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             // decay factors of this chunk: gamma_C for h, e^{G_C-G_t} for D', gamma_t for QH
             const float gC = expf(GC), sc = q < 2 ? expf(GC - Gt) : expf(Gt);
             asm volatile("" ::"f"(gC), "f"(sc));   // keep them here, off the critical path
-            if (n + 1 < nch) {
+            if (i + 1 < cnt) {
                 const int t0 = (n + 1) * PFG_C + lane;
                 gl_lo = t0 < S ? gl[t0] : 0.f;
                 gl_hi = t0 + 32 < S ? gl[t0 + 32] : 0.f;
             }
-            if (q < 2) {   // this chunk's U; the next chunk's loads are issued a chunk ahead
-#pragma unroll
-                for (int i = 0; i < SCAN_EC / 4; ++i) {
-                    u[4 * i] = un[i].x; u[4 * i + 1] = un[i].y; u[4 * i + 2] = un[i].z; u[4 * i + 3] = un[i].w;
-                }
-                if (n + 1 < nch) load_u(n + 1);
-            }
             // ---- h -> h^T (tf32) for (a); gamma_C h back into TMEM for (c)
-            if (n > 0) {
-                mbar_wait(&c_done, (n - 1) & 1);
+            if (i > 0) {
+                mbar_wait(&c_done, (i - 1) & 1);
                 tc::fence_after();
-                tc::ldn<SCAN_EC>(tH + lane_off, hv);
+                tc::ldn<EC>(tH + lane_off, hv);
                 tc::wait_ld();
             }
 #pragma unroll
-            for (int j = 0; j < SCAN_EC; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(SCAN_CB, c0 + j, r)) = tf32r(hv[j]);
+            for (int j = 0; j < EC; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(NC, c0 + j, r)) = tf32r(hv[j]);
             fence_proxy_async();                    // h^T visible to the tensor core
             tc::fence_before();
             mbar_arrive(&h_ready);                  // (a) may start
 #pragma unroll
-            for (int j = 0; j < SCAN_EC; ++j) hv[j] *= gC;
-            tc::stn<SCAN_EC>(tH + lane_off, hv);
+            for (int j = 0; j < EC; ++j) hv[j] *= gC;
+            tc::stn<EC>(tH + lane_off, hv);
             tc::wait_st();
             tc::fence_before();
             mbar_arrive(&hs_ready);                 // gamma_C h in place for (c)
             // ---- P = [W; Q] h is in TMEM
-            mbar_wait(&a_done, n & 1);
+            mbar_wait(&a_done, i & 1);
             tc::fence_after();
-            tc::ldn<SCAN_EC>(tP + lane_off, pv);
-            tc::wait_ld();
+            if (q < 2 || !TRANS) {
+                tc::ldn<EC>(tP + lane_off, pv);
+                tc::wait_ld();
+            }
             if (q < 2) {
-                float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cblk * SCAN_CB + c0) * PFG_C + t;
+                if (!phi) {                         // D = U - W h (U of this chunk by TMA)
+                    mbar_wait(&u_full, i & 1);
+                    const float *ur = reinterpret_cast<const float *>(sU + (c0 >> 5) * PFG_C * 128 + t * 128);
 #pragma unroll
-                for (int j = 0; j < SCAN_EC; ++j) {
-                    pv[j] = u[j] - pv[j];           // D
-                    *reinterpret_cast<float *>(sBd + kmaj_off(SCAN_CB, c0 + j, t)) = tf32r(pv[j] * sc);
+                    for (int k = 0; k < EC / 4; ++k) {
+                        const float4 v = *reinterpret_cast<const float4 *>(ur + (((((c0 & 31) >> 2) + k) ^ (t & 7)) << 2));
+                        pv[4 * k] = v.x - pv[4 * k]; pv[4 * k + 1] = v.y - pv[4 * k + 1];
+                        pv[4 * k + 2] = v.z - pv[4 * k + 2]; pv[4 * k + 3] = v.w - pv[4 * k + 3];
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&u_empty);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < EC; ++j) pv[j] = -pv[j];
                 }
+#pragma unroll
+                for (int j = 0; j < EC; ++j)
+                    *reinterpret_cast<float *>(sBd + kmaj_off(NC, c0 + j, t)) = tf32r(pv[j] * sc);
                 fence_proxy_async();                // D'^T visible to the tensor core
                 tc::fence_before();
                 mbar_arrive(&d_ready);
-                // D^T for the output kernel, off the critical path
+                if (!TRANS) {  // D^T for the output kernel, off the critical path
+                    float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cl) * PFG_C + t;
 #pragma unroll
-                for (int j = 0; j < SCAN_EC; ++j) dt[j * PFG_C] = tf32r(pv[j]);
-            } else {
-                float *qh = p.QH + (((size_t)n * VH + h) * PFG_C + t) * PFG_D + cblk * SCAN_CB + c0;
+                    for (int j = 0; j < EC; ++j) dt[j * PFG_C] = tf32r(pv[j]);
+                }
+            } else if (!TRANS) {                    // QH^T, same layout as D^T
+                float *qh = p.QH + (((size_t)n * VH + h) * PFG_D + cl) * PFG_C + t;
 #pragma unroll
-                for (int i = 0; i < SCAN_EC / 4; ++i)
-                    reinterpret_cast<float4 *>(qh)[i] =
-                        make_float4(pv[4 * i] * sc, pv[4 * i + 1] * sc, pv[4 * i + 2] * sc, pv[4 * i + 3] * sc);
+                for (int j = 0; j < EC; ++j) qh[j * PFG_C] = pv[j] * sc;
             }
         }
-        // final state back to HBM
-        mbar_wait(&c_done, (nch - 1) & 1);
-        tc::fence_after();
-        tc::ldn<SCAN_EC>(tH + lane_off, hv);
-        tc::wait_ld();
+        // the state after this segment: the request's state (last segment),
+        // [Phi | Psi] of the segment (TRANS)
+        if (cnt > 0) {
+            mbar_wait(&c_done, (cnt - 1) & 1);
+            tc::fence_after();
+            tc::ldn<EC>(tH + lane_off, hv);
+            tc::wait_ld();
+        }
+        float *dst = nullptr;
+        if (TRANS) dst = p.XS + (((size_t)seg * VH + h) * PFG_D + r) * (2 * PFG_D) + blk * NC + c0;
+        else if (seg == p.nseg - 1) dst = p.state + ((size_t)h * PFG_D + r) * PFG_D + cl;
+        if (dst) {
 #pragma unroll
-        for (int i = 0; i < SCAN_EC / 4; ++i)
-            reinterpret_cast<float4 *>(st)[i] = make_float4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+            for (int k = 0; k < EC / 4; ++k)
+                reinterpret_cast<float4 *>(dst)[k] = make_float4(hv[4 * k], hv[4 * k + 1], hv[4 * k + 2], hv[4 * k + 3]);
+        }
         tc::fence_before();
     }
     __syncthreads();
     if (warp == 1) {
         tc::fence_after();
-        tc::dealloc(tmem_base, 64);
+        tc::dealloc(tmem_base, 2 * NC);
     }
 }
+
+// Segment start states, in fp32: Hs[0] = S0, Hs[s+1] = Phi_s Hs[s] + Psi_s.
+// Columns are independent (Phi acts from the left), so a CTA owns 16 state
+// columns of one head: grid (VH, 8), 256 threads, thread = 2 rows x 4
+// columns. Phi_{s+1} is copied into shared memory (cp.async) while step s
+// computes.
+constexpr int CMB_LD = 132;   // Phi row stride in shared memory (floats)
+constexpr int CMB_NC = 16;    // state columns per CTA
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__global__ void __launch_bounds__(256)
+gdn_pf_combine_kernel(GdnPrefillArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    float *sPhi = reinterpret_cast<float *>(smem_raw);          // [2][128][CMB_LD]
+    float *sH = sPhi + 2 * PFG_D * CMB_LD;                      // [128][CMB_NC]
+    const int h = blockIdx.x, cb = blockIdx.y * CMB_NC, VH = p.VH, tid = threadIdx.x;
+    const int r0 = (tid >> 2) * 2, c0 = (tid & 3) * 4;          // 2 rows x 4 columns
+    auto fetch_phi = [&](int s) {
+        const float *X = p.XS + ((size_t)s * VH + h) * PFG_D * (2 * PFG_D);
+        float *dst = sPhi + (s & 1) * PFG_D * CMB_LD;
+        for (int i = tid; i < PFG_D * PFG_D / 4; i += 256) {
+            const int row = i >> 5, k4 = (i & 31) * 4;
+            cp_async16(dst + row * CMB_LD + k4, X + (size_t)row * (2 * PFG_D) + k4);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch_phi(0);
+    for (int i = 0; i < 2; ++i) {
+        const float4 v = *reinterpret_cast<const float4 *>(p.state + ((size_t)h * PFG_D + r0 + i) * PFG_D + cb + c0);
+        *reinterpret_cast<float4 *>(sH + (r0 + i) * CMB_NC + c0) = v;
+        *reinterpret_cast<float4 *>(p.Hs + ((size_t)h * PFG_D + r0 + i) * PFG_D + cb + c0) = v;
+    }
+    for (int s = 0; s + 1 < p.nseg; ++s) {
+        if (s + 2 < p.nseg) {
+            fetch_phi(s + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();                                        // Phi_s and H_s in place
+        const float *X = p.XS + ((size_t)s * VH + h) * PFG_D * (2 * PFG_D);
+        const float *ph = sPhi + (s & 1) * PFG_D * CMB_LD;
+        float acc[2][4];
+        for (int i = 0; i < 2; ++i) {
+            const float4 v = *reinterpret_cast<const float4 *>(X + (size_t)(r0 + i) * (2 * PFG_D) + PFG_D + cb + c0);
+            acc[i][0] = v.x; acc[i][1] = v.y; acc[i][2] = v.z; acc[i][3] = v.w;   // Psi
+        }
+#pragma unroll 4
+        for (int k = 0; k < PFG_D; k += 4) {
+            float4 hk[4], pr[2];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) hk[e] = *reinterpret_cast<const float4 *>(sH + (k + e) * CMB_NC + c0);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) pr[i] = *reinterpret_cast<const float4 *>(ph + (r0 + i) * CMB_LD + k);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float a[4] = {pr[i].x, pr[i].y, pr[i].z, pr[i].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    acc[i][0] += a[e] * hk[e].x; acc[i][1] += a[e] * hk[e].y;
+                    acc[i][2] += a[e] * hk[e].z; acc[i][3] += a[e] * hk[e].w;
+                }
+            }
+        }
+        __syncthreads();                                        // every read of H_s done
+        for (int i = 0; i < 2; ++i) {
+            const float4 v = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4 *>(sH + (r0 + i) * CMB_NC + c0) = v;
+            *reinterpret_cast<float4 *>(p.Hs + (((size_t)(s + 1) * VH + h) * PFG_D + r0 + i) * PFG_D + cb + c0) = v;
+        }
+    }
+}
+size_t gdn_combine_smem() { return (size_t)(2 * PFG_D * CMB_LD + PFG_D * CMB_NC) * 4; }
 
 // ---------------------------------------------------------------- outputs
 // Parallel over (chunk, V head): Y = QH + M D, then the gated RMSNorm over the
@@ -636,12 +769,13 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(128)
 gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmDt,
-                  GdnPrefillArgs p)
+                  const __grid_constant__ CUtensorMap tmQH, GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *sM = base;                    // [64 x 64] swizzled (2 boxes of 32 columns)
     float *sDT = sM + PFG_C * PFG_C;     // D^T [128 dv x 64 tokens] swizzled (2 boxes of 32 tokens)
+    float *sQT = sDT + PFG_D * PFG_C;    // QH^T, same layout
     __shared__ __align__(8) uint64_t bar;
     const int n = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
@@ -650,22 +784,21 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
-        mbar_expect_tx(&bar, (PFG_C * PFG_C + PFG_D * PFG_C) * 4);
+        mbar_expect_tx(&bar, (PFG_C * PFG_C + 2 * PFG_D * PFG_C) * 4);
         for (int c = 0; c < 2; ++c) tma_load_3d(sM + c * PFG_C * 32, &tmM, 32 * c, 0, n * VH + h, &bar);
         for (int c = 0; c < 2; ++c) tma_load_3d(sDT + c * PFG_D * 32, &tmDt, 32 * c, 0, n * VH + h, &bar);
+        for (int c = 0; c < 2; ++c) tma_load_3d(sQT + c * PFG_D * 32, &tmQH, 32 * c, 0, n * VH + h, &bar);
     }
     const int r0 = warp * 16, ta = n * PFG_C + r0 + g, tb = ta + 8;
     float y[16][4];
-    const float *qh = p.QH + ((size_t)n * VH + h) * PFG_C * PFG_D;
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-        const int col = nt * 8 + 2 * tq;
-        const float2 u0 = *reinterpret_cast<const float2 *>(qh + (size_t)(r0 + g) * PFG_D + col);
-        const float2 u1 = *reinterpret_cast<const float2 *>(qh + (size_t)(r0 + g + 8) * PFG_D + col);
-        y[nt][0] = u0.x; y[nt][1] = u0.y; y[nt][2] = u1.x; y[nt][3] = u1.y;
-    }
     __syncthreads();
     mbar_wait(&bar, 0);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {   // Y starts from QH (element (token, dv) of QH^T)
+        const int col = nt * 8 + 2 * tq;
+        y[nt][0] = sw_ld(sQT, PFG_D, col, r0 + g);     y[nt][1] = sw_ld(sQT, PFG_D, col + 1, r0 + g);
+        y[nt][2] = sw_ld(sQT, PFG_D, col, r0 + g + 8); y[nt][3] = sw_ld(sQT, PFG_D, col + 1, r0 + g + 8);
+    }
     const uint32_t aM = smem_u32(sM), aD = smem_u32(sDT);
 #pragma unroll
     for (int ks = 0; ks < PFG_C / 8; ++ks) {
@@ -709,8 +842,8 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
 
 // ---------------------------------------------------------------- launch
 size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD + 3 * 256) * 4 + 1024; }
-size_t gdn_scan_smem() { return (size_t)SC_SMEM + 1024; }
-size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + PFG_D * PFG_C) * 4 + 1024; }
+template <int NC> size_t gdn_scan_smem() { return (size_t)ScanSmem<NC>::TOTAL + 1024; }
+size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + 2 * PFG_D * PFG_C) * 4 + 1024; }
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st)
@@ -729,14 +862,28 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     if (e != cudaSuccess) return e;
     gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), 128, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gdn_pf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_scan_smem());
+    auto scan = [&](auto kern, size_t smem, int grid) -> cudaError_t {
+        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e2 != cudaSuccess) return e2;
+        kern<<<grid, SCAN_THREADS, smem, st>>>(m.W, m.Q, m.KT, m.U, a);
+        return cudaGetLastError();
+    };
+    if (a.nseg > 1) {
+        if ((e = scan(gdn_pf_scan_kernel<true, 64>, gdn_scan_smem<64>(), (a.nseg - 1) * a.VH * 4)) != cudaSuccess)
+            return e;
+        e = cudaFuncSetAttribute(gdn_pf_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_combine_smem());
+        if (e != cudaSuccess) return e;
+        gdn_pf_combine_kernel<<<dim3(a.VH, PFG_D / CMB_NC), 256, gdn_combine_smem(), st>>>(a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        e = scan(gdn_pf_scan_kernel<false, 64>, gdn_scan_smem<64>(), a.nseg * a.VH * 2);
+    } else {
+        e = scan(gdn_pf_scan_kernel<false, 32>, gdn_scan_smem<32>(), a.VH * 4);
+    }
     if (e != cudaSuccess) return e;
-    gdn_pf_scan_kernel<<<a.VH * 4, SCAN_THREADS, gdn_scan_smem(), st>>>(m.W, m.Q, m.KT, a);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     auto out = [&](auto kern) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_out_smem());
         if (e2 != cudaSuccess) return e2;
-        kern<<<dim3(nchunks, a.VH), 128, gdn_out_smem(), st>>>(m.M, m.Dt, a);
+        kern<<<dim3(nchunks, a.VH), 128, gdn_out_smem(), st>>>(m.M, m.Dt, m.QH, a);
         return cudaGetLastError();
     };
     return bf16 ? out(gdn_pf_out_kernel<__nv_bfloat16, __nv_bfloat16>) : out(gdn_pf_out_kernel<float, float>);

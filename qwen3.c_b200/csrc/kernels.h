@@ -91,7 +91,10 @@ struct GdnPrefillArgs {
     float *W, *U;                         // scratch [nchunks][VH][64][128]
     float *M;                             // scratch [nchunks][VH][64][64]
     float *Dt;                            // scratch [nchunks][VH][128][64] (D transposed)
-    float *QH;                            // scratch [nchunks][VH][64][128] (diag(gamma) Q S0)
+    float *QH;                            // scratch [nchunks][VH][128][64] (diag(gamma) Q S0, transposed)
+    float *Hs;                            // scratch [nseg][VH][128][128] segment start states
+    float *XS;                            // scratch [nseg-1][VH][128][256] segment maps [Phi | Psi]
+    int nseg, seglen;                     // chunk segments walked in parallel (1 = one walk)
     int S, KH, VH;
     float eps;
     // head-sharded prefill: this call owns K heads [kh0, kh0+KH) (V heads
@@ -100,7 +103,7 @@ struct GdnPrefillArgs {
     int kh0, KHin, VHin;
 };
 struct GdnPrefillMaps {
-    CUtensorMap Q, K, V, W, M, Dt, KT;
+    CUtensorMap Q, K, V, W, U, M, Dt, QH, KT;
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st);

@@ -149,3 +149,41 @@ def test_bf16_device_path(be, orc):
         want = orc.gdn_seq(ins[r]["qkv"], ins[r]["z"], ins[r]["a"], ins[r]["b"], prm["conv_w"],
                            prm["A_log"], prm["dt_bias"], prm["gnorm"], r0, s0, KH=KH_G, KD=KD)
         assert_close(y[r].float().cpu().numpy(), want[0], what=f"bf16 req {r}")
+
+
+@pytest.mark.parametrize("kh0,nkh", [(0, 2), (6, 2), (8, 4), (4, 8)])
+def test_head_sharded_segmented_prefill_vs_oracle(be, orc, kh0, nkh):
+    """A head shard of 2-8 K heads at S = 4096 walks its 64 chunks as several
+    segments in parallel (segment maps, fp32 chaining, replay); outputs and
+    final state of the owned heads against the token-by-token oracle from a
+    nonzero carried state."""
+    import ctypes
+    import torch
+    S = 4096
+    cfg = "gdn_segmented"
+    prm = gdn_params(cfg)
+    state, ring = gdn_state0(cfg)
+    ins = gdn_inputs(cfg, S)
+    s_ref, r_ref = state.copy(), ring.copy()
+    y_ref = orc.gdn_seq(ins["qkv"], ins["z"], ins["a"], ins["b"], prm["conv_w"], prm["A_log"],
+                        prm["dt_bias"], prm["gnorm"], r_ref, s_ref, KH=KH_G, KD=KD)
+    layer, nv, v0 = 30, 2 * nkh, 2 * kh0
+    lib = be.lib
+    fp = ctypes.POINTER(ctypes.c_float)
+    assert lib.coli_cuda_gdn_state_ensure(layer, 1, nv, KD, VD) == 1
+    assert lib.coli_cuda_gdn_conv_ensure(layer, 1, CONVK, CD) == 1
+    cw = np.ascontiguousarray(prm["conv_w"], np.float32)
+    assert lib.coli_cuda_gdn_conv_weight(layer, cw.ctypes.data_as(fp), CONVK, CD) == 1
+    arrs = [np.ascontiguousarray(prm[n], np.float32) for n in ("A_log", "dt_bias", "gnorm")]
+    assert lib.coli_cuda_gdn_params(layer, *[x.ctypes.data_as(fp) for x in arrs], VH_G, VD) == 1
+    be.gdn_state_set(layer, 0, np.ascontiguousarray(state[v0:v0 + nv]))
+    be.gdn_conv_set(layer, 0, ring)
+    dev = {k: torch.from_numpy(np.ascontiguousarray(ins[k], np.float32)).cuda() for k in ("qkv", "z", "a", "b")}
+    y = torch.zeros(S, nv * VD, dtype=torch.float32, device="cuda")
+    be.gdn_prefill_heads_dev(layer, 0, S, dev["qkv"].data_ptr(), dev["z"].data_ptr(), dev["a"].data_ptr(),
+                             dev["b"].data_ptr(), y.data_ptr(), kh0, nkh, dtype=0)
+    be.sync()
+    assert_close(y.cpu().numpy(), y_ref.reshape(S, VH_G * VD)[:, v0 * VD:(v0 + nv) * VD],
+                 what=f"segmented prefill heads {kh0}+{nkh}")
+    err = rel_l2(be.gdn_state_get(layer, 0, VH=nv), s_ref[v0:v0 + nv])
+    assert err <= 1e-2, err
