@@ -820,22 +820,48 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
     sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
     sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
     const float ra_ = 1.f / sqrtf(sa / VD + p.eps), rb_ = 1.f / sqrtf(sb / VD + p.eps);
-    const TI *z = static_cast<const TI *>(p.z);
-    TO *out = static_cast<TO *>(p.y);
+    // normalised rows (times gnorm) to shared memory, then the gate and the
+    // store row by row so that z loads and y stores are 16-byte vectors
+    __syncthreads();                     // every warp is done with sDT / sQT
+    constexpr int YLD = PFG_D + 4;
+    float *sY = sDT;                     // [64][YLD] over the D^T / QH^T tiles
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
+        const int col = nt * 8 + 2 * tq;
+        const float g0 = p.gnorm[col], g1 = p.gnorm[col + 1];
+        *reinterpret_cast<float2 *>(sY + (r0 + g) * YLD + col) = make_float2(y[nt][0] * ra_ * g0, y[nt][1] * ra_ * g1);
+        *reinterpret_cast<float2 *>(sY + (r0 + g + 8) * YLD + col) = make_float2(y[nt][2] * rb_ * g0, y[nt][3] * rb_ * g1);
+    }
+    __syncthreads();
+    const TI *z = static_cast<const TI *>(p.z);
+    TO *out = static_cast<TO *>(p.y);
+    for (int e = tid; e < PFG_C * (PFG_D / 8); e += 128) {
+        const int row = e >> 4, c8 = (e & 15) * 8, tok = n * PFG_C + row;
+        if (tok >= S) continue;
+        const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + c8;
+        TO *orow = out + (size_t)tok * VH * VD + h * VD + c8;
+        float zv[8], v[8];
+        if constexpr (sizeof(TI) == 2) {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(zr);
+            const __nv_bfloat16 *zb = reinterpret_cast<const __nv_bfloat16 *>(&raw);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int col = nt * 8 + 2 * tq + e;
-            const float gw = p.gnorm[col];
-            if (ta < S) {
-                const float zv = to_f32(z[(size_t)ta * VHin * VD + vg * VD + col]);
-                out[(size_t)ta * VH * VD + h * VD + col] = from_f32<TO>(y[nt][e] * ra_ * gw * siluf_(zv));
-            }
-            if (tb < S) {
-                const float zv = to_f32(z[(size_t)tb * VHin * VD + vg * VD + col]);
-                out[(size_t)tb * VH * VD + h * VD + col] = from_f32<TO>(y[nt][2 + e] * rb_ * gw * siluf_(zv));
-            }
+            for (int j = 0; j < 8; ++j) zv[j] = to_f32(zb[j]);
+        } else {
+            const float4 z0 = *reinterpret_cast<const float4 *>(zr), z1 = *reinterpret_cast<const float4 *>(zr + 4);
+            zv[0] = z0.x; zv[1] = z0.y; zv[2] = z0.z; zv[3] = z0.w; zv[4] = z1.x; zv[5] = z1.y; zv[6] = z1.z; zv[7] = z1.w;
+        }
+        const float4 y0 = *reinterpret_cast<const float4 *>(sY + row * YLD + c8);
+        const float4 y1 = *reinterpret_cast<const float4 *>(sY + row * YLD + c8 + 4);
+        v[0] = y0.x; v[1] = y0.y; v[2] = y0.z; v[3] = y0.w; v[4] = y1.x; v[5] = y1.y; v[6] = y1.z; v[7] = y1.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= siluf_(zv[j]);
+        if constexpr (sizeof(TO) == 2) {
+            uint4 o;
+            o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]); o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
+            *reinterpret_cast<uint4 *>(orow) = o;
+        } else {
+            *reinterpret_cast<float4 *>(orow) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4 *>(orow + 4) = make_float4(v[4], v[5], v[6], v[7]);
         }
     }
 }
