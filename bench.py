@@ -477,17 +477,27 @@ def run_gdn_prefill_secondary(be, args, st, peak_hbm):
                  (torch.rand(VHg, generator=g, device="cuda") * 2.77).cpu().numpy(),
                  torch.randn(VHg, generator=g, device="cuda").cpu().numpy(),
                  (1 + 0.1 * torch.randn(VD, generator=g, device="cuda")).cpu().numpy())
+    nkh = args.gdn_kheads or KHg          # K heads this GPU owns (a head shard when < 16)
+    if nkh != KHg:
+        assert be.lib.coli_cuda_gdn_state_ensure(2, 1, 2 * nkh, KD, VD) == 1
     for S in [int(x) for x in args.lengths.split(",")]:
         qkv = torch.randn(S, CD, generator=g, device="cuda").bfloat16()
         z = torch.randn(S, VHg * VD, generator=g, device="cuda").bfloat16()
         a = torch.randn(S, VHg, generator=g, device="cuda").bfloat16()
         b = torch.randn(S, VHg, generator=g, device="cuda").bfloat16()
-        y = torch.empty(S, VHg * VD, dtype=torch.bfloat16, device="cuda")
+        y = torch.empty(S, 2 * nkh * VD, dtype=torch.bfloat16, device="cuda")
+
+        def call():
+            if nkh == KHg:
+                be.gdn_prefill_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
+                                   y.data_ptr(), KHg, KD, VHg, VD, 1e-6, 1)
+            else:
+                be.gdn_prefill_heads_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(),
+                                         b.data_ptr(), y.data_ptr(), 0, nkh)
 
         def step():
             be.gdn_reset()
-            be.gdn_prefill_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
-                               y.data_ptr(), KHg, KD, VHg, VD, 1e-6, 1)
+            call()
         for _ in range(2):
             step()
         be.sync()
@@ -499,17 +509,17 @@ def run_gdn_prefill_secondary(be, args, st, peak_hbm):
             be.gdn_reset()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
-            be.gdn_prefill_dev(2, 0, S, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(),
-                               y.data_ptr(), KHg, KD, VHg, VD, 1e-6, 1)
+            call()
             e1.record(st)
             torch.cuda.synchronize()
             tot += e0.elapsed_time(e1)
         be.ktimer_enable(False)
         be.ktimer_read(be.K_GDN_PREFILL)
         ms = tot / reps
-        bytes_ = S * 32896 + 2 * 1024 * 1024
-        out[f"gdn_prefill_{S}"] = {
-            "metric": "GDN chunked prefill tok/s (one layer)", "S": S, "value": S / (ms / 1e3),
+        bytes_ = (S * 32896 + 2 * 1024 * 1024) * nkh // KHg
+        out[f"gdn_prefill_{S}" + (f"_kheads{nkh}" if nkh != KHg else "")] = {
+            "metric": "GDN chunked prefill tok/s (one layer)", "S": S, "k_heads": nkh,
+            "value": S / (ms / 1e3),
             "unit": "tok/s", "ms_per_call": ms, "achieved_GBs": bytes_ / (ms / 1e3) / 1e9,
             "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm}
         del qkv, z, a, b, y
@@ -603,6 +613,8 @@ def main():
                     default=None,
                     help="run one secondary leg alone and print its JSON (profiling)")
     ap.add_argument("--lengths", default="8192,32768", help="prefill lengths of the secondary legs")
+    ap.add_argument("--gdn-kheads", type=int, default=0,
+                    help="GDN prefill leg: K heads owned by this GPU (e.g. 2 = one rank of an 8-way head shard)")
     ap.add_argument("--stack-batch", type=int, default=256, help="stack decode requests (all GPUs)")
     args = ap.parse_args()
     globals()["B_REQ"], globals()["T_CTX"] = args.requests, args.context
