@@ -226,6 +226,127 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
         *reinterpret_cast<float4 *>(kt + i) = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// bf16 inputs: the same prologue with the CTA's whole input tile (64 tokens x
+// the 512 channels of one K head: q, k and its two V heads) brought into
+// shared memory with wide loads first, then 8 warps x 8 tokens; the q/k norm
+// is a warp reduction (lane = 4 q, 4 k and 8 v channels), and K^T leaves
+// through a shared-memory transpose as contiguous rows.
+constexpr int PRT_CH = 512;                  // channels of one K head's q|k|v0|v1
+constexpr int PRT_KT_LD = PRO_T + 1;
+size_t gdn_prologue_tile_smem()
+{
+    return (size_t)PRO_T * PRT_CH * 2 + 3 * PRT_CH * 4 + PRT_CH * 16 + PFG_D * PRT_KT_LD * 4;
+}
+__global__ void __launch_bounds__(256)
+gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __nv_bfloat16 *sX = reinterpret_cast<__nv_bfloat16 *>(smem_raw);        // [64][512]
+    float *sHalo = reinterpret_cast<float *>(sX + PRO_T * PRT_CH);          // [3][512] tokens s_begin-3..-1
+    float4 *sW = reinterpret_cast<float4 *>(sHalo + 3 * PRT_CH);            // [512] conv taps
+    float *sKT = reinterpret_cast<float *>(sW + PRT_CH);                    // [128][65]
+    const int kh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int S = p.S, s_begin = blockIdx.x * PRO_T, nrow = min(S, s_begin + PRO_T) - s_begin;
+    const int KHin = p.KHin ? p.KHin : p.KH, VHin = p.VHin ? p.VHin : p.VH;
+    const int kg = p.kh0 + kh;
+    const int key_dim = KHin * PFG_D, CD = 2 * key_dim + VHin * PFG_D;
+    const __nv_bfloat16 *x = static_cast<const __nv_bfloat16 *>(p.qkv);
+    auto gch = [&](int lc) {                 // local channel -> input channel
+        return lc < PFG_D ? kg * PFG_D + lc
+             : lc < 2 * PFG_D ? key_dim + kg * PFG_D + (lc - PFG_D)
+                              : 2 * key_dim + 2 * kg * PFG_D + (lc - 2 * PFG_D);
+    };
+    {   // the tile: 64 rows x 64 16-byte pieces, all loads in flight before any store
+        uint4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int e = tid + 256 * i, row = e >> 6, lc = (e & 63) * 8;
+            v[i] = row < nrow ? *reinterpret_cast<const uint4 *>(x + (size_t)(s_begin + row) * CD + gch(lc))
+                              : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int e = tid + 256 * i, row = e >> 6, lc = (e & 63) * 8;
+            *reinterpret_cast<uint4 *>(sX + row * PRT_CH + lc) = v[i];
+        }
+    }
+    for (int e = tid; e < 3 * PRT_CH; e += 256) {
+        const int j = e / PRT_CH, lc = e - j * PRT_CH, ts = s_begin - 3 + j;
+        sHalo[e] = ts >= 0 ? __bfloat162float(x[(size_t)ts * CD + gch(lc)]) : p.hist[(size_t)j * CD + gch(lc)];
+    }
+    for (int lc = tid; lc < PRT_CH; lc += 256) sW[lc] = *reinterpret_cast<const float4 *>(p.conv_w + (size_t)gch(lc) * 4);
+    __syncthreads();
+
+    const int r0 = warp * (PRO_T / 8);
+    auto xin = [&](int r, int lc) -> float {
+        return r >= 0 ? __bfloat162float(sX[r * PRT_CH + lc]) : sHalo[(3 + r) * PRT_CH + lc];
+    };
+    float h0[16], h1[16], h2[16];            // values at tokens s-3, s-2, s-1 of this lane's channels
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int lc = j * 32 + lane;
+        h0[j] = xin(r0 - 3, lc); h1[j] = xin(r0 - 2, lc); h2[j] = xin(r0 - 1, lc);
+    }
+    for (int rr = 0; rr < PRO_T / 8; ++rr) {
+        const int r = r0 + rr, s = s_begin + r;
+        if (r >= nrow) break;                // warp-uniform
+        float out[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int lc = j * 32 + lane;
+            const float4 w = sW[lc];
+            const float xv = __bfloat162float(sX[r * PRT_CH + lc]);
+            float a = 0.f;
+            a += w.x * h0[j]; a += w.y * h1[j]; a += w.z * h2[j]; a += w.w * xv;
+            out[j] = __fdividef(a, 1.f + __expf(-a));  // silu (fast exp / divide)
+            h0[j] = h1[j]; h1[j] = h2[j]; h2[j] = xv;
+        }
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { sq += out[j] * out[j]; sk += out[4 + j] * out[4 + j]; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
+        const float rk = 1.f / sqrtf(sk + p.eps);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = j * 32 + lane;
+            const float kv = tf32r(out[4 + j] * rk);
+            p.Qh[((size_t)kh * S + s) * PFG_D + c] = tf32r(out[j] * rq);
+            p.Kh[((size_t)kh * S + s) * PFG_D + c] = kv;
+            sKT[c * PRT_KT_LD + r] = kv;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int vh = kh * 2 + (j >> 2);
+            p.Vh[((size_t)vh * S + s) * PFG_D + (j & 3) * 32 + lane] = out[8 + j];
+        }
+        if (lane < 2) {
+            const int vh = kh * 2 + lane, vg = kg * 2 + lane;   // local / input-layout V head
+            const float av = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.a)[(size_t)s * VHin + vg]);
+            const float bv = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.b)[(size_t)s * VHin + vg]);
+            // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
+            p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
+            p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
+        }
+    }
+    __syncthreads();
+    // K^T of the chunk ([dk][64 tokens], tokens past S zero), row-contiguous
+    float *kt = p.KT + ((size_t)kh * gridDim.x + blockIdx.x) * PFG_D * PFG_C;
+    for (int e = tid; e < PFG_D * (PFG_C / 4); e += 256) {
+        const int d = e >> 4, t4 = (e & 15) * 4;
+        float4 v;
+        v.x = t4 < nrow ? sKT[d * PRT_KT_LD + t4] : 0.f;
+        v.y = t4 + 1 < nrow ? sKT[d * PRT_KT_LD + t4 + 1] : 0.f;
+        v.z = t4 + 2 < nrow ? sKT[d * PRT_KT_LD + t4 + 2] : 0.f;
+        v.w = t4 + 3 < nrow ? sKT[d * PRT_KT_LD + t4 + 3] : 0.f;
+        *reinterpret_cast<float4 *>(kt + d * PFG_C + t4) = v;
+    }
+}
+
 // New conv history = the last 3 pre-conv rows of the owned channels. Needs
 // S >= 3 (the host routes shorter runs through the token-by-token decode kernel).
 template <typename TI>
@@ -878,8 +999,14 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     const int nchunks = (a.S + PFG_C - 1) / PFG_C;
     const int CD = 2 * (a.KHin ? a.KHin : a.KH) * PFG_D + (a.VHin ? a.VHin : a.VH) * PFG_D;
     cudaError_t e;
-    if (bf16) gdn_pf_prologue_kernel<__nv_bfloat16><<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), PFG_D, 0, st>>>(a);
-    else gdn_pf_prologue_kernel<float><<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), PFG_D, 0, st>>>(a);
+    if (bf16) {
+        e = cudaFuncSetAttribute(gdn_pf_prologue_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)gdn_prologue_tile_smem());
+        if (e != cudaSuccess) return e;
+        gdn_pf_prologue_tile_kernel<<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), 256, gdn_prologue_tile_smem(), st>>>(a);
+    } else {
+        gdn_pf_prologue_kernel<float><<<dim3((a.S + PRO_T - 1) / PRO_T, a.KH), PFG_D, 0, st>>>(a);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (bf16) gdn_pf_hist_kernel<__nv_bfloat16><<<(3 * CD + 255) / 256, 256, 0, st>>>(a);
     else gdn_pf_hist_kernel<float><<<(3 * CD + 255) / 256, 256, 0, st>>>(a);
