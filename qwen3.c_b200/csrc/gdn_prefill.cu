@@ -368,7 +368,10 @@ __global__ void gdn_pf_hist_kernel(GdnPrefillArgs p)
 // ---------------------------------------------------------------- chunk prep
 constexpr int PREP_LD = 68;  // padded row stride (floats) of A / T in shared memory
 
-__global__ void __launch_bounds__(128)
+// 8 warps: warp w owns token rows 16 (w % 4).. of K K^T (w < 4) or Q K^T
+// (w >= 4), and later the same rows of W (w < 4) or U (w >= 4).
+constexpr int PREP_THREADS = 256;
+__global__ void __launch_bounds__(PREP_THREADS)
 gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, GdnPrefillArgs p)
 {
@@ -407,27 +410,25 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     mbar_wait(&bar_qk, 0);  // a time-out raises the device error word
 
-    // K K^T and Q K^T for this warp's 16 rows, all 64 columns
-    const int r0 = warp * 16;
+    // K K^T (warps 0-3) or Q K^T (warps 4-7) for this warp's 16 rows, all 64 columns
+    const int r0 = (warp & 3) * 16, second = warp >> 2;
     {
-        float kk[8][4], qk[8][4];
+        float acc[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) kk[nt][e] = qk[nt][e] = 0.f;
+            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
         // Q and K were rounded to tf32 by the prologue: ldmatrix feeds them as is
-        const uint32_t aKs = smem_u32(sK), aQs = smem_u32(sQV);
+        const uint32_t aKs = smem_u32(sK), aAs = second ? smem_u32(sQV) : aKs;
 #pragma unroll 2
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            uint32_t ak[4], aq[4];
-            lda_sw(aKs, r0, ks, lane, ak);
-            lda_sw(aQs, r0, ks, lane, aq);
+            uint32_t a[4];
+            lda_sw(aAs, r0, ks, lane, a);
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
                 uint32_t b0, b1;
                 ldb_sw(aKs, nt * 8, ks, lane, b0, b1);
-                mma_tf32(kk[nt], ak[0], ak[1], ak[2], ak[3], b0, b1);
-                mma_tf32(qk[nt], aq[0], aq[1], aq[2], aq[3], b0, b1);
+                mma_tf32(acc[nt], a[0], a[1], a[2], a[3], b0, b1);
             }
         }
         float *Mg = p.M + ((size_t)n * p.VH + h) * PFG_C * PFG_C;
@@ -437,8 +438,8 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int e = 0; e < 4; ++e) {
                 const int i = r0 + g + ((e >> 1) << 3), j = nt * 8 + 2 * tq + (e & 1);
                 const float dec = expf(G[i] - G[j]);
-                sA[i * PREP_LD + j] = j < i ? bet[i] * dec * kk[nt][e] : 0.f;
-                Mg[i * PFG_C + j] = j <= i ? tf32r(dec * qk[nt][e]) : 0.f;
+                if (second) Mg[i * PFG_C + j] = j <= i ? tf32r(dec * acc[nt][e]) : 0.f;
+                else sA[i * PREP_LD + j] = j < i ? bet[i] * dec * acc[nt][e] : 0.f;
             }
         }
     }
@@ -453,7 +454,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // diagonal blocks by forward substitution (one column per thread), then
     // T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one block diagonal at a time.
     {
-        for (int e = tid; e < PFG_C * PFG_C; e += 128) sT[(e >> 6) * PREP_LD + (e & 63)] = 0.f;
+        for (int e = tid; e < PFG_C * PFG_C; e += PREP_THREADS) sT[(e >> 6) * PREP_LD + (e & 63)] = 0.f;
         __syncthreads();
         if (tid < 64) {
             const int o = (tid >> 4) * 16, c = tid & 15;
@@ -467,7 +468,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int dist = 1; dist < 4; ++dist) {
             const int nblk = 4 - dist;                 // blocks (p, p - dist), p = dist..3
             // X_p = sum_{r=q}^{p-1} A_pr T_rq
-            for (int e = tid; e < nblk * 256; e += 128) {
+            for (int e = tid; e < nblk * 256; e += PREP_THREADS) {
                 const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
                 const int pr = (dist + bi) * 16, q = bi * 16;
                 float acc = 0.f;
@@ -478,7 +479,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             __syncthreads();
             // T_pq = -T_pp X_p
-            for (int e = tid; e < nblk * 256; e += 128) {
+            for (int e = tid; e < nblk * 256; e += PREP_THREADS) {
                 const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
                 const int pr = (dist + bi) * 16, q = bi * 16;
                 float acc = 0.f;
@@ -492,42 +493,41 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     mbar_wait(&bar_v, 0);
 
-    // W = T (beta gamma K), U = T (beta V) for this warp's 16 rows, 128 columns
-    float *Wg = p.W + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
-    float *Ug = p.U + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
+    // W = T (beta gamma K) (warps 0-3) or U = T (beta V) (warps 4-7) for this
+    // warp's 16 rows, 128 columns in two halves
+    float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
+    const float *sB = second ? sQV : sK;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
-        float w[8][4], u[8][4];
+        float w[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) w[nt][e] = u[nt][e] = 0.f;
+            for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
 #pragma unroll 2
         for (int ks = 0; ks < PFG_C / 8; ++ks) {
             const int c0 = ks * 8 + tq, c1 = c0 + 4;
             const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0]), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0]);
             const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1]), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1]);
-            const float bg0 = bet[c0] * expf(G[c0]), bg1 = bet[c1] * expf(G[c1]);
-            const float bb0 = bet[c0], bb1 = bet[c1];
+            const float s0 = second ? bet[c0] : bet[c0] * expf(G[c0]);
+            const float s1 = second ? bet[c1] : bet[c1] * expf(G[c1]);
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
                 const int col = half * 64 + nt * 8 + g;
-                const uint32_t bk0 = f2tf32(bg0 * sw_ld(sK, PFG_C, c0, col));
-                const uint32_t bk1 = f2tf32(bg1 * sw_ld(sK, PFG_C, c1, col));
-                const uint32_t bv0 = f2tf32(bb0 * sw_ld(sQV, PFG_C, c0, col));
-                const uint32_t bv1 = f2tf32(bb1 * sw_ld(sQV, PFG_C, c1, col));
-                mma_tf32(w[nt], a0, a1, a2, a3, bk0, bk1);
-                mma_tf32(u[nt], a0, a1, a2, a3, bv0, bv1);
+                const uint32_t b0 = f2tf32(s0 * sw_ld(sB, PFG_C, c0, col));
+                const uint32_t b1 = f2tf32(s1 * sw_ld(sB, PFG_C, c1, col));
+                mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
             }
         }
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int col = half * 64 + nt * 8 + 2 * tq;
             const int ra = r0 + g, rb = ra + 8;
-            *reinterpret_cast<float2 *>(Wg + ra * PFG_D + col) = make_float2(tf32r(w[nt][0]), tf32r(w[nt][1]));
-            *reinterpret_cast<float2 *>(Wg + rb * PFG_D + col) = make_float2(tf32r(w[nt][2]), tf32r(w[nt][3]));
-            *reinterpret_cast<float2 *>(Ug + ra * PFG_D + col) = make_float2(u[nt][0], u[nt][1]);
-            *reinterpret_cast<float2 *>(Ug + rb * PFG_D + col) = make_float2(u[nt][2], u[nt][3]);
+            // W feeds the walk's tensor core as is: rounded to tf32 here
+            const float x0 = second ? w[nt][0] : tf32r(w[nt][0]), x1 = second ? w[nt][1] : tf32r(w[nt][1]);
+            const float x2 = second ? w[nt][2] : tf32r(w[nt][2]), x3 = second ? w[nt][3] : tf32r(w[nt][3]);
+            *reinterpret_cast<float2 *>(Og + ra * PFG_D + col) = make_float2(x0, x1);
+            *reinterpret_cast<float2 *>(Og + rb * PFG_D + col) = make_float2(x2, x3);
         }
     }
 }
@@ -1013,7 +1013,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(gdn_pf_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_prep_smem());
     if (e != cudaSuccess) return e;
-    gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), 128, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, a);
+    gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), PREP_THREADS, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     auto scan = [&](auto kern, size_t smem, int grid) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

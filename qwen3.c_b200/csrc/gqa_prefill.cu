@@ -34,6 +34,15 @@ constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES;  // 208 KiB
 constexpr int PF_THREADS = 576;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
+// 2^x with the MUFU instruction (relative error ~2^-22, -inf -> 0): one
+// instruction per probability in the softmax, which is issue bound.
+__device__ __forceinline__ float ex2_approx(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 struct PfBars {
     uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
@@ -189,18 +198,21 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tc::wait_ld();
             tc::fence_before();
             mbar_arrive(&bars.s_free[b]);
+            // Raw scores; the log2-domain scale is applied inside the exponent
+            // (scale > 0, so the max commutes with it).
             const int key0 = i * PF_BN + 16 * qr;
             float mx = -INFINITY;
             if (key0 + 15 <= qpos) {                       // tile fully visible to this row
 #pragma unroll
-                for (int c = 0; c < 16; ++c) { x[c] *= sl2; mx = fmaxf(mx, x[c]); }
+                for (int c = 0; c < 16; ++c) mx = fmaxf(mx, x[c]);
             } else {
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
-                    x[c] = (key0 + c <= qpos) ? x[c] * sl2 : -INFINITY;
+                    x[c] = (key0 + c <= qpos) ? x[c] : -INFINITY;
                     mx = fmaxf(mx, x[c]);
                 }
             }
+            mx *= sl2;
             bars.mx[b][qr][row] = mx;
             asm volatile("bar.sync 1, 512;" ::: "memory");
             mx = fmaxf(fmaxf(bars.mx[b][0][row], bars.mx[b][1][row]),
@@ -234,7 +246,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             uint32_t pk[8];
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const float p0 = exp2f(x[2 * c] - mu), p1 = exp2f(x[2 * c + 1] - mu);
+                const float p0 = ex2_approx(fmaf(x[2 * c], sl2, -mu)), p1 = ex2_approx(fmaf(x[2 * c + 1], sl2, -mu));
                 rs += p0 + p1;
                 pk[c] = pack_bf16(p0, p1);
             }
