@@ -211,6 +211,52 @@ int  coli_cuda_gdn_prefill_heads_dev(int layer, int req, int S, const void *qkv,
                                      const void *a, const void *b, void *y, int KH, int KD,
                                      int VH, int VD, float eps, int dtype, int kh0, int nkh);
 
+/* ==== Block level: projections + mixer + out-projection ====
+ * Resident dense weights, W [O][I] row-major as the engine stores it, held on
+ * the device in bf16. Replaces coli_vk_tensor_ensure / _free / _bytes
+ * (c/backend_vulkan.h:105, 143-144): fmt 0 = f32 weights, fmt 1 = int8 with
+ * one scale per output row (dequantised to bf16 on upload); other formats
+ * return 0 (caller keeps its own path). An existing handle of the same shape
+ * is kept as is. I must be a multiple of 8. */
+typedef struct ColiCudaTensor ColiCudaTensor;
+int    coli_cuda_tensor_ensure(ColiCudaTensor **tensor, const void *weights, const float *scales,
+                               int fmt, int I, int O, int grp);
+void   coli_cuda_tensor_free(ColiCudaTensor *t);
+size_t coli_cuda_tensor_bytes(const ColiCudaTensor *t);
+
+/* y[S][O] = x[S][I] W^T (c/qwen.c:178-189 matmul; coli_vk_matmul,
+ * c/backend_vulkan.h:56): uploads the tensor on first use. */
+int  coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const void *w,
+                      const float *scales, int fmt, int S, int I, int O, int gs);
+
+/* Whole gated-GQA block for S rows of request 0 (coli_vk_gqa_full,
+ * c/backend_vulkan.h:173-177; CPU c/qwen.c:595-665): q|gate, k, v
+ * projections -> q/k norm + RoPE + KV append -> causal attention -> gate ->
+ * o_proj. Needs coli_cuda_kv_ensure + coli_cuda_gqa_norm_weight. x [S][D],
+ * out [S][Dout] fp32 host. */
+int  coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t,
+                        ColiCudaTensor *gk_t, ColiCudaTensor *gv_t, ColiCudaTensor *out_t,
+                        float *out, int S, int H, int KH, int hd, int rot, int pos_base,
+                        int max_t, float eps, float theta, int Dout);
+
+/* Whole GatedDeltaNet block for one token of request 0 (coli_vk_gdn_full,
+ * c/backend_vulkan.h:266-272; CPU c/qwen.c:697-773): in_proj_qkv / in_proj_z
+ * -> conv4 (+ history) -> q/k norm -> delta rule -> gated RMSNorm ->
+ * out_proj. params = [decay(VH) | beta(VH) | gnorm(VD)] as the engine packs
+ * them (c/qwen.c:681-686). Needs coli_cuda_gdn_state_ensure,
+ * coli_cuda_gdn_conv_ensure and coli_cuda_gdn_conv_weight. */
+int  coli_cuda_gdn_full(int layer, const float *x, int D, ColiCudaTensor *gqkv_t,
+                        ColiCudaTensor *gz_t, const float *params, ColiCudaTensor *out_t,
+                        float *out, int KH, int KD, int VH, int VD, int conv_dim, int conv_k,
+                        float eps, int Dout);
+/* S tokens of the same block (coli_vk_gdn_full_seq, c/backend_vulkan.h:276-281):
+ * params [S][2*VH+VD], out [S][Dout]; S >= 64 runs the chunk-parallel prefill,
+ * shorter runs step token by token. */
+int  coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t,
+                            ColiCudaTensor *gz_t, const float *params, ColiCudaTensor *out_t,
+                            float *out, int KH, int KD, int VH, int VD, int conv_dim,
+                            int conv_k, float eps, int Dout);
+
 #ifdef __cplusplus
 }
 #endif

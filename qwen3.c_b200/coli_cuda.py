@@ -69,6 +69,13 @@ SIGNATURES = {
     "coli_cuda_gdn_decode_dev": ([_i, _i] + [_vp] * 5 + [_i] * 4 + [_f, _i], _i),
     "coli_cuda_gdn_prefill": ([_i, _i, _i] + [_fp] * 5 + [_i] * 4 + [_f], _i),
     "coli_cuda_gdn_prefill_dev": ([_i, _i, _i] + [_vp] * 5 + [_i] * 4 + [_f, _i], _i),
+    "coli_cuda_tensor_ensure": ([ctypes.POINTER(_vp), _vp, _fp, _i, _i, _i, _i], _i),
+    "coli_cuda_tensor_free": ([_vp], None),
+    "coli_cuda_tensor_bytes": ([_vp], ctypes.c_size_t),
+    "coli_cuda_matmul": ([ctypes.POINTER(_vp), _fp, _fp, _vp, _fp] + [_i] * 5, _i),
+    "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
+    "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
+    "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
 }
 
 
@@ -315,3 +322,75 @@ class Backend:
                         eps=1e-6, dtype=1):
         self._ok(self.lib.coli_cuda_gdn_prefill_dev(layer, req, S, qkv, z, a, b, y, KH, KD, VH, VD,
                                                     eps, dtype), "gdn_prefill_dev")
+
+
+class DenseTensor:
+    """A resident dense weight W [O][I] (bf16 on the device), the handle the
+    block-level calls take. fmt 0 = fp32 weights, 1 = int8 with per-row scales."""
+
+    def __init__(self, be, w, scales=None, fmt=0):
+        self.be = be
+        self.O, self.I = w.shape
+        self.h = _vp()
+        if fmt == 0:
+            w = np.ascontiguousarray(w, np.float32)
+            sp = None
+        else:
+            w = np.ascontiguousarray(w, np.int8)
+            scales, sp = _f32(scales)
+        be._ok(be.lib.coli_cuda_tensor_ensure(ctypes.byref(self.h), w.ctypes.data, sp, fmt, self.I, self.O, 0),
+               "tensor_ensure")
+
+    @property
+    def nbytes(self):
+        return self.be.lib.coli_cuda_tensor_bytes(self.h)
+
+    def free(self):
+        if self.h:
+            self.be.lib.coli_cuda_tensor_free(self.h)
+            self.h = _vp()
+
+
+def _block_methods():
+    """Block-level calls (projections + mixer + out-projection) on Backend."""
+
+    def matmul(self, t, x):
+        """y = x W^T with a DenseTensor t; x [S][I] fp32 host."""
+        x, xp = _f32(x)
+        S = x.shape[0] if x.ndim > 1 else 1
+        y = np.zeros((S, t.O), np.float32)
+        self._ok(self.lib.coli_cuda_matmul(ctypes.byref(t.h), y.ctypes.data_as(_fp), xp, None, None, 0, S, t.I,
+                                           t.O, 0), "matmul")
+        return y
+
+    def gqa_full(self, layer, x, gq, gk, gv, go, pos_base, H=16, KH=2, hd=256, rot=64, max_t=None, eps=1e-6,
+                 theta=1e7):
+        x, xp = _f32(x)
+        S, D = x.shape
+        out = np.zeros((S, go.O), np.float32)
+        self._ok(self.lib.coli_cuda_gqa_full(layer, xp, D, gq.h, gk.h, gv.h, go.h, out.ctypes.data_as(_fp), S, H, KH,
+                                             hd, rot, pos_base, max_t or (pos_base + S), eps, theta, go.O),
+                 "gqa_full")
+        return out
+
+    def gdn_full_seq(self, layer, x, params, gqkv, gz, gout, KH=16, KD=128, VH=32, VD=128, eps=1e-6):
+        """S tokens (S = 1 goes through coli_cuda_gdn_full); params [S][2*VH+VD]."""
+        x, xp = _f32(x)
+        S, D = x.shape
+        params, pp = _f32(params)
+        out = np.zeros((S, gout.O), np.float32)
+        CD = 2 * KH * KD + VH * VD
+        if S == 1:
+            rc = self.lib.coli_cuda_gdn_full(layer, xp, D, gqkv.h, gz.h, pp, gout.h, out.ctypes.data_as(_fp), KH, KD,
+                                             VH, VD, CD, 4, eps, gout.O)
+        else:
+            rc = self.lib.coli_cuda_gdn_full_seq(layer, xp, S, D, gqkv.h, gz.h, pp, gout.h,
+                                                 out.ctypes.data_as(_fp), KH, KD, VH, VD, CD, 4, eps, gout.O)
+        self._ok(rc, "gdn_full")
+        return out
+
+    for f in (matmul, gqa_full, gdn_full_seq):
+        setattr(Backend, f.__name__, f)
+
+
+_block_methods()

@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <vector>
+#include <algorithm>
 
 #include "../../include/backend_cuda.h"
 #include "common.cuh"
@@ -24,6 +25,7 @@
 #include "gqa_decode.cu"
 #include "gqa_prefill.cu"
 #include "gdn_prefill.cu"
+#include "linear.cu"
 
 namespace {
 
@@ -58,7 +60,8 @@ struct GdnLayer {
 
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
-            S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_GHS, S_GXS, S_COUNT };
+            S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_GHS, S_GXS,
+            S_XB, S_PQ, S_PK, S_PV, S_PCTX, S_LPART, S_PAR, S_PY, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -341,7 +344,8 @@ int gdn_shape_ok(GdnLayer &L, int KH, int KD, int VH, int VD, int need_conv)
 }
 
 int gdn_decode_run(int layer, int B, int req0, const void *qkv, const void *z, const void *a,
-                   const void *b, void *y, int KH, int KD, int VH, int VD, float eps, int bf16)
+                   const void *b, void *y, int KH, int KD, int VH, int VD, float eps, int bf16,
+                   const float *pdecay = nullptr, const float *pbeta = nullptr, const float *pgnorm = nullptr)
 {
     GdnLayer &L = G.gdn[layer];
     if (!gdn_shape_ok(L, KH, KD, VH, VD, 1)) return 0;
@@ -350,6 +354,9 @@ int gdn_decode_run(int layer, int B, int req0, const void *qkv, const void *z, c
     memset(&ga, 0, sizeof(ga));
     ga.qkv = qkv; ga.z = z; ga.a = a; ga.b = b;
     ga.conv_w = L.conv_w; ga.A_log = L.A_log; ga.dt_bias = L.dt_bias; ga.gnorm = L.gnorm;
+    ga.pdecay = pdecay; ga.pbeta = pbeta;
+    if (pgnorm) ga.gnorm = pgnorm;
+    if (!pdecay && !L.A_log) return fail("GDN A_log/dt_bias/gnorm not set");
     ga.hist = L.hist + (size_t)req0 * 3 * L.conv_dim;
     ga.state = L.state + (size_t)req0 * VH * KD * VD;
     ga.y = y;
@@ -378,7 +385,7 @@ int make_f32_3d(CUtensorMap *m, void *base, int d0, int d1, int d2, int box0, in
 constexpr int GDN_CHUNK_MIN_ROWS = 64;
 int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *z, const void *a,
                         const void *b, void *y, int KHin, int KD, int VHin, int VD, float eps,
-                        int dtype, int kh0 = 0, int nkh = -1)
+                        int dtype, int kh0 = 0, int nkh = -1, const float *params = nullptr)
 {
     GdnLayer &L = G.gdn[layer];
     if (nkh < 0) nkh = KHin;
@@ -388,13 +395,16 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     if (kh0 < 0 || kh0 + nkh > KHin) return fail("bad K head range");
     if (!L.hist || !L.conv_w || L.conv_k != 4 || L.conv_dim != 2 * KHin * KD + VHin * VD)
         return fail("GDN conv history/weights not set for this layer");
-    if (!L.A_log || L.pVH != VHin) return fail("GDN A_log/dt_bias/gnorm not set for %d V heads", VHin);
+    if (!params && (!L.A_log || L.pVH != VHin)) return fail("GDN A_log/dt_bias/gnorm not set for %d V heads", VHin);
     if (req < 0 || req >= L.batch || req >= L.hbatch) return fail("request out of range");
     const int nch = (S + 63) / 64;
     GdnPrefillArgs p;
     memset(&p, 0, sizeof(p));
     p.qkv = qkv; p.z = z; p.a = a; p.b = b;
     p.conv_w = L.conv_w; p.A_log = L.A_log; p.dt_bias = L.dt_bias; p.gnorm = L.gnorm;
+    if (params) {   // rows [decay(VHin) | beta(VHin) | gnorm(VD)]; gnorm from the first row
+        p.params = params; p.pstride = 2 * VHin + VD; p.gnorm = params + 2 * VHin;
+    }
     p.hist = L.hist + (size_t)req * 3 * L.conv_dim;
     p.state = L.state + (size_t)req * VH * KD * VD;
     p.y = y;
@@ -1088,3 +1098,4 @@ int coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const flo
 
 // Fixed-scratch decode entry point (no device allocation on its path).
 #include "noalloc.cu"
+#include "block.cu"

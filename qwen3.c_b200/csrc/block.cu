@@ -1,0 +1,220 @@
+// Block-level entry points: the mixer with its projections, the role of
+// coli_vk_gqa_full / coli_vk_gdn_full / coli_vk_gdn_full_seq
+// (c/backend_vulkan.h:173-185, 266-283) and of the resident dense tensors
+// they take (coli_vk_tensor_ensure, c/backend_vulkan.h:105). Included at the
+// end of backend.cu (one translation unit).
+//
+// Weights are held in bf16 ([O][I], the engine's row-major layout), uploaded
+// once; activations between the steps stay on the device (bf16), only x goes
+// up and the block output comes back, as in the Vulkan backend's single
+// submit. The projections run on linear_kernel (tcgen05); the mixer steps are
+// the same kernels as the *_dev entry points.
+
+struct ColiCudaTensor {
+    __nv_bfloat16 *w = nullptr;   // [O][I]
+    int I = 0, O = 0;
+    CUtensorMap tm;               // 64 x 128 boxes, 128B swizzle
+};
+
+namespace {
+
+int make_bf16_2d(CUtensorMap *m, const void *base, int inner, int outer, int box_inner, int box_outer)
+{
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = G.encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled (bf16 2d) failed (%d)", (int)r);
+    return 1;
+}
+
+// y[S][O] = x[S][I] W^T on the device (x bf16, y fp32 or bf16).
+int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, int y_bf16)
+{
+    if (!t || !t->w) return fail("dense tensor not uploaded");
+    const int bn = linear_pick_bn(S);
+    CUtensorMap tx;
+    if (!make_bf16_2d(&tx, x, t->I, S, 64, bn)) return 0;
+    const int tiles = ((t->O + 127) / 128) * ((S + bn - 1) / bn), nk = (t->I + 63) / 64;
+    int splits = 1;
+    if (2 * tiles <= G.num_sms) splits = std::max(1, std::min(G.num_sms / tiles, nk / 4));
+    LinearArgs la;
+    memset(&la, 0, sizeof(la));
+    la.y = y; la.S = S; la.I = t->I; la.O = t->O; la.y_bf16 = y_bf16;
+    if (splits > 1) {
+        la.part = (float *)scratch(S_LPART, (size_t)splits * S * t->O * 4);
+        if (!la.part) return 0;
+    }
+    CK(launch_linear(t->tm, tx, la, bn, splits, stream()));
+    g_launches += splits > 1 ? 2 : 1;
+    return 1;
+}
+
+// Host fp32 [n] -> device bf16 (through an fp32 staging slot).
+const __nv_bfloat16 *upload_bf16(const float *x, size_t n)
+{
+    const float *xd = (const float *)upload(S_IN0, x, n * 4);
+    __nv_bfloat16 *xb = (__nv_bfloat16 *)scratch(S_XB, n * 2);
+    if (!xd || !xb) return nullptr;
+    if (launch_f32_to_bf16(xd, xb, n, stream()) != cudaSuccess) {
+        cuda_fail(cudaGetLastError(), "f32_to_bf16");
+        return nullptr;
+    }
+    g_launches += 1;
+    return xb;
+}
+
+int tensor_shape(const ColiCudaTensor *t, int I, int O, const char *what)
+{
+    if (!t || !t->w) return fail("%s tensor not uploaded", what);
+    if (t->I != I || t->O != O) return fail("%s tensor is %dx%d, expected %dx%d", what, t->O, t->I, O, I);
+    return 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int coli_cuda_tensor_ensure(ColiCudaTensor **tensor, const void *weights, const float *scales, int fmt, int I,
+                            int O, int grp)
+{
+    READY();
+    (void)grp;
+    if (!tensor) return fail("null tensor handle");
+    if (*tensor && (*tensor)->I == I && (*tensor)->O == O) return 1;   // resident already
+    if (fmt != 0 && fmt != 1) return fail("dense format %d not supported (0 = f32, 1 = int8 per-row scale)", fmt);
+    if (fmt == 1 && !scales) return fail("int8 weights need per-row scales");
+    if (I < 8 || I % 8 || O < 1 || !weights) return fail("bad dense shape %dx%d (I must be a multiple of 8)", O, I);
+    ColiCudaTensor *t = *tensor ? *tensor : new ColiCudaTensor();
+    if (t->w) { dev_free(t->w, (size_t)t->I * t->O * 2); t->w = nullptr; }
+    std::vector<__nv_bfloat16> h((size_t)I * O);
+    for (int o = 0; o < O; ++o) {
+        for (int i = 0; i < I; ++i) {
+            const size_t k = (size_t)o * I + i;
+            const float v = fmt == 0 ? static_cast<const float *>(weights)[k]
+                                     : (float)static_cast<const int8_t *>(weights)[k] * scales[o];
+            h[k] = __float2bfloat16_rn(v);
+        }
+    }
+    void *d = nullptr;
+    if (!dev_alloc(&d, h.size() * 2)) { if (!*tensor) delete t; return 0; }
+    t->w = (__nv_bfloat16 *)d;
+    t->I = I; t->O = O;
+    if (cudaMemcpyAsync(t->w, h.data(), h.size() * 2, cudaMemcpyHostToDevice, stream()) != cudaSuccess ||
+        cudaStreamSynchronize(stream()) != cudaSuccess) {
+        cuda_fail(cudaGetLastError(), "tensor upload");
+        return 0;
+    }
+    if (!make_bf16_2d(&t->tm, t->w, I, O, 64, 128)) return 0;
+    *tensor = t;
+    return 1;
+}
+
+void coli_cuda_tensor_free(ColiCudaTensor *t)
+{
+    if (!t) return;
+    if (t->w) dev_free(t->w, (size_t)t->I * t->O * 2);
+    delete t;
+}
+
+size_t coli_cuda_tensor_bytes(const ColiCudaTensor *t) { return t && t->w ? (size_t)t->I * t->O * 2 : 0; }
+
+int coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const void *w, const float *scales, int fmt,
+                     int S, int I, int O, int gs)
+{
+    READY();
+    if (S < 1) return fail("bad S");
+    if (!coli_cuda_tensor_ensure(tensor, w, scales, fmt, I, O, gs)) return 0;
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * I);
+    float *yd = (float *)scratch(S_OUT, (size_t)S * O * 4);
+    if (!xb || !yd) return 0;
+    if (!linear_dev(*tensor, xb, S, yd, 0)) return 0;
+    if (!download(y, yd, (size_t)S * O * 4)) return 0;
+    return check_dev_error();
+}
+
+int coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
+                       ColiCudaTensor *gv_t, ColiCudaTensor *out_t, float *out, int S, int H, int KH, int hd,
+                       int rot, int pos_base, int max_t, float eps, float theta, int Dout)
+{
+    READY();
+    if (!check_layer(layer)) return fail("layer %d out of range", layer);
+    if (S < 1 || pos_base < 0) return fail("bad S/pos_base");
+    KvLayer &L = G.kv[layer];
+    if (!L.k) return fail("KV layer %d not allocated", layer);
+    if (max_t > L.max_t || pos_base + S > L.max_t) return fail("positions beyond the cache (max_t %d)", L.max_t);
+    if (!tensor_shape(gq_t, D, H * 2 * hd, "q|gate") || !tensor_shape(gk_t, D, KH * hd, "k") ||
+        !tensor_shape(gv_t, D, KH * hd, "v") || !tensor_shape(out_t, H * hd, Dout, "o_proj"))
+        return 0;
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
+    auto *qg = (__nv_bfloat16 *)scratch(S_PQ, (size_t)S * H * 2 * hd * 2);
+    auto *k = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * KH * hd * 2);
+    auto *v = (__nv_bfloat16 *)scratch(S_PV, (size_t)S * KH * hd * 2);
+    auto *ctx = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * H * hd * 2);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!xb || !qg || !k || !v || !ctx || !od) return 0;
+    if (!linear_dev(gq_t, xb, S, qg, 1) || !linear_dev(gk_t, xb, S, k, 1) || !linear_dev(gv_t, xb, S, v, 1))
+        return 0;
+    if (!coli_cuda_gqa_step_dev(layer, 0, S, pos_base, qg, k, v, ctx, H, KH, hd, rot, eps, theta, 1)) return 0;
+    if (!linear_dev(out_t, ctx, S, od, 0)) return 0;
+    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
+    return check_dev_error();
+}
+
+// S tokens of one request (request 0), params rows [decay(VH) | beta(VH) | gnorm(VD)].
+static int gdn_full_rows(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                         const float *params, ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
+                         int conv_dim, int conv_k, float eps, int Dout)
+{
+    READY();
+    if (!check_layer(layer)) return fail("layer %d out of range", layer);
+    if (S < 1 || !params) return fail("bad S / params");
+    if (conv_k != 4 || conv_dim != 2 * KH * KD + VH * VD) return fail("conv shape %d x %d not supported", conv_k, conv_dim);
+    if (!tensor_shape(gqkv_t, D, conv_dim, "in_proj_qkv") || !tensor_shape(gz_t, D, VH * VD, "in_proj_z") ||
+        !tensor_shape(out_t, VH * VD, Dout, "out_proj"))
+        return 0;
+    const int ps = 2 * VH + VD;
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
+    const float *pd = (const float *)upload(S_PAR, params, (size_t)S * ps * 4);
+    auto *qkv = (__nv_bfloat16 *)scratch(S_PQ, (size_t)S * conv_dim * 2);
+    auto *z = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * VH * VD * 2);
+    auto *y = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * VH * VD * 2);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!xb || !pd || !qkv || !z || !y || !od) return 0;
+    if (!linear_dev(gqkv_t, xb, S, qkv, 1) || !linear_dev(gz_t, xb, S, z, 1)) return 0;
+    if (S >= GDN_CHUNK_MIN_ROWS) {
+        if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, y, KH, KD, VH, VD, eps, 1, 0, -1, pd))
+            return 0;
+    } else {
+        for (int s = 0; s < S; ++s) {
+            const float *pr = pd + (size_t)s * ps;
+            if (!gdn_decode_run(layer, 1, 0, qkv + (size_t)s * conv_dim, z + (size_t)s * VH * VD, nullptr, nullptr,
+                                y + (size_t)s * VH * VD, KH, KD, VH, VD, eps, 1, pr, pr + VH, pr + 2 * VH))
+                return 0;
+        }
+    }
+    if (!linear_dev(out_t, y, S, od, 0)) return 0;
+    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
+    return check_dev_error();
+}
+
+int coli_cuda_gdn_full(int layer, const float *x, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                       const float *params, ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
+                       int conv_dim, int conv_k, float eps, int Dout)
+{
+    return gdn_full_rows(layer, x, 1, D, gqkv_t, gz_t, params, out_t, out, KH, KD, VH, VD, conv_dim, conv_k, eps,
+                         Dout);
+}
+
+int coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                           const float *params, ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
+                           int conv_dim, int conv_k, float eps, int Dout)
+{
+    return gdn_full_rows(layer, x, S, D, gqkv_t, gz_t, params, out_t, out, KH, KD, VH, VD, conv_dim, conv_k, eps,
+                         Dout);
+}
+
+}  // extern "C"

@@ -96,9 +96,15 @@ gdn_decode_kernel(GdnDecodeArgs p)
         const float rk = 1.f / sqrtf(sk + p.eps);
         qs[t] = qc * rq;
         ks[t] = kc * rk;
-        const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)b * VH + vh]), bv = to_f32(static_cast<const TI *>(p.b)[(size_t)b * VH + vh]);
-        beta = sigmoidf_(bv);
-        decay = expf(-expf(p.A_log[vh]) * softplusf_(av + p.dt_bias[vh]));
+        if (p.pdecay) {
+            beta = p.pbeta[(size_t)b * VH + vh];
+            decay = p.pdecay[(size_t)b * VH + vh];
+        } else {
+            const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)b * VH + vh]);
+            const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)b * VH + vh]);
+            beta = sigmoidf_(bv);
+            decay = expf(-expf(p.A_log[vh]) * softplusf_(av + p.dt_bias[vh]));
+        }
         // All CTAs of the cluster have read (and used) the old q/k history:
         // the owner (rank 0) may now shift it. The history stores are issued
         // only after this barrier, so the arrive does not wait on them.

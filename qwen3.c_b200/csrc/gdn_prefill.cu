@@ -134,6 +134,28 @@ __device__ __forceinline__ void chunk_cumsum(const float *gl, int t0, int S, int
     dst[i0 + 1] = excl + g0 + g1;
 }
 
+// Log decay and beta of token s, V head vh (vg in the input layout): from the
+// a / b projections as the reference's gdn_step does (decay = exp(-exp(A_log)
+// * softplus(a + dt_bias)), beta = sigmoid(b), c/qwen.c:725-730), or given by
+// the caller (params rows [decay | beta | ...]); a decay of exactly 0 is kept
+// finite in the log domain.
+template <typename TI>
+__device__ __forceinline__ void gdn_gates(const GdnPrefillArgs &p, int s, int vh, int vg, int VHin, const TI *a,
+                                          const TI *b)
+{
+    float gl, beta;
+    if (p.params) {
+        const float *pr = p.params + (size_t)s * p.pstride;
+        gl = fmaxf(logf(pr[vg]), -1.0e4f);
+        beta = pr[VHin + vg];
+    } else {
+        gl = -expf(p.A_log[vg]) * softplusf_(to_f32(a[(size_t)s * VHin + vg]) + p.dt_bias[vg]);
+        beta = sigmoidf_(to_f32(b[(size_t)s * VHin + vg]));
+    }
+    p.GL[(size_t)vh * p.S + s] = gl;
+    p.BETA[(size_t)vh * p.S + s] = beta;
+}
+
 // ---------------------------------------------------------------- prologue
 // One CTA walks a run of PRO_T tokens of one K head; thread t owns channel t
 // of q, k and of the head's two V heads, keeping the last three pre-conv
@@ -211,13 +233,7 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
             for (int j = 0; j < 2; ++j) {
                 const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
                 p.Vh[((size_t)vh * S + s) * PFG_D + t] = out[2 + j];
-                if (t == j) {
-                    const float av = to_f32(static_cast<const TI *>(p.a)[(size_t)s * VHin + vg]);
-                    const float bv = to_f32(static_cast<const TI *>(p.b)[(size_t)s * VHin + vg]);
-                    // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
-                    p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
-                    p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
-                }
+                if (t == j) gdn_gates(p, s, vh, vg, VHin, static_cast<const TI *>(p.a), static_cast<const TI *>(p.b));
             }
         }
         *reinterpret_cast<float4 *>(kt + (s4 - s_begin)) = make_float4(kb[0], kb[1], kb[2], kb[3]);
@@ -324,14 +340,9 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
             const int vh = kh * 2 + (j >> 2);
             p.Vh[((size_t)vh * S + s) * PFG_D + (j & 3) * 32 + lane] = out[8 + j];
         }
-        if (lane < 2) {
-            const int vh = kh * 2 + lane, vg = kg * 2 + lane;   // local / input-layout V head
-            const float av = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.a)[(size_t)s * VHin + vg]);
-            const float bv = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.b)[(size_t)s * VHin + vg]);
-            // log of the reference's decay exp(-exp(A_log) * softplus(a + dt_bias))
-            p.GL[(size_t)vh * S + s] = -expf(p.A_log[vg]) * softplusf_(av + p.dt_bias[vg]);
-            p.BETA[(size_t)vh * S + s] = sigmoidf_(bv);
-        }
+        if (lane < 2)   // local / input-layout V head
+            gdn_gates(p, s, kh * 2 + lane, kg * 2 + lane, VHin, static_cast<const __nv_bfloat16 *>(p.a),
+                      static_cast<const __nv_bfloat16 *>(p.b));
     }
     __syncthreads();
     // K^T of the chunk ([dk][64 tokens], tokens past S zero), row-contiguous

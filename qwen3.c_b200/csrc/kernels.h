@@ -13,6 +13,7 @@ struct GdnDecodeArgs {
     const void *z;        // [B][VH*VD]
     const void *a, *b;    // [B][VH] (fused)
     const float *decay, *beta;  // [B][VH] (prenorm)
+    const float *pdecay, *pbeta;  // [B][VH] given decay / beta (fused; nullptr = from a, b)
     const float *conv_w;  // [CD][4]
     const float *A_log, *dt_bias, *gnorm;
     float *hist;          // [B][3][CD] conv history (fused)
@@ -95,6 +96,8 @@ struct GdnPrefillArgs {
     float *Hs;                            // scratch [nseg][VH][128][128] segment start states
     float *XS;                            // scratch [nseg-1][VH][128][256] segment maps [Phi | Psi]
     int nseg, seglen;                     // chunk segments walked in parallel (1 = one walk)
+    const float *params;                  // [S][pstride] = decay | beta (per input V head) | ..., or nullptr (from a, b)
+    int pstride;
     int S, KH, VH;
     float eps;
     // head-sharded prefill: this call owns K heads [kh0, kh0+KH) (V heads
@@ -107,4 +110,19 @@ struct GdnPrefillMaps {
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st);
+}  // namespace coli
+
+namespace coli {
+// ---------------------------------------------------------------- dense projections
+struct LinearArgs {
+    void *y;              // [S][O] fp32 or bf16 (y_bf16)
+    float *part;          // split-K partials [splits][S][O] (nullptr = no split)
+    int S, I, O;
+    int kchunks;          // 64-element K chunks per split (set by launch_linear)
+    int y_bf16;
+};
+cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
+                          cudaStream_t st);
+cudaError_t launch_f32_to_bf16(const float *x, __nv_bfloat16 *y, size_t n, cudaStream_t st);
+int linear_pick_bn(int S);
 }  // namespace coli

@@ -1,0 +1,177 @@
+// Dense projections on the 5th-gen tensor core: y[s][o] = sum_i x[s][i] W[o][i]
+// (the reference's matmul(), c/qwen.c:178-189, with W [O][I] row-major as the
+// engine stores it). bf16 W and x, fp32 accumulation in TMEM.
+//
+// One CTA = 128 output features x BN tokens (BN = 16..256 by S, so decode with
+// a handful of tokens is a weight-streaming pass), K walked in 64-element
+// (128 B) steps through a 4-stage TMA ring. W is the M operand (K-major rows),
+// x the N operand (K-major rows); both 128B-swizzled. When the output tiles
+// cannot fill the GPU (decode), K is split over blockIdx.z and the partial sums
+// are added in split order by linear_reduce_kernel (deterministic).
+// Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 = epilogue
+// (TMEM lane = output feature; stores are contiguous along o for each token).
+#include "common.cuh"
+#include "kernels.h"
+#include "tc05.cuh"
+
+namespace coli {
+
+constexpr int LN_BM = 128, LN_BK = 64, LN_STAGES = 4;
+constexpr int LN_A_BYTES = LN_BM * LN_BK * 2;   // 16 KiB
+
+template <int BN> struct LinSmem {
+    static constexpr int B_BYTES = BN * LN_BK * 2;
+    static constexpr int STAGE = LN_A_BYTES + B_BYTES;
+    static constexpr int TOTAL = LN_STAGES * STAGE + 1024;
+    static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, LinearArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[LN_STAGES], empty[LN_STAGES], done;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int o0 = blockIdx.x * LN_BM, s0 = blockIdx.y * BN, z = blockIdx.z;
+    const int nk = (a.I + LN_BK - 1) / LN_BK;
+    const int k0 = z * a.kchunks, k1 = min(nk, k0 + a.kchunks), cnt = max(0, k1 - k0);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < LN_STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        mbar_init(&done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tc::alloc(&tmem_base, LinSmem<BN>::TMEM_COLS);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tD = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmW); tma_prefetch_desc(&tmX);
+            for (int i = 0; i < cnt; ++i) {
+                const int st = i % LN_STAGES;
+                if (i >= LN_STAGES) mbar_wait(&empty[st], ((i / LN_STAGES) + 1) & 1);
+                uint8_t *sA = sm + st * LinSmem<BN>::STAGE, *sB = sA + LN_A_BYTES;
+                mbar_expect_tx(&full[st], LinSmem<BN>::STAGE);
+                tma_load_2d(sA, &tmW, (k0 + i) * LN_BK, o0, &full[st]);
+                tma_load_2d(sB, &tmX, (k0 + i) * LN_BK, s0, &full[st]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_bf16(LN_BM, BN, 0, 0);
+            const uint32_t base = smem_u32(sm);
+            for (int i = 0; i < cnt; ++i) {
+                const int st = i % LN_STAGES;
+                mbar_wait(&full[st], (i / LN_STAGES) & 1);
+                tc::fence_after();
+                const uint32_t aA = base + st * LinSmem<BN>::STAGE, aB = aA + LN_A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < LN_BK / 16; ++kk)
+                    tc::mma_bf16(tD, tc::desc_k_sw128(aA + kk * 32), tc::desc_k_sw128(aB + kk * 32), idesc,
+                                 (i > 0 || kk > 0) ? 1u : 0u);
+                tc::commit(&empty[st]);
+            }
+            tc::commit(&done);
+        }
+    } else {
+        const int q = warp & 3, o = o0 + q * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        if (cnt > 0) {
+            mbar_wait(&done, 0);
+            tc::fence_after();
+        }
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            if (cnt > 0) {
+                tc::ld16(tD + lane_off + c0, v);
+                tc::wait_ld();
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            }
+            if (o < a.O) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int s = s0 + c0 + j;
+                    if (s >= a.S) break;
+                    const size_t idx = (size_t)s * a.O + o;
+                    if (a.part) a.part[(size_t)z * a.S * a.O + idx] = v[j];
+                    else if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[idx] = __float2bfloat16_rn(v[j]);
+                    else static_cast<float *>(a.y)[idx] = v[j];
+                }
+            }
+        }
+        tc::fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after();
+        tc::dealloc(tmem_base, LinSmem<BN>::TMEM_COLS);
+    }
+}
+
+// y = sum over splits of the partials, in split order.
+__global__ void linear_reduce_kernel(LinearArgs a, int splits)
+{
+    const size_t n = (size_t)a.S * a.O;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int z = 0; z < splits; ++z) acc += a.part[(size_t)z * n + i];
+        if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[i] = __float2bfloat16_rn(acc);
+        else static_cast<float *>(a.y)[i] = acc;
+    }
+}
+
+// fp32 -> bf16, n elements (n a multiple of 4 is not required).
+__global__ void f32_to_bf16_kernel(const float *x, __nv_bfloat16 *y, size_t n)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+cudaError_t launch_f32_to_bf16(const float *x, __nv_bfloat16 *y, size_t n, cudaStream_t st)
+{
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 4096);
+    f32_to_bf16_kernel<<<blocks, 256, 0, st>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+int linear_pick_bn(int S)
+{
+    return S <= 16 ? 16 : S <= 32 ? 32 : S <= 64 ? 64 : S <= 128 ? 128 : 256;
+}
+
+cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
+                          cudaStream_t st)
+{
+    const int nk = (a.I + LN_BK - 1) / LN_BK;
+    a.kchunks = (nk + splits - 1) / splits;
+    dim3 grid((a.O + LN_BM - 1) / LN_BM, (a.S + bn - 1) / bn, splits);
+    auto run = [&](auto kern, int smem) -> cudaError_t {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, 192, smem, st>>>(tmW, tmX, a);
+        return cudaGetLastError();
+    };
+    cudaError_t e;
+    switch (bn) {
+    case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL); break;
+    case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL); break;
+    case 64: e = run(linear_kernel<64>, LinSmem<64>::TOTAL); break;
+    case 128: e = run(linear_kernel<128>, LinSmem<128>::TOTAL); break;
+    case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL); break;
+    default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess || splits == 1) return e;
+    const size_t n = (size_t)a.S * a.O;
+    linear_reduce_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(a, splits);
+    return cudaGetLastError();
+}
+
+}  // namespace coli

@@ -1,0 +1,135 @@
+"""Block-level entry points (projections + mixer + out-projection) on the GPU
+against the fp32 CPU path: numpy fp32 projections (the reference's matmul(),
+c/qwen.c:178-189) around the C oracle, and where the reference harness was
+built, the reference's own attention() / gdn_step() with the same weights."""
+import numpy as np
+import pytest
+
+from conftest import load_pkg
+from helpers import (CD, CONVK, KD, KH, KH_G, H, HD, VD, VH_G, assert_close, gdn_params, gdn_state0,
+                     rel_l2)
+from oracle import Oracle, Reference
+import synth
+
+pytestmark = pytest.mark.gpu
+D = 2048          # hidden size of the benchmark container
+
+
+@pytest.fixture(scope="module")
+def be():
+    pkg = load_pkg()
+    pkg.build()
+    b = pkg.Backend(0)
+    yield b
+    b.shutdown()
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return Oracle()
+
+
+def _w(cfg, name, O, I, std=0.02):
+    return synth.normal(synth.seed_of(cfg, name), (O, I), std=std)
+
+
+def _dense(be, w, **kw):
+    return load_pkg().coli_cuda.DenseTensor(be, w, **kw)
+
+
+@pytest.mark.parametrize("S", [1, 7, 64, 300])
+def test_linear_vs_bf16_product(be, S):
+    """y = x W^T for O not a multiple of the 128-row tile, decode (split-K)
+    and prefill shapes; the reference product uses the same bf16 operands."""
+    W = _w("lin", "W", 1000, D)
+    x = synth.normal(synth.seed_of("lin", "x", S), (S, D))
+    t = _dense(be, W)
+    y = be.matmul(t, x)
+    ref = synth.bf16_round(x).astype(np.float64) @ synth.bf16_round(W).astype(np.float64).T
+    err = np.max(np.abs(y - ref))
+    assert err <= 1e-4 * np.max(np.abs(ref)) + 1e-6, err
+    t.free()
+
+
+def test_linear_int8_rows(be):
+    rng = np.random.default_rng(5)
+    q = rng.integers(-127, 128, size=(384, D), dtype=np.int8)
+    s = (rng.random(384).astype(np.float32) + 0.5) * 1e-3
+    x = synth.normal(synth.seed_of("lin8", "x"), (3, D))
+    t = _dense(be, q, scales=s, fmt=1)
+    y = be.matmul(t, x)
+    Wd = synth.bf16_round(q.astype(np.float32) * s[:, None])
+    ref = synth.bf16_round(x).astype(np.float64) @ Wd.astype(np.float64).T
+    assert np.max(np.abs(y - ref)) <= 1e-4 * np.max(np.abs(ref)) + 1e-6
+    assert t.nbytes == 384 * D * 2
+    t.free()
+
+
+def test_gqa_block_prefill_then_decode(be, orc):
+    """Prefill 130 rows (tcgen05 path), one decode row, then 5 rows through the
+    split-KV path, all continuing one cache; against fp32 projections around
+    the oracle with an fp32 cache."""
+    cfg = "gqa_block"
+    Wq, Wk, Wv = _w(cfg, "q", H * 2 * HD, D), _w(cfg, "k", KH * HD, D), _w(cfg, "v", KH * HD, D)
+    Wo = _w(cfg, "o", D, H * HD)
+    qnw = synth.normal(synth.seed_of(cfg, "qn"), (HD,), std=0.1)
+    knw = synth.normal(synth.seed_of(cfg, "kn"), (HD,), std=0.1)
+    T = 256
+    layer = 8
+    be.kv_ensure(layer, 1, KH, T)
+    be.gqa_norm_weight(layer, qnw, knw)
+    tq, tk, tv, to = (_dense(be, w) for w in (Wq, Wk, Wv, Wo))
+    Kc = np.zeros((KH, T, HD), np.float32)
+    Vc = np.zeros_like(Kc)
+    ref = Reference(path=None) if Reference.available() else None
+    Kr, Vr = np.zeros_like(Kc), np.zeros_like(Kc)
+    pos = 0
+    for S in (130, 1, 5):
+        x = synth.normal(synth.seed_of(cfg, "x", pos), (S, D))
+        got = be.gqa_full(layer, x, tq, tk, tv, to, pos, max_t=T)
+        qg = (x @ Wq.T).reshape(S, H, 2 * HD)
+        k = (x @ Wk.T).reshape(S, KH, HD)
+        v = (x @ Wv.T).reshape(S, KH, HD)
+        orc.gqa_prologue(qg, k, v, qnw, knw, pos, Kc, Vc)
+        ctx = orc.gqa_attend(qg, Kc, Vc, pos)
+        want = ctx.reshape(S, H * HD) @ Wo.T
+        assert_close(got, want, what=f"gqa block S={S} pos={pos}")
+        if ref is not None:   # the reference's own attention() on the same weights
+            rout = ref.attention(x, pos, H, KH, HD, Wq, Wk, Wv, Wo, qnw, knw, Kr, Vr)
+            assert_close(got, rout, what=f"gqa block vs reference S={S}")
+        pos += S
+    for t in (tq, tk, tv, to):
+        t.free()
+
+
+@pytest.mark.parametrize("S", [1, 20, 100])
+def test_gdn_block_vs_oracle(be, orc, S):
+    """in_proj_qkv / in_proj_z -> conv + delta rule + gated norm -> out_proj
+    with the engine's params packing (decay | beta | gnorm), from a nonzero
+    carried state; S = 1 is coli_cuda_gdn_full, 20 the token-stepped sequence,
+    100 the chunk-parallel prefill."""
+    cfg = f"gdn_block_{S}"
+    prm = gdn_params(cfg)
+    state, ring = gdn_state0(cfg)
+    Wqkv, Wz = _w(cfg, "qkv", CD, D), _w(cfg, "z", VH_G * VD, D)
+    Wa, Wb, Wo = _w(cfg, "a", VH_G, D), _w(cfg, "b", VH_G, D), _w(cfg, "o", D, VH_G * VD)
+    x = synth.normal(synth.seed_of(cfg, "x"), (S, D))
+    a, b = x @ Wa.T, x @ Wb.T
+    sp = np.where(a + prm["dt_bias"] > 20, a + prm["dt_bias"], np.log1p(np.exp(a + prm["dt_bias"])))
+    decay = np.exp(-np.exp(prm["A_log"]) * sp).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-b))).astype(np.float32)
+    params = np.concatenate([decay, beta, np.broadcast_to(prm["gnorm"], (S, VD))], axis=1)
+    layer = 12 + S % 7
+    be.gdn_setup(layer, 1, prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"])
+    be.gdn_state_set(layer, 0, state)
+    be.gdn_conv_set(layer, 0, ring)
+    tqkv, tz, to = _dense(be, Wqkv), _dense(be, Wz), _dense(be, Wo)
+    got = be.gdn_full_seq(layer, x, params, tqkv, tz, to)
+    s_ref, r_ref = state.copy(), ring.copy()
+    y = orc.gdn_seq(x @ Wqkv.T, x @ Wz.T, a, b, prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"],
+                    r_ref, s_ref, KH=KH_G, KD=KD)
+    want = y.reshape(S, VH_G * VD) @ Wo.T
+    assert_close(got, want, what=f"gdn block S={S}")
+    assert rel_l2(be.gdn_state_get(layer, 0), s_ref) <= 1e-2
+    for t in (tqkv, tz, to):
+        t.free()
