@@ -228,7 +228,7 @@ def run_ours(args, ws, rank, local):
     if args.only:  # one secondary leg alone (profiling runs)
         fn = {"gdn": run_gdn_secondary, "prefill": run_prefill_secondary,
               "gdnprefill": run_gdn_prefill_secondary, "stack": run_stack_decode,
-              "stackprefill": run_stack_prefill}[args.only]
+              "stackprefill": run_stack_prefill, "linear": run_linear}[args.only]
         res = fn(be, args, st, peak_tc if args.only in ("prefill", "stackprefill") else peak_hbm)
         if rank == 0:
             print(json.dumps(res))
@@ -568,6 +568,46 @@ def run_stack_decode(be, args, st, peak_hbm):
         "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm, "steps": n}}
 
 
+def run_linear(be, args, st, peak_hbm):
+    """Dense projections of one block (hidden 2048, BASELINE config 1 shapes) on
+    the tcgen05 linear kernel: decode (S = 1, 64: weight streaming, HBM bound)
+    and prefill (S = 4096: tensor bound). Six copies of each weight are
+    rotated so every call streams its weights from HBM (> L2)."""
+    import torch
+    import numpy as np
+    pkg = _pkg()
+    _, peak_tc, _ = _peaks()
+    shapes = {"gqa_q_gate": (8192, 2048), "gqa_o": (2048, 4096), "gdn_qkv": (8192, 2048),
+              "gdn_z": (4096, 2048), "gdn_out": (2048, 4096)}
+    out = {}
+    rng = np.random.default_rng(3)
+    for name, (O, I) in shapes.items():
+        ts = [pkg.coli_cuda.DenseTensor(be, (rng.standard_normal((O, I), dtype=np.float32) * 0.02))
+              for _ in range(6)]
+        for S in (1, 64, 4096):
+            x = torch.randn(S, I, device="cuda").bfloat16()
+            y = torch.empty(S, O, device="cuda", dtype=torch.bfloat16)
+            for i in range(6):
+                be.matmul_dev(ts[i], x.data_ptr(), S, y.data_ptr(), 1)
+            reps = 30 if S < 4096 else 10
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            be.sync()
+            e0.record(st)
+            for i in range(reps):
+                be.matmul_dev(ts[i % 6], x.data_ptr(), S, y.data_ptr(), 1)
+            e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            wbytes = O * I * 2 + S * (I + O) * 2
+            out[f"{name}_S{S}"] = {"O": O, "I": I, "S": S, "us": us,
+                                   "GBs": wbytes / us / 1e3, "frac_of_hbm": wbytes / us / 1e3 / peak_hbm,
+                                   "TFLOPs": 2.0 * S * O * I / us / 1e6,
+                                   "frac_of_bf16": 2.0 * S * O * I / us / 1e6 / peak_tc}
+        for t in ts:
+            t.free()
+    return {"linear": out}
+
+
 def run_stack_prefill(be, args, st, peak_tc):
     """BASELINE config 5 (ii): prefill of one 32k-token prompt through the
     40-layer mixer stack, heads sharded over the GPUs, each layer's output
@@ -609,7 +649,7 @@ def main():
     ap.add_argument("--context", type=int, default=T_CTX, help="decode context length")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e / secondary / CPU legs), for profiling")
-    ap.add_argument("--only", choices=["gdn", "prefill", "gdnprefill", "stack", "stackprefill"],
+    ap.add_argument("--only", choices=["gdn", "prefill", "gdnprefill", "stack", "stackprefill", "linear"],
                     default=None,
                     help="run one secondary leg alone and print its JSON (profiling)")
     ap.add_argument("--lengths", default="8192,32768", help="prefill lengths of the secondary legs")

@@ -229,6 +229,10 @@ size_t coli_cuda_tensor_bytes(const ColiCudaTensor *t);
 int  coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const void *w,
                       const float *scales, int fmt, int S, int I, int O, int gs);
 
+/* Device-pointer form: x bf16 [S][I] (16-byte aligned), y [S][O] fp32
+ * (y_bf16 = 0) or bf16 (1), asynchronous on the backend stream. */
+int  coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, void *y, int y_bf16);
+
 /* Whole gated-GQA block for S rows of request 0 (coli_vk_gqa_full,
  * c/backend_vulkan.h:173-177; CPU c/qwen.c:595-665): q|gate, k, v
  * projections -> q/k norm + RoPE + KV append -> causal attention -> gate ->

@@ -73,6 +73,7 @@ SIGNATURES = {
     "coli_cuda_tensor_free": ([_vp], None),
     "coli_cuda_tensor_bytes": ([_vp], ctypes.c_size_t),
     "coli_cuda_matmul": ([ctypes.POINTER(_vp), _fp, _fp, _vp, _fp] + [_i] * 5, _i),
+    "coli_cuda_matmul_dev": ([_vp, _vp, _i, _vp, _i], _i),
     "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
     "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
@@ -389,7 +390,11 @@ def _block_methods():
         self._ok(rc, "gdn_full")
         return out
 
-    for f in (matmul, gqa_full, gdn_full_seq):
+    def matmul_dev(self, t, x, S, y, y_bf16=0):
+        """Device pointers: x bf16 [S][I], y [S][O]."""
+        self._ok(self.lib.coli_cuda_matmul_dev(t.h, x, S, y, y_bf16), "matmul_dev")
+
+    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq):
         setattr(Backend, f.__name__, f)
 
 

@@ -136,6 +136,14 @@ int coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const vo
     return check_dev_error();
 }
 
+int coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, void *y, int y_bf16)
+{
+    READY();
+    if (S < 1 || !x || !y) return fail("bad matmul_dev arguments");
+    if (reinterpret_cast<uintptr_t>(x) & 15) return fail("x must be 16-byte aligned");
+    return linear_dev(tensor, static_cast<const __nv_bfloat16 *>(x), S, y, y_bf16);
+}
+
 int coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
                        ColiCudaTensor *gv_t, ColiCudaTensor *out_t, float *out, int S, int H, int KH, int hd,
                        int rot, int pos_base, int max_t, float eps, float theta, int Dout)
