@@ -133,6 +133,14 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // ---------------------------------------------------------------- scalar math
 // The reference's scalar helpers (c/qwen.c:172-175), evaluated with CUDA's
 // IEEE-accurate expf/log1pf (no fast-math anywhere in this library).
+// 2^x with the MUFU instruction (relative error ~2^-22, -inf -> 0), for
+// softmax probabilities and decay factors where one instruction matters.
+__device__ __forceinline__ float ex2_approx(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float siluf_(float x) { return x / (1.f + expf(-x)); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(expf(x)); }

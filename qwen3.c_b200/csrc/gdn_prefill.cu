@@ -253,7 +253,7 @@ size_t gdn_prologue_tile_smem()
 {
     return (size_t)PRO_T * PRT_CH * 2 + 3 * PRT_CH * 4 + PRT_CH * 16 + PFG_D * PRT_KT_LD * 4;
 }
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)   // two CTAs per SM: at most 128 registers
 gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -384,16 +384,17 @@ constexpr int PREP_LD = 68;  // padded row stride (floats) of A / T in shared me
 constexpr int PREP_THREADS = 256;
 __global__ void __launch_bounds__(PREP_THREADS)
 gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, GdnPrefillArgs p)
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKT,
+                   GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *sQV = base;                          // Q chunk, later V chunk [64 x 128] swizzled
-    float *sK = sQV + PFG_C * PFG_D;            // K chunk
+    float *sK = sQV + PFG_C * PFG_D;            // K chunk, later K^T [128 x 64] swizzled
     float *sA = sK + PFG_C * PFG_D;             // [64][68] strictly lower A
     float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1
     float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
-    __shared__ float G[PFG_C], bet[PFG_C];
+    __shared__ float G[PFG_C], bet[PFG_C], bgam[PFG_C];   // bgam = beta e^G
     __shared__ __align__(8) uint64_t bar_qk, bar_v;
 
     const int n = blockIdx.x, h = blockIdx.y, kh = h >> 1;
@@ -419,6 +420,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             bet[i] = (s0 + i < p.S) ? p.BETA[(size_t)h * p.S + s0 + i] : 0.f;
     }
     __syncthreads();
+    if (tid < PFG_C) bgam[tid] = bet[tid] * expf(G[tid]);   // read after later barriers
     mbar_wait(&bar_qk, 0);  // a time-out raises the device error word
 
     // K K^T (warps 0-3) or Q K^T (warps 4-7) for this warp's 16 rows, all 64 columns
@@ -446,20 +448,29 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = r0 + g + ((e >> 1) << 3), j = nt * 8 + 2 * tq + (e & 1);
-                const float dec = expf(G[i] - G[j]);
-                if (second) Mg[i * PFG_C + j] = j <= i ? tf32r(dec * acc[nt][e]) : 0.f;
-                else sA[i * PREP_LD + j] = j < i ? bet[i] * dec * acc[nt][e] : 0.f;
+            for (int hr = 0; hr < 2; ++hr) {
+                const int i = r0 + g + 8 * hr, j = nt * 8 + 2 * tq;
+                const float d0 = ex2_approx((G[i] - G[j]) * 1.4426950408889634f);
+                const float d1 = ex2_approx((G[i] - G[j + 1]) * 1.4426950408889634f);
+                const float v0 = acc[nt][2 * hr], v1 = acc[nt][2 * hr + 1];
+                if (second) {
+                    *reinterpret_cast<float2 *>(Mg + i * PFG_C + j) =
+                        make_float2(j <= i ? tf32r(d0 * v0) : 0.f, j + 1 <= i ? tf32r(d1 * v1) : 0.f);
+                } else {
+                    sA[i * PREP_LD + j] = j < i ? bet[i] * d0 * v0 : 0.f;
+                    sA[i * PREP_LD + j + 1] = j + 1 < i ? bet[i] * d1 * v1 : 0.f;
+                }
             }
         }
     }
     __syncthreads();
-    // V replaces Q in shared memory while T is solved
+    // V replaces Q and K^T replaces K in shared memory while T is solved
     if (tid == 0) {
         fence_proxy_async();
-        mbar_expect_tx(&bar_v, PFG_C * PFG_D * 4);
+        mbar_expect_tx(&bar_v, 2 * PFG_C * PFG_D * 4);
         for (int c = 0; c < 4; ++c) tma_load_3d(sQV + c * PFG_C * 32, &tmV, 32 * c, s0, h, &bar_v);
+        const int nch = (p.S + PFG_C - 1) / PFG_C;
+        for (int c = 0; c < 2; ++c) tma_load_3d(sK + c * PFG_D * 32, &tmKT, 32 * c, 0, kh * nch + n, &bar_v);
     }
     // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
     // diagonal blocks by forward substitution (one column per thread), then
@@ -467,36 +478,49 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     {
         for (int e = tid; e < PFG_C * PFG_C; e += PREP_THREADS) sT[(e >> 6) * PREP_LD + (e & 63)] = 0.f;
         __syncthreads();
-        if (tid < 64) {
+        if (tid < 64) {   // column c of diagonal block o, kept in registers
             const int o = (tid >> 4) * 16, c = tid & 15;
-            for (int i = c; i < 16; ++i) {
+            float t[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                // t[j] = 0 for j < c, so the sum may run over every j < i
                 float acc = (i == c) ? 1.f : 0.f;
-                for (int j = c; j < i; ++j) acc -= sA[(o + i) * PREP_LD + o + j] * sT[(o + j) * PREP_LD + o + c];
-                sT[(o + i) * PREP_LD + o + c] = acc;
+#pragma unroll
+                for (int j = 0; j < i; ++j) acc -= sA[(o + i) * PREP_LD + o + j] * t[j];
+                t[i] = acc;
             }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sT[(o + i) * PREP_LD + o + c] = t[i];
         }
         __syncthreads();
         for (int dist = 1; dist < 4; ++dist) {
             const int nblk = 4 - dist;                 // blocks (p, p - dist), p = dist..3
-            // X_p = sum_{r=q}^{p-1} A_pr T_rq
-            for (int e = tid; e < nblk * 256; e += PREP_THREADS) {
-                const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
+            // X_p = sum_{r=q}^{p-1} A_pr T_rq; a thread owns 4 adjacent columns
+            for (int e = tid; e < nblk * 64; e += PREP_THREADS) {
+                const int bi = e >> 6, i = (e >> 2) & 15, j = (e & 3) * 4;
                 const int pr = (dist + bi) * 16, q = bi * 16;
-                float acc = 0.f;
-                for (int r = q; r < pr; r += 16)
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) acc += sA[(pr + i) * PREP_LD + r + k] * sT[(r + k) * PREP_LD + q + j];
-                sX[e] = acc;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int k = q; k < pr; ++k) {
+                    const float a = sA[(pr + i) * PREP_LD + k];
+                    const float4 t = *reinterpret_cast<const float4 *>(sT + k * PREP_LD + q + j);
+                    acc.x += a * t.x; acc.y += a * t.y; acc.z += a * t.z; acc.w += a * t.w;
+                }
+                *reinterpret_cast<float4 *>(sX + (bi << 8) + (i << 4) + j) = acc;
             }
             __syncthreads();
             // T_pq = -T_pp X_p
-            for (int e = tid; e < nblk * 256; e += PREP_THREADS) {
-                const int bi = e >> 8, i = (e >> 4) & 15, j = e & 15;
+            for (int e = tid; e < nblk * 64; e += PREP_THREADS) {
+                const int bi = e >> 6, i = (e >> 2) & 15, j = (e & 3) * 4;
                 const int pr = (dist + bi) * 16, q = bi * 16;
-                float acc = 0.f;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) acc += sT[(pr + i) * PREP_LD + pr + k] * sX[(bi << 8) + (k << 4) + j];
-                sT[(pr + i) * PREP_LD + q + j] = -acc;
+                for (int k = 0; k < 16; ++k) {
+                    const float a = sT[(pr + i) * PREP_LD + pr + k];
+                    const float4 x = *reinterpret_cast<const float4 *>(sX + (bi << 8) + (k << 4) + j);
+                    acc.x += a * x.x; acc.y += a * x.y; acc.z += a * x.z; acc.w += a * x.w;
+                }
+                *reinterpret_cast<float4 *>(sT + (pr + i) * PREP_LD + q + j) =
+                    make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
             }
             __syncthreads();
         }
@@ -504,10 +528,11 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     mbar_wait(&bar_v, 0);
 
-    // W = T (beta gamma K) (warps 0-3) or U = T (beta V) (warps 4-7) for this
-    // warp's 16 rows, 128 columns in two halves
+    // W = (T diag(beta gamma)) K (warps 0-3; K^T rows by ldmatrix) or
+    // U = T (diag(beta) V) (warps 4-7) for this warp's 16 rows, 128 columns
+    // in two halves
     float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
-    const float *sB = second ? sQV : sK;
+    const uint32_t aKT = smem_u32(sK);
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
         float w[8][4];
@@ -515,19 +540,34 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
+        if (!second) {
 #pragma unroll 2
-        for (int ks = 0; ks < PFG_C / 8; ++ks) {
-            const int c0 = ks * 8 + tq, c1 = c0 + 4;
-            const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0]), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0]);
-            const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1]), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1]);
-            const float s0 = second ? bet[c0] : bet[c0] * expf(G[c0]);
-            const float s1 = second ? bet[c1] : bet[c1] * expf(G[c1]);
+            for (int ks = 0; ks < PFG_C / 8; ++ks) {
+                const int c0 = ks * 8 + tq, c1 = c0 + 4;
+                const float s0 = bgam[c0], s1 = bgam[c1];
+                const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0] * s0), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0] * s0);
+                const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1] * s1), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1] * s1);
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                const int col = half * 64 + nt * 8 + g;
-                const uint32_t b0 = f2tf32(s0 * sw_ld(sB, PFG_C, c0, col));
-                const uint32_t b1 = f2tf32(s1 * sw_ld(sB, PFG_C, c1, col));
-                mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
+                for (int nt = 0; nt < 8; ++nt) {
+                    uint32_t b0, b1;   // K was rounded to tf32 by the prologue
+                    ldb_sw_rows(aKT, PFG_D, half * 64 + nt * 8, ks, lane, b0, b1);
+                    mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
+                }
+            }
+        } else {
+#pragma unroll 2
+            for (int ks = 0; ks < PFG_C / 8; ++ks) {
+                const int c0 = ks * 8 + tq, c1 = c0 + 4;
+                const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0]), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0]);
+                const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1]), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1]);
+                const float s0 = bet[c0], s1 = bet[c1];
+#pragma unroll
+                for (int nt = 0; nt < 8; ++nt) {
+                    const int col = half * 64 + nt * 8 + g;
+                    const uint32_t b0 = f2tf32(s0 * sw_ld(sQV, PFG_C, c0, col));
+                    const uint32_t b1 = f2tf32(s1 * sw_ld(sQV, PFG_C, c1, col));
+                    mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
+                }
             }
         }
 #pragma unroll
@@ -1024,7 +1064,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(gdn_pf_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_prep_smem());
     if (e != cudaSuccess) return e;
-    gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), PREP_THREADS, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, a);
+    gdn_pf_prep_kernel<<<dim3(nchunks, a.VH), PREP_THREADS, gdn_prep_smem(), st>>>(m.Q, m.K, m.V, m.KT, a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     auto scan = [&](auto kern, size_t smem, int grid) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -34,14 +34,6 @@ constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES;  // 208 KiB
 constexpr int PF_THREADS = 576;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
-// 2^x with the MUFU instruction (relative error ~2^-22, -inf -> 0): one
-// instruction per probability in the softmax, which is issue bound.
-__device__ __forceinline__ float ex2_approx(float x)
-{
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 struct PfBars {
     uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
