@@ -939,7 +939,7 @@ size_t gdn_combine_smem() { return (size_t)(2 * PFG_D * CMB_LD + PFG_D * CMB_NC)
 // head's 128 columns (all in this CTA) and y = Y * rsqrt(mean Y^2 + eps) *
 // gnorm * silu(z).
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmDt,
                   const __grid_constant__ CUtensorMap tmQH, GdnPrefillArgs p)
 {
@@ -961,13 +961,15 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         for (int c = 0; c < 2; ++c) tma_load_3d(sDT + c * PFG_D * 32, &tmDt, 32 * c, 0, n * VH + h, &bar);
         for (int c = 0; c < 2; ++c) tma_load_3d(sQT + c * PFG_D * 32, &tmQH, 32 * c, 0, n * VH + h, &bar);
     }
-    const int r0 = warp * 16, ta = n * PFG_C + r0 + g, tb = ta + 8;
-    float y[16][4];
+    // warp w: token rows 16 (w % 4).., value columns 64 (w / 4)..
+    const int r0 = (warp & 3) * 16, cq = (warp >> 2) * 64;
+    __shared__ float rsum[2][PFG_C];
+    float y[8][4];
     __syncthreads();
     mbar_wait(&bar, 0);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {   // Y starts from QH (element (token, dv) of QH^T)
-        const int col = nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 8; ++nt) {    // Y starts from QH (element (token, dv) of QH^T)
+        const int col = cq + nt * 8 + 2 * tq;
         y[nt][0] = sw_ld(sQT, PFG_D, col, r0 + g);     y[nt][1] = sw_ld(sQT, PFG_D, col + 1, r0 + g);
         y[nt][2] = sw_ld(sQT, PFG_D, col, r0 + g + 8); y[nt][3] = sw_ld(sQT, PFG_D, col + 1, r0 + g + 8);
     }
@@ -977,29 +979,32 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         uint32_t a[4];
         lda_sw(aM, r0, ks, lane, a);
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
+        for (int nt = 0; nt < 8; ++nt) {
             uint32_t b0, b1;
-            ldb_sw_rows(aD, PFG_D, nt * 8, ks, lane, b0, b1);
+            ldb_sw_rows(aD, PFG_D, cq + nt * 8, ks, lane, b0, b1);
             mma_tf32(y[nt], a[0], a[1], a[2], a[3], b0, b1);
         }
     }
     float sa = 0.f, sb = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
+    for (int nt = 0; nt < 8; ++nt) {
         sa += y[nt][0] * y[nt][0] + y[nt][1] * y[nt][1];
         sb += y[nt][2] * y[nt][2] + y[nt][3] * y[nt][3];
     }
     sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
     sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    if (tq == 0) { rsum[warp >> 2][r0 + g] = sa; rsum[warp >> 2][r0 + g + 8] = sb; }
+    __syncthreads();                     // row sums of both column halves; every warp is done with sDT / sQT
+    sa = rsum[0][r0 + g] + rsum[1][r0 + g];
+    sb = rsum[0][r0 + g + 8] + rsum[1][r0 + g + 8];
     const float ra_ = 1.f / sqrtf(sa / VD + p.eps), rb_ = 1.f / sqrtf(sb / VD + p.eps);
     // normalised rows (times gnorm) to shared memory, then the gate and the
     // store row by row so that z loads and y stores are 16-byte vectors
-    __syncthreads();                     // every warp is done with sDT / sQT
     constexpr int YLD = PFG_D + 4;
     float *sY = sDT;                     // [64][YLD] over the D^T / QH^T tiles
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-        const int col = nt * 8 + 2 * tq;
+    for (int nt = 0; nt < 8; ++nt) {
+        const int col = cq + nt * 8 + 2 * tq;
         const float g0 = p.gnorm[col], g1 = p.gnorm[col + 1];
         *reinterpret_cast<float2 *>(sY + (r0 + g) * YLD + col) = make_float2(y[nt][0] * ra_ * g0, y[nt][1] * ra_ * g1);
         *reinterpret_cast<float2 *>(sY + (r0 + g + 8) * YLD + col) = make_float2(y[nt][2] * rb_ * g0, y[nt][3] * rb_ * g1);
@@ -1007,7 +1012,7 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
     __syncthreads();
     const TI *z = static_cast<const TI *>(p.z);
     TO *out = static_cast<TO *>(p.y);
-    for (int e = tid; e < PFG_C * (PFG_D / 8); e += 128) {
+    for (int e = tid; e < PFG_C * (PFG_D / 8); e += 256) {
         const int row = e >> 4, c8 = (e & 15) * 8, tok = n * PFG_C + row;
         if (tok >= S) continue;
         const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + c8;
@@ -1087,7 +1092,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     auto out = [&](auto kern) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_out_smem());
         if (e2 != cudaSuccess) return e2;
-        kern<<<dim3(nchunks, a.VH), 128, gdn_out_smem(), st>>>(m.M, m.Dt, m.QH, a);
+        kern<<<dim3(nchunks, a.VH), 256, gdn_out_smem(), st>>>(m.M, m.Dt, m.QH, a);
         return cudaGetLastError();
     };
     return bf16 ? out(gdn_pf_out_kernel<__nv_bfloat16, __nv_bfloat16>) : out(gdn_pf_out_kernel<float, float>);
