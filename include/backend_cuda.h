@@ -261,6 +261,30 @@ int  coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTen
                             float *out, int KH, int KD, int VH, int VD, int conv_dim,
                             int conv_k, float eps, int Dout);
 
+/* Route tail (the fused residual + post_ln + router epilogue):
+ * coli_vk_layer_norm_weight / coli_vk_moe_route_available /
+ * coli_vk_gqa_full_route / coli_vk_gdn_full_route (c/backend_vulkan.h:180-198).
+ * layer_norm_weight uploads one model layer's in_ln and post_ln (D floats each).
+ * gqa_full_route: x = rmsnorm_zc(resid, in_ln) on the device, the GQA block,
+ * then resid_out = resid + delta, nrm_out = rmsnorm_zc(resid_out, post_ln)
+ * (c/qwen.c:326-330) and pr_out = nrm_out router^T [S][E]; gdn_full_route
+ * takes x_in already normed (the caller computes b/a from it) for one token.
+ * Dout must equal D. */
+int  coli_cuda_moe_route_available(void);
+int  coli_cuda_layer_norm_weight(int layer, const float *in_ln, const float *post_ln, int D);
+int  coli_cuda_gqa_full_route(int layer, const float *resid, int D,
+                              ColiCudaTensor *gq_t, ColiCudaTensor *gk_t, ColiCudaTensor *gv_t,
+                              ColiCudaTensor *out_t, ColiCudaTensor *router, int ln_layer,
+                              float *resid_out, float *nrm_out, float *pr_out,
+                              int S, int H, int KH, int hd, int rot, int pos_base, int max_t,
+                              float eps, float theta, int Dout, int E);
+int  coli_cuda_gdn_full_route(int layer, const float *x_in, const float *resid, int D,
+                              ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t, const float *params,
+                              ColiCudaTensor *out_t, ColiCudaTensor *router, int ln_layer,
+                              float *resid_out, float *nrm_out, float *pr_out,
+                              int KH, int KD, int VH, int VD, int conv_dim, int conv_k,
+                              float eps, int Dout, int E);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,6 +77,11 @@ SIGNATURES = {
     "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
     "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
+    "coli_cuda_moe_route_available": ([], _i),
+    "coli_cuda_layer_norm_weight": ([_i, _fp, _fp, _i], _i),
+    "coli_cuda_gqa_full_route": ([_i, _fp, _i] + [_vp] * 5 + [_i, _fp, _fp, _fp] + [_i] * 7 + [_f, _f, _i, _i], _i),
+    "coli_cuda_gdn_full_route": ([_i, _fp, _fp, _i, _vp, _vp, _fp, _vp, _vp, _i, _fp, _fp, _fp] + [_i] * 6
+                                 + [_f, _i, _i], _i),
 }
 
 
@@ -394,7 +399,40 @@ def _block_methods():
         """Device pointers: x bf16 [S][I], y [S][O]."""
         self._ok(self.lib.coli_cuda_matmul_dev(t.h, x, S, y, y_bf16), "matmul_dev")
 
-    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq):
+    def layer_norm_weight(self, layer, in_ln, post_ln):
+        a, ap = _f32(in_ln)
+        b, bp = _f32(post_ln)
+        self._ok(self.lib.coli_cuda_layer_norm_weight(layer, ap, bp, a.shape[0]), "layer_norm_weight")
+
+    def gqa_full_route(self, layer, resid, gq, gk, gv, go, router, ln_layer, pos_base, H=16, KH=2, hd=256, rot=64,
+                       max_t=None, eps=1e-6, theta=1e7):
+        resid, rp = _f32(resid)
+        S, D = resid.shape
+        ro, nr = np.zeros((S, D), np.float32), np.zeros((S, D), np.float32)
+        pr = np.zeros((S, router.O), np.float32)
+        self._ok(self.lib.coli_cuda_gqa_full_route(layer, rp, D, gq.h, gk.h, gv.h, go.h, router.h, ln_layer,
+                                                   ro.ctypes.data_as(_fp), nr.ctypes.data_as(_fp),
+                                                   pr.ctypes.data_as(_fp), S, H, KH, hd, rot, pos_base,
+                                                   max_t or (pos_base + S), eps, theta, go.O, router.O),
+                 "gqa_full_route")
+        return ro, nr, pr
+
+    def gdn_full_route(self, layer, x_in, resid, params, gqkv, gz, gout, router, ln_layer, KH=16, KD=128, VH=32,
+                       VD=128, eps=1e-6):
+        x_in, xp = _f32(x_in)
+        resid, rp = _f32(resid)
+        params, pp = _f32(params)
+        D = x_in.shape[-1]
+        ro, nr = np.zeros(D, np.float32), np.zeros(D, np.float32)
+        pr = np.zeros(router.O, np.float32)
+        CD = 2 * KH * KD + VH * VD
+        self._ok(self.lib.coli_cuda_gdn_full_route(layer, xp, rp, D, gqkv.h, gz.h, pp, gout.h, router.h, ln_layer,
+                                                   ro.ctypes.data_as(_fp), nr.ctypes.data_as(_fp),
+                                                   pr.ctypes.data_as(_fp), KH, KD, VH, VD, CD, 4, eps, gout.O,
+                                                   router.O), "gdn_full_route")
+        return ro, nr, pr
+
+    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq, layer_norm_weight, gqa_full_route, gdn_full_route):
         setattr(Backend, f.__name__, f)
 
 

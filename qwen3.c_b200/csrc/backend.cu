@@ -61,7 +61,7 @@ struct GdnLayer {
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
             S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_GHS, S_GXS,
-            S_XB, S_PQ, S_PK, S_PV, S_PCTX, S_LPART, S_PAR, S_PY, S_COUNT };
+            S_XB, S_PQ, S_PK, S_PV, S_PCTX, S_LPART, S_PAR, S_PY, S_RX, S_RXO, S_RN, S_RNB, S_RP, S_COUNT };
 
 struct Global {
     int ready = 0;
@@ -75,6 +75,8 @@ struct Global {
     void *slot[S_COUNT] = {};
     size_t slot_bytes[S_COUNT] = {};
     size_t bytes = 0, tensors = 0;
+    float *ln_w[MAX_LAYERS] = {};      // per model layer: [in_ln(D) | post_ln(D)] (route tail)
+    int ln_D[MAX_LAYERS] = {};
     char err[512] = "not initialised";
     EncodeTiledFn encode = nullptr;
 };
@@ -500,6 +502,11 @@ void coli_cuda_shutdown(void)
         dev_free(L.conv_w, (size_t)L.conv_dim * L.conv_k * 4);
         dev_free(L.A_log, (size_t)(2 * L.pVH + L.pVD) * 4);
         L = GdnLayer();
+    }
+    for (int i = 0; i < MAX_LAYERS; ++i) {
+        dev_free(G.ln_w[i], (size_t)2 * G.ln_D[i] * 4);
+        G.ln_w[i] = nullptr;
+        G.ln_D[i] = 0;
     }
     for (int s = 0; s < S_COUNT; ++s) {
         dev_free(G.slot[s], G.slot_bytes[s]);

@@ -144,11 +144,15 @@ int coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, voi
     return linear_dev(tensor, static_cast<const __nv_bfloat16 *>(x), S, y, y_bf16);
 }
 
-int coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
-                       ColiCudaTensor *gv_t, ColiCudaTensor *out_t, float *out, int S, int H, int KH, int hd,
-                       int rot, int pos_base, int max_t, float eps, float theta, int Dout)
+}  // extern "C"
+
+namespace {
+
+// The GQA block on device data: x bf16 [S][D] -> out fp32 [S][Dout].
+int gqa_block_dev(int layer, const __nv_bfloat16 *xb, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
+                  ColiCudaTensor *gv_t, ColiCudaTensor *out_t, float *od, int S, int H, int KH, int hd, int rot,
+                  int pos_base, int max_t, float eps, float theta, int Dout)
 {
-    READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
     if (S < 1 || pos_base < 0) return fail("bad S/pos_base");
     KvLayer &L = G.kv[layer];
@@ -157,41 +161,34 @@ int coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t, C
     if (!tensor_shape(gq_t, D, H * 2 * hd, "q|gate") || !tensor_shape(gk_t, D, KH * hd, "k") ||
         !tensor_shape(gv_t, D, KH * hd, "v") || !tensor_shape(out_t, H * hd, Dout, "o_proj"))
         return 0;
-    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
     auto *qg = (__nv_bfloat16 *)scratch(S_PQ, (size_t)S * H * 2 * hd * 2);
     auto *k = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * KH * hd * 2);
     auto *v = (__nv_bfloat16 *)scratch(S_PV, (size_t)S * KH * hd * 2);
     auto *ctx = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * H * hd * 2);
-    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
-    if (!xb || !qg || !k || !v || !ctx || !od) return 0;
+    if (!qg || !k || !v || !ctx) return 0;
     if (!linear_dev(gq_t, xb, S, qg, 1) || !linear_dev(gk_t, xb, S, k, 1) || !linear_dev(gv_t, xb, S, v, 1))
         return 0;
     if (!coli_cuda_gqa_step_dev(layer, 0, S, pos_base, qg, k, v, ctx, H, KH, hd, rot, eps, theta, 1)) return 0;
-    if (!linear_dev(out_t, ctx, S, od, 0)) return 0;
-    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
-    return check_dev_error();
+    return linear_dev(out_t, ctx, S, od, 0);
 }
 
-// S tokens of one request (request 0), params rows [decay(VH) | beta(VH) | gnorm(VD)].
-static int gdn_full_rows(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
-                         const float *params, ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
-                         int conv_dim, int conv_k, float eps, int Dout)
+// The GDN block on device data (request 0): x bf16 [S][D], params device
+// [S][2*VH+VD] -> out fp32 [S][Dout].
+int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                  const float *pd, ColiCudaTensor *out_t, float *od, int KH, int KD, int VH, int VD, int conv_dim,
+                  int conv_k, float eps, int Dout)
 {
-    READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
-    if (S < 1 || !params) return fail("bad S / params");
+    if (S < 1) return fail("bad S");
     if (conv_k != 4 || conv_dim != 2 * KH * KD + VH * VD) return fail("conv shape %d x %d not supported", conv_k, conv_dim);
     if (!tensor_shape(gqkv_t, D, conv_dim, "in_proj_qkv") || !tensor_shape(gz_t, D, VH * VD, "in_proj_z") ||
         !tensor_shape(out_t, VH * VD, Dout, "out_proj"))
         return 0;
     const int ps = 2 * VH + VD;
-    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
-    const float *pd = (const float *)upload(S_PAR, params, (size_t)S * ps * 4);
     auto *qkv = (__nv_bfloat16 *)scratch(S_PQ, (size_t)S * conv_dim * 2);
     auto *z = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * VH * VD * 2);
     auto *y = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * VH * VD * 2);
-    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
-    if (!xb || !pd || !qkv || !z || !y || !od) return 0;
+    if (!qkv || !z || !y) return 0;
     if (!linear_dev(gqkv_t, xb, S, qkv, 1) || !linear_dev(gz_t, xb, S, z, 1)) return 0;
     if (S >= GDN_CHUNK_MIN_ROWS) {
         if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, y, KH, KD, VH, VD, eps, 1, 0, -1, pd))
@@ -204,7 +201,69 @@ static int gdn_full_rows(int layer, const float *x, int S, int D, ColiCudaTensor
                 return 0;
         }
     }
-    if (!linear_dev(out_t, y, S, od, 0)) return 0;
+    return linear_dev(out_t, y, S, od, 0);
+}
+
+// resid + delta -> resid_out; rmsnorm_zc(., post_ln) -> nrm; router logits;
+// all three read back (the route tail of the Vulkan backend,
+// c/backend_vulkan.c:2378-2406).
+int route_tail(const float *rd, const float *delta, ColiCudaTensor *router, int ln_layer, float *resid_out,
+               float *nrm_out, float *pr_out, int S, int D, int E, float eps)
+{
+    float *xo = (float *)scratch(S_RXO, (size_t)S * D * 4);
+    float *nrm = (float *)scratch(S_RN, (size_t)S * D * 4);
+    auto *nb = (__nv_bfloat16 *)scratch(S_RNB, (size_t)S * D * 2);
+    float *pr = (float *)scratch(S_RP, (size_t)S * E * 4);
+    if (!xo || !nrm || !nb || !pr) return 0;
+    CK(launch_rmsnorm_zc_rows(rd, delta, G.ln_w[ln_layer] + D, xo, nrm, nb, S, D, eps, stream()));
+    g_launches += 1;
+    if (!linear_dev(router, nb, S, pr, 0)) return 0;
+    if (!download(resid_out, xo, (size_t)S * D * 4) || !download(nrm_out, nrm, (size_t)S * D * 4) ||
+        !download(pr_out, pr, (size_t)S * E * 4))
+        return 0;
+    return check_dev_error();
+}
+
+int route_checks(ColiCudaTensor *router, int ln_layer, int D, int Dout, int E)
+{
+    if (ln_layer < 0 || ln_layer >= MAX_LAYERS || !G.ln_w[ln_layer] || G.ln_D[ln_layer] != D)
+        return fail("layer norm weights of layer %d not set for D = %d", ln_layer, D);
+    if (Dout != D) return fail("the residual tail needs Dout == D");
+    return tensor_shape(router, D, E, "router");
+}
+
+}  // namespace
+
+extern "C" {
+
+int coli_cuda_gqa_full(int layer, const float *x, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
+                       ColiCudaTensor *gv_t, ColiCudaTensor *out_t, float *out, int S, int H, int KH, int hd,
+                       int rot, int pos_base, int max_t, float eps, float theta, int Dout)
+{
+    READY();
+    if (S < 1) return fail("bad S");
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!xb || !od) return 0;
+    if (!gqa_block_dev(layer, xb, D, gq_t, gk_t, gv_t, out_t, od, S, H, KH, hd, rot, pos_base, max_t, eps, theta,
+                       Dout))
+        return 0;
+    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
+    return check_dev_error();
+}
+
+static int gdn_full_rows(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                         const float *params, ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
+                         int conv_dim, int conv_k, float eps, int Dout)
+{
+    READY();
+    if (S < 1 || !params) return fail("bad S / params");
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
+    const float *pd = (const float *)upload(S_PAR, params, (size_t)S * (2 * VH + VD) * 4);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!xb || !pd || !od) return 0;
+    if (!gdn_block_dev(layer, xb, S, D, gqkv_t, gz_t, pd, out_t, od, KH, KD, VH, VD, conv_dim, conv_k, eps, Dout))
+        return 0;
     if (!download(out, od, (size_t)S * Dout * 4)) return 0;
     return check_dev_error();
 }
@@ -223,6 +282,67 @@ int coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTens
 {
     return gdn_full_rows(layer, x, S, D, gqkv_t, gz_t, params, out_t, out, KH, KD, VH, VD, conv_dim, conv_k, eps,
                          Dout);
+}
+
+int coli_cuda_moe_route_available(void) { return G.ready; }
+
+int coli_cuda_layer_norm_weight(int layer, const float *in_ln, const float *post_ln, int D)
+{
+    READY();
+    if (layer < 0 || layer >= MAX_LAYERS || D < 1 || !in_ln || !post_ln) return fail("bad layer norm weights");
+    if (G.ln_w[layer] && G.ln_D[layer] != D) {
+        dev_free(G.ln_w[layer], (size_t)2 * G.ln_D[layer] * 4);
+        G.ln_w[layer] = nullptr;
+    }
+    if (!G.ln_w[layer]) {
+        void *d = nullptr;
+        if (!dev_alloc(&d, (size_t)2 * D * 4)) return 0;
+        G.ln_w[layer] = (float *)d;
+        G.ln_D[layer] = D;
+    }
+    CK(cudaMemcpyAsync(G.ln_w[layer], in_ln, (size_t)D * 4, cudaMemcpyHostToDevice, stream()));
+    CK(cudaMemcpyAsync(G.ln_w[layer] + D, post_ln, (size_t)D * 4, cudaMemcpyHostToDevice, stream()));
+    CK(cudaStreamSynchronize(stream()));
+    return 1;
+}
+
+int coli_cuda_gqa_full_route(int layer, const float *resid, int D, ColiCudaTensor *gq_t, ColiCudaTensor *gk_t,
+                             ColiCudaTensor *gv_t, ColiCudaTensor *out_t, ColiCudaTensor *router, int ln_layer,
+                             float *resid_out, float *nrm_out, float *pr_out, int S, int H, int KH, int hd, int rot,
+                             int pos_base, int max_t, float eps, float theta, int Dout, int E)
+{
+    READY();
+    if (S < 1 || !resid || !resid_out || !nrm_out || !pr_out) return fail("bad route arguments");
+    if (!route_checks(router, ln_layer, D, Dout, E)) return 0;
+    const float *rd = (const float *)upload(S_RX, resid, (size_t)S * D * 4);
+    auto *xb = (__nv_bfloat16 *)scratch(S_XB, (size_t)S * D * 2);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!rd || !xb || !od) return 0;
+    // in_ln on the device: the attention input
+    CK(launch_rmsnorm_zc_rows(rd, nullptr, G.ln_w[ln_layer], nullptr, nullptr, xb, S, D, eps, stream()));
+    g_launches += 1;
+    if (!gqa_block_dev(layer, xb, D, gq_t, gk_t, gv_t, out_t, od, S, H, KH, hd, rot, pos_base, max_t, eps, theta,
+                       Dout))
+        return 0;
+    return route_tail(rd, od, router, ln_layer, resid_out, nrm_out, pr_out, S, D, E, eps);
+}
+
+int coli_cuda_gdn_full_route(int layer, const float *x_in, const float *resid, int D, ColiCudaTensor *gqkv_t,
+                             ColiCudaTensor *gz_t, const float *params, ColiCudaTensor *out_t, ColiCudaTensor *router,
+                             int ln_layer, float *resid_out, float *nrm_out, float *pr_out, int KH, int KD, int VH,
+                             int VD, int conv_dim, int conv_k, float eps, int Dout, int E)
+{
+    READY();
+    if (!x_in || !resid || !params || !resid_out || !nrm_out || !pr_out) return fail("bad route arguments");
+    if (!route_checks(router, ln_layer, D, Dout, E)) return 0;
+    const __nv_bfloat16 *xb = upload_bf16(x_in, (size_t)D);
+    const float *rd = (const float *)upload(S_RX, resid, (size_t)D * 4);
+    const float *pd = (const float *)upload(S_PAR, params, (size_t)(2 * VH + VD) * 4);
+    float *od = (float *)scratch(S_PY, (size_t)Dout * 4);
+    if (!xb || !rd || !pd || !od) return 0;
+    if (!gdn_block_dev(layer, xb, 1, D, gqkv_t, gz_t, pd, out_t, od, KH, KD, VH, VD, conv_dim, conv_k, eps, Dout))
+        return 0;
+    return route_tail(rd, od, router, ln_layer, resid_out, nrm_out, pr_out, 1, D, E, eps);
 }
 
 }  // extern "C"

@@ -125,4 +125,7 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
                           cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float *x, __nv_bfloat16 *y, size_t n, cudaStream_t st);
 int linear_pick_bn(int S);
+cudaError_t launch_rmsnorm_zc_rows(const float *x, const float *delta, const float *w, float *sum_out,
+                                   float *nrm_out, __nv_bfloat16 *nrm_bf16, int S, int D, float eps,
+                                   cudaStream_t st);
 }  // namespace coli

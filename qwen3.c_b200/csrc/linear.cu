@@ -175,3 +175,52 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
 }
 
 }  // namespace coli
+
+namespace coli {
+// ---------------------------------------------------------------- norm / residual tail
+// Zero-centred RMSNorm of one row (c/qwen.c:326-330: x * rsqrt(mean x^2 + eps)
+// * (1 + w)), one CTA of 256 threads per row; with `delta` the row is first
+// resid + delta (the residual add of the route tail), written to `sum_out`.
+// The normed row goes out in fp32 (optional) and bf16 (the next projection's
+// input).
+__global__ void __launch_bounds__(256)
+rmsnorm_zc_rows_kernel(const float *x, const float *delta, const float *w, float *sum_out, float *nrm_out,
+                       __nv_bfloat16 *nrm_bf16, int D, float eps)
+{
+    const size_t row = blockIdx.x;
+    const float *xr = x + row * D;
+    const float *dr = delta ? delta + row * D : nullptr;
+    __shared__ float red[8];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += 256) {
+        float v = xr[i];
+        if (dr) {
+            v += dr[i];
+            sum_out[row * D + i] = v;
+        }
+        ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[k];
+    const float r = 1.f / sqrtf(tot / D + eps);
+    for (int i = threadIdx.x; i < D; i += 256) {
+        const float v = dr ? sum_out[row * D + i] : xr[i];
+        const float o = v * r * (1.f + w[i]);
+        if (nrm_out) nrm_out[row * D + i] = o;
+        if (nrm_bf16) nrm_bf16[row * D + i] = __float2bfloat16_rn(o);
+    }
+}
+
+cudaError_t launch_rmsnorm_zc_rows(const float *x, const float *delta, const float *w, float *sum_out,
+                                   float *nrm_out, __nv_bfloat16 *nrm_bf16, int S, int D, float eps,
+                                   cudaStream_t st)
+{
+    rmsnorm_zc_rows_kernel<<<S, 256, 0, st>>>(x, delta, w, sum_out, nrm_out, nrm_bf16, D, eps);
+    return cudaGetLastError();
+}
+}  // namespace coli

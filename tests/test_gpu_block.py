@@ -133,3 +133,81 @@ def test_gdn_block_vs_oracle(be, orc, S):
     assert rel_l2(be.gdn_state_get(layer, 0), s_ref) <= 1e-2
     for t in (tqkv, tz, to):
         t.free()
+
+
+def _rmsnorm_zc(x, w, eps=1e-6):
+    """c/qwen.c:326-330 (double accumulation of the mean square)."""
+    x = np.asarray(x, np.float32)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    r = (1.0 / np.sqrt((ms + eps).astype(np.float32))).astype(np.float32)
+    return (x * r * (1.0 + w)).astype(np.float32)
+
+
+def test_gqa_route_tail(be, orc):
+    """in_ln on the device, the GQA block, then resid + delta, post_ln and the
+    router logits (coli_cuda_gqa_full_route) for 3 prompt rows."""
+    cfg = "gqa_route"
+    E, S, T, layer, ln_layer = 8, 3, 64, 9, 3
+    Wq, Wk, Wv = _w(cfg, "q", H * 2 * HD, D), _w(cfg, "k", KH * HD, D), _w(cfg, "v", KH * HD, D)
+    Wo, Wr = _w(cfg, "o", D, H * HD), _w(cfg, "r", E, D)
+    qnw = synth.normal(synth.seed_of(cfg, "qn"), (HD,), std=0.1)
+    knw = synth.normal(synth.seed_of(cfg, "kn"), (HD,), std=0.1)
+    in_ln = synth.normal(synth.seed_of(cfg, "in"), (D,), std=0.1)
+    post_ln = synth.normal(synth.seed_of(cfg, "post"), (D,), std=0.1)
+    resid = synth.normal(synth.seed_of(cfg, "resid"), (S, D))
+    be.kv_ensure(layer, 1, KH, T)
+    be.gqa_norm_weight(layer, qnw, knw)
+    be.layer_norm_weight(ln_layer, in_ln, post_ln)
+    ts = [_dense(be, w) for w in (Wq, Wk, Wv, Wo, Wr)]
+    ro, nr, pr = be.gqa_full_route(layer, resid, *ts[:4], ts[4], ln_layer, 0, max_t=T)
+    x = _rmsnorm_zc(resid, in_ln)
+    qg = (x @ Wq.T).reshape(S, H, 2 * HD)
+    k = (x @ Wk.T).reshape(S, KH, HD)
+    v = (x @ Wv.T).reshape(S, KH, HD)
+    Kc = np.zeros((KH, T, HD), np.float32)
+    Vc = np.zeros_like(Kc)
+    orc.gqa_prologue(qg, k, v, qnw, knw, 0, Kc, Vc)
+    delta = orc.gqa_attend(qg, Kc, Vc, 0).reshape(S, H * HD) @ Wo.T
+    want_ro = resid + delta
+    want_nr = _rmsnorm_zc(want_ro, post_ln)
+    assert_close(ro, want_ro, what="resid_out")
+    assert_close(nr, want_nr, what="nrm_out")
+    assert_close(pr, want_nr @ Wr.T, what="router logits")
+    for t in ts:
+        t.free()
+
+
+def test_gdn_route_tail(be, orc):
+    """One GDN token with the route tail (coli_cuda_gdn_full_route); x_in is
+    the host-normed input the caller also derives b/a from."""
+    cfg = "gdn_route"
+    E, layer, ln_layer = 8, 20, 4
+    prm = gdn_params(cfg)
+    state, ring = gdn_state0(cfg)
+    Wqkv, Wz = _w(cfg, "qkv", CD, D), _w(cfg, "z", VH_G * VD, D)
+    Wa, Wb, Wo, Wr = _w(cfg, "a", VH_G, D), _w(cfg, "b", VH_G, D), _w(cfg, "o", D, VH_G * VD), _w(cfg, "r", E, D)
+    in_ln = synth.normal(synth.seed_of(cfg, "in"), (D,), std=0.1)
+    post_ln = synth.normal(synth.seed_of(cfg, "post"), (D,), std=0.1)
+    resid = synth.normal(synth.seed_of(cfg, "resid"), (1, D))
+    x = _rmsnorm_zc(resid, in_ln)
+    a, b = x @ Wa.T, x @ Wb.T
+    sp = np.where(a + prm["dt_bias"] > 20, a + prm["dt_bias"], np.log1p(np.exp(a + prm["dt_bias"])))
+    decay = np.exp(-np.exp(prm["A_log"]) * sp).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-b))).astype(np.float32)
+    params = np.concatenate([decay, beta, prm["gnorm"][None, :]], axis=1)
+    be.gdn_setup(layer, 1, prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"])
+    be.gdn_state_set(layer, 0, state)
+    be.gdn_conv_set(layer, 0, ring)
+    be.layer_norm_weight(ln_layer, in_ln, post_ln)
+    ts = [_dense(be, w) for w in (Wqkv, Wz, Wo, Wr)]
+    ro, nr, pr = be.gdn_full_route(layer, x[0], resid[0], params[0], ts[0], ts[1], ts[2], ts[3], ln_layer)
+    s_ref, r_ref = state.copy(), ring.copy()
+    y = orc.gdn_seq(x @ Wqkv.T, x @ Wz.T, a, b, prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"],
+                    r_ref, s_ref, KH=KH_G, KD=KD)
+    want_ro = resid[0] + (y.reshape(1, VH_G * VD) @ Wo.T)[0]
+    want_nr = _rmsnorm_zc(want_ro, post_ln)
+    assert_close(ro, want_ro, what="resid_out")
+    assert_close(nr, want_nr, what="nrm_out")
+    assert_close(pr, want_nr @ Wr.T, what="router logits")
+    for t in ts:
+        t.free()
