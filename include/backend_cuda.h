@@ -285,6 +285,22 @@ int  coli_cuda_gdn_full_route(int layer, const float *x_in, const float *resid, 
                               int KH, int KD, int VH, int VD, int conv_dim, int conv_k,
                               float eps, int Dout, int E);
 
+/* ==== Snapshot loader (safetensors) ====
+ * The reference's shard index (c/st.h:248-479) and the mixer part of
+ * model_init (c/qwen.c:433-485): st_open indexes every *.safetensors file of
+ * a snapshot directory (name order) and returns a handle (-1 on a missing or
+ * malformed file; offsets, shapes and byte spans are checked before any
+ * read). st_info gives shape / ndim / dtype (0 BF16, 1 F16, 2 F32, 3 I8/U8)
+ * of a named tensor; st_read_f32 converts a float tensor into out (at most
+ * cap elements; returns the element count, -1 on error); st_dense uploads a
+ * 2-D [O][I] weight as a resident dense tensor (BF16 sources exactly). The
+ * st_open / st_info / st_read_f32 / st_close calls need no device. */
+int       coli_cuda_st_open(const char *snap_dir);
+void      coli_cuda_st_close(int handle);
+int       coli_cuda_st_info(int handle, const char *name, long long *shape, int *ndim, int *dtype);
+long long coli_cuda_st_read_f32(int handle, const char *name, float *out, long long cap);
+int       coli_cuda_st_dense(int handle, const char *name, ColiCudaTensor **tensor);
+
 #ifdef __cplusplus
 }
 #endif

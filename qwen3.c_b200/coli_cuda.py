@@ -78,6 +78,11 @@ SIGNATURES = {
     "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_moe_route_available": ([], _i),
+    "coli_cuda_st_open": ([ctypes.c_char_p], _i),
+    "coli_cuda_st_close": ([_i], None),
+    "coli_cuda_st_info": ([_i, ctypes.c_char_p, ctypes.POINTER(ctypes.c_longlong), _ip, _ip], _i),
+    "coli_cuda_st_read_f32": ([_i, ctypes.c_char_p, _fp, ctypes.c_longlong], ctypes.c_longlong),
+    "coli_cuda_st_dense": ([_i, ctypes.c_char_p, ctypes.POINTER(_vp)], _i),
     "coli_cuda_layer_norm_weight": ([_i, _fp, _fp, _i], _i),
     "coli_cuda_gqa_full_route": ([_i, _fp, _i] + [_vp] * 5 + [_i, _fp, _fp, _fp] + [_i] * 7 + [_f, _f, _i, _i], _i),
     "coli_cuda_gdn_full_route": ([_i, _fp, _fp, _i, _vp, _vp, _fp, _vp, _vp, _i, _fp, _fp, _fp] + [_i] * 6

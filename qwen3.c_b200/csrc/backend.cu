@@ -1106,3 +1106,4 @@ int coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const flo
 // Fixed-scratch decode entry point (no device allocation on its path).
 #include "noalloc.cu"
 #include "block.cu"
+#include "container.cu"

@@ -211,3 +211,67 @@ def test_gdn_route_tail(be, orc):
     assert_close(pr, want_nr @ Wr.T, what="router logits")
     for t in ts:
         t.free()
+
+
+def test_snapshot_layers_end_to_end(be, orc, tmp_path):
+    """A two-layer container (layer 0 GatedDeltaNet, layer 1 gated GQA, the
+    benchmark shapes, bf16 weights N(0, 0.02)) written as safetensors, loaded
+    through coli_cuda_st_* into resident tensors, then one prompt of 5 rows
+    through both blocks against fp32 references built from the same stored
+    values."""
+    import json
+    import st_writer
+    snapmod = load_pkg().snapshot
+    cfg = {"hidden_size": D, "num_hidden_layers": 2, "layer_types": ["linear_attention", "full_attention"],
+           "num_attention_heads": H, "num_key_value_heads": KH, "head_dim": HD, "partial_rotary_factor": 0.25,
+           "rope_theta": 1e7, "rms_norm_eps": 1e-6, "linear_num_key_heads": KH_G, "linear_key_head_dim": KD,
+           "linear_num_value_heads": VH_G, "linear_value_head_dim": VD, "linear_conv_kernel_dim": CONVK}
+    c = "snap"
+    prm = gdn_params(c)
+    t = {}
+    for i in (0, 1):
+        t[f"model.layers.{i}.input_layernorm.weight"] = ("F32", synth.normal(synth.seed_of(c, "in", i), (D,), std=0.1))
+        t[f"model.layers.{i}.post_attention_layernorm.weight"] = ("F32", synth.normal(synth.seed_of(c, "po", i), (D,), std=0.1))
+    p0, p1 = "model.layers.0.linear_attn.", "model.layers.1.self_attn."
+    t.update({p0 + "in_proj_qkv.weight": ("BF16", _w(c, "qkv", CD, D)), p0 + "in_proj_z.weight": ("BF16", _w(c, "z", VH_G * VD, D)),
+              p0 + "in_proj_a.weight": ("BF16", _w(c, "a", VH_G, D)), p0 + "in_proj_b.weight": ("BF16", _w(c, "b", VH_G, D)),
+              p0 + "out_proj.weight": ("BF16", _w(c, "o", D, VH_G * VD)),
+              p0 + "conv1d.weight": ("BF16", prm["conv_w"].reshape(CD, 1, CONVK)),
+              p0 + "A_log": ("F32", prm["A_log"]), p0 + "dt_bias": ("F32", prm["dt_bias"]), p0 + "norm.weight": ("F32", prm["gnorm"]),
+              p1 + "q_proj.weight": ("BF16", _w(c, "q", H * 2 * HD, D)), p1 + "k_proj.weight": ("BF16", _w(c, "k", KH * HD, D)),
+              p1 + "v_proj.weight": ("BF16", _w(c, "v", KH * HD, D)), p1 + "o_proj.weight": ("BF16", _w(c, "oo", D, H * HD)),
+              p1 + "q_norm.weight": ("F32", synth.normal(synth.seed_of(c, "qn"), (HD,), std=0.1)),
+              p1 + "k_norm.weight": ("F32", synth.normal(synth.seed_of(c, "kn"), (HD,), std=0.1))})
+    st_writer.write(str(tmp_path / "model-00001-of-00001.safetensors"), t)
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    snap = snapmod.Snapshot(be.lib, str(tmp_path))
+    gdn = snapmod.load_mixer_layer(be, snap, 0, slot=24)
+    gqa = snapmod.load_mixer_layer(be, snap, 1, slot=10, max_t=64)
+    S = 5
+    x = synth.normal(synth.seed_of(c, "x"), (S, D))
+    # GDN layer 0 from zero state and history
+    be.gdn_state_set(24, 0, np.zeros((VH_G, KD, VD), np.float32))
+    be.gdn_conv_set(24, 0, np.zeros((CONVK, CD), np.float32))
+    got = be.gdn_full_seq(24, x, snapmod.gdn_params(gdn, x), gdn["qkv"], gdn["z"], gdn["out"])
+    rd = lambda n: snap.read(n)
+    a, b = x @ rd(p0 + "in_proj_a.weight").T, x @ rd(p0 + "in_proj_b.weight").T
+    s_ref, r_ref = np.zeros((VH_G, KD, VD), np.float32), np.zeros((CONVK, CD), np.float32)
+    y = orc.gdn_seq(x @ rd(p0 + "in_proj_qkv.weight").T, x @ rd(p0 + "in_proj_z.weight").T, a, b,
+                    rd(p0 + "conv1d.weight").reshape(CD, CONVK), prm["A_log"], prm["dt_bias"], prm["gnorm"],
+                    r_ref, s_ref, KH=KH_G, KD=KD)
+    assert_close(got, y.reshape(S, VH_G * VD) @ rd(p0 + "out_proj.weight").T, what="snapshot GDN layer")
+    # GQA layer 1
+    got = be.gqa_full(10, x, gqa["q"], gqa["k"], gqa["v"], gqa["o"], 0, max_t=64)
+    qg = (x @ rd(p1 + "q_proj.weight").T).reshape(S, H, 2 * HD)
+    k = (x @ rd(p1 + "k_proj.weight").T).reshape(S, KH, HD)
+    v = (x @ rd(p1 + "v_proj.weight").T).reshape(S, KH, HD)
+    Kc = np.zeros((KH, 64, HD), np.float32)
+    Vc = np.zeros_like(Kc)
+    orc.gqa_prologue(qg, k, v, rd(p1 + "q_norm.weight"), rd(p1 + "k_norm.weight"), 0, Kc, Vc)
+    want = orc.gqa_attend(qg, Kc, Vc, 0).reshape(S, H * HD) @ rd(p1 + "o_proj.weight").T
+    assert_close(got, want, what="snapshot GQA layer")
+    for lt in (gdn, gqa):
+        for v_ in lt.values():
+            if hasattr(v_, "free"):
+                v_.free()
+    snap.close()
