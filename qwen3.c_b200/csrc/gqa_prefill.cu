@@ -6,16 +6,17 @@
 // sigmoid(gate). The prologue (q/k norm, RoPE, K/V append) runs before this
 // kernel (gqa_prologue_kernel), so the new rows are already in the cache.
 //
-// One CTA = 128 query rows of one Q head. Warp roles (576 threads):
+// One CTA = 128 query rows of one Q head. Warp roles (320 threads):
 //   warp 0      TMA producers (lane 0: Q once, then K; lane 1: V): 64-key
 //               tiles into separate 2-stage K and V rings (128B swizzle).
 //   warp 1      MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
 //               two TMEM score buffers (M=128, N=64, K=256), then
 //               O += P V (M=128, N=256, K=64) with V read MN-major.
-//   warps 2..17 softmax: four threads per query row (TMEM lane), scores read
-//               with tcgen05.ld, causal mask, online softmax in the log2
-//               domain with lazy rescaling (O is corrected in TMEM only when
-//               the running max grows by more than 2^8), P written to shared
+//   warps 2..9  softmax: 16 query rows per warp read with the 16x256b TMEM
+//               shape (a lane quad per row, so row max and sum are quad
+//               shuffles), causal mask, online softmax in the log2 domain
+//               with lazy rescaling (O is corrected in TMEM only when the
+//               running max grows by more than 2^8), P written to shared
 //               memory in the UMMA K-major layout; final epilogue O / l *
 //               sigmoid(gate).
 // TMEM: 2 x 64 columns of scores + 256 columns of O (512 allocated).
@@ -31,16 +32,15 @@ constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB
 constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 32 KiB per K (or V) tile
 constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 16 KiB
 constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES;  // 208 KiB
-constexpr int PF_THREADS = 576;
+constexpr int PF_SOFTMAX = 256;                    // softmax / epilogue threads
+constexpr int PF_THREADS = 64 + PF_SOFTMAX;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 
 struct PfBars {
     uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
-    // per-tile row max of each half (double-buffered by tile parity); after
-    // the loop the buffer the last tile did not use carries the row sums
-    float mx[2][4][PF_BM];
+    float lsum[PF_BM];        // final row sums for the epilogue
 };
 constexpr int PF_SMEM = PF_DATA + (int)sizeof(PfBars);
 static_assert(PF_SMEM <= 232448, "prefill shared memory exceeds the 227 KiB per-CTA limit");
@@ -84,8 +84,8 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_init(&bars.k_empty[i], 1);
             mbar_init(&bars.v_empty[i], 1);
             mbar_init(&bars.s_full[i], 1);
-            mbar_init(&bars.s_free[i], 512);
-            mbar_init(&bars.p_full[i], 512);
+            mbar_init(&bars.s_free[i], PF_SOFTMAX);
+            mbar_init(&bars.p_full[i], PF_SOFTMAX);
             mbar_init(&bars.pv_done[i], 1);
         }
         fence_mbar_init();
@@ -168,111 +168,124 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     } else {
         // ------------------------------------------------ softmax + epilogue
-        // Four threads per query row: warp w (2..17) takes score columns
-        // 16q..16q+15 and O columns 64q..64q+63 with q = (w-2)/4, of TMEM lanes
-        // 32(w%4).. Row maxima are exchanged through shared memory under a
-        // named barrier of the 512 softmax threads. Waits never break out of
-        // the loop (a time-out raises the error word and the loop runs on), so
-        // every thread meets every named barrier.
-        const int qr = (warp - 2) >> 2;
-        const int row = 32 * (warp & 3) + lane;            // TMEM lane == query row in tile
-        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-        const int srow = q0 + row;                         // query row index in [0, S)
-        const int qpos = p.pos_base + srow;
+        // Warp w (2..9) owns 16 query rows, 32 (w % 4) + 16 u with u = (w - 2) / 4,
+        // through the 16x256b TMEM shape: thread (g = lane / 4, tq = lane % 4)
+        // holds rows g and g + 8 of the 16 and columns 8j + 2tq, +1 of every
+        // 8-column block, so the four threads of a row are one lane quad and
+        // the row max and sum need two shuffles, no shared memory or barrier.
+        // Waits never break out of the loop (a time-out raises the error word
+        // and the loop runs on).
+        const int quarter = warp & 3, u = (warp - 2) >> 2;
+        const int g = lane >> 2, tq = lane & 3;
+        const int rbase = 32 * quarter + 16 * u;                // first TMEM lane (tile row) of the warp
+        const uint32_t lane_off = (uint32_t)rbase << 16;
+        const int row0 = rbase + g, row1 = row0 + 8;           // tile rows of this thread
+        const int qpos0 = p.pos_base + q0 + row0, qpos1 = qpos0 + 8;
         const float sl2 = p.scale_log2;
-        float m = -INFINITY, l = 0.f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
         for (int i = 0; i < nt; ++i) {
             const int b = i & 1;
             mbar_wait(&bars.s_full[b], (i >> 1) & 1);
             tc::fence_after();
-            float x[16];
-            tc::ld16(tS0 + b * PF_BN + 16 * qr + lane_off, x);
+            float x[32];
+            tc::ld16x256_x8(tS0 + b * PF_BN + lane_off, x);
             tc::wait_ld();
             tc::fence_before();
             mbar_arrive(&bars.s_free[b]);
             // Raw scores; the log2-domain scale is applied inside the exponent
             // (scale > 0, so the max commutes with it).
-            const int key0 = i * PF_BN + 16 * qr;
-            float mx = -INFINITY;
-            if (key0 + 15 <= qpos) {                       // tile fully visible to this row
+            const int key0 = i * PF_BN;
+            if (key0 + PF_BN - 1 > qpos0) {                    // the tile crosses row0's diagonal
 #pragma unroll
-                for (int c = 0; c < 16; ++c) mx = fmaxf(mx, x[c]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    x[c] = (key0 + c <= qpos) ? x[c] : -INFINITY;
-                    mx = fmaxf(mx, x[c]);
+                for (int j = 0; j < 8; ++j) {
+                    const int k = key0 + 8 * j + 2 * tq;
+                    if (k > qpos0) x[4 * j] = -INFINITY;
+                    if (k + 1 > qpos0) x[4 * j + 1] = -INFINITY;
+                    if (k > qpos1) x[4 * j + 2] = -INFINITY;
+                    if (k + 1 > qpos1) x[4 * j + 3] = -INFINITY;
                 }
             }
-            mx *= sl2;
-            bars.mx[b][qr][row] = mx;
-            asm volatile("bar.sync 1, 512;" ::: "memory");
-            mx = fmaxf(fmaxf(bars.mx[b][0][row], bars.mx[b][1][row]),
-                       fmaxf(bars.mx[b][2][row], bars.mx[b][3][row]));
-            const float mnew = fmaxf(m, mx);
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                mx0 = fmaxf(mx0, fmaxf(x[4 * j], x[4 * j + 1]));
+                mx1 = fmaxf(mx1, fmaxf(x[4 * j + 2], x[4 * j + 3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * sl2;
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * sl2;
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
             if (i == 0) {
-                m = mnew;
+                m0 = mn0; m1 = mn1;
             } else {
-                const bool need = mnew > m + PF_RESCALE_LOG2;
-                if (__any_sync(0xffffffffu, need)) {
+                const bool need0 = mn0 > m0 + PF_RESCALE_LOG2, need1 = mn1 > m1 + PF_RESCALE_LOG2;
+                if (__any_sync(0xffffffffu, need0 || need1)) {
                     // O must be complete up to tile i-1 before it is rescaled
                     mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
                     tc::fence_after();
-                    const float alpha = need ? exp2f(m - mnew) : 1.f;
+                    const float a0 = need0 ? exp2f(m0 - mn0) : 1.f, a1 = need1 ? exp2f(m1 - mn1) : 1.f;
 #pragma unroll 1
-                    for (int c = 0; c < 2; ++c) {
+                    for (int c = 0; c < PF_HD / 64; ++c) {
                         float o[32];
-                        const uint32_t col = tO + 64 * qr + 32 * c + lane_off;
-                        tc::ld32(col, o);
+                        tc::ld16x256_x8(tO + 64 * c + lane_off, o);
                         tc::wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                        tc::st32(col, o);
+                        for (int j = 0; j < 8; ++j) {
+                            o[4 * j] *= a0; o[4 * j + 1] *= a0; o[4 * j + 2] *= a1; o[4 * j + 3] *= a1;
+                        }
+                        tc::st16x256_x8(tO + 64 * c + lane_off, o);
                     }
                     tc::wait_st();
-                    if (need) { l *= alpha; m = mnew; }
+                    if (need0) { l0 *= a0; m0 = mn0; }
+                    if (need1) { l1 *= a1; m1 = mn1; }
                 }
             }
-            const float mu = (m == -INFINITY) ? 0.f : m;
-            float rs = 0.f;
-            uint32_t pk[8];
+            const float mu0 = (m0 == -INFINITY) ? 0.f : m0, mu1 = (m1 == -INFINITY) ? 0.f : m1;
+            uint32_t pk0[8], pk1[8];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float p0 = ex2_approx(fmaf(x[2 * c], sl2, -mu)), p1 = ex2_approx(fmaf(x[2 * c + 1], sl2, -mu));
-                rs += p0 + p1;
-                pk[c] = pack_bf16(p0, p1);
+            for (int j = 0; j < 8; ++j) {
+                const float p00 = ex2_approx(fmaf(x[4 * j], sl2, -mu0)), p01 = ex2_approx(fmaf(x[4 * j + 1], sl2, -mu0));
+                const float p10 = ex2_approx(fmaf(x[4 * j + 2], sl2, -mu1)), p11 = ex2_approx(fmaf(x[4 * j + 3], sl2, -mu1));
+                l0 += p00 + p01;
+                l1 += p10 + p11;
+                pk0[j] = pack_bf16(p00, p01);
+                pk1[j] = pack_bf16(p10, p11);
             }
-            l += rs;
             // the single P buffer was last read by PV(i-1)
             if (i >= 1) mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
-            uint8_t *prow = sP + row * 128;
+            // P row r: 128 B, 16-byte chunk j (keys 8j..8j+7) at (j ^ (r & 7)), pair tq at 4 tq
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int ch = 2 * qr + q;
-                *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) =
-                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            for (int j = 0; j < 8; ++j) {
+                *reinterpret_cast<uint32_t *>(sP + row0 * 128 + ((j ^ (row0 & 7)) << 4) + 4 * tq) = pk0[j];
+                *reinterpret_cast<uint32_t *>(sP + row1 * 128 + ((j ^ (row1 & 7)) << 4) + 4 * tq) = pk1[j];
             }
             fence_proxy_async();
             mbar_arrive(&bars.p_full[b]);
         }
-        // row sum = the four partial sums (same running max); the buffer the
-        // last tile did not use carries them
-        bars.mx[nt & 1][qr][row] = l;
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        l = (bars.mx[nt & 1][0][row] + bars.mx[nt & 1][1][row]) +
-            (bars.mx[nt & 1][2][row] + bars.mx[nt & 1][3][row]);
+        // row sums: the quad's partial sums (same running max)
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        if (tq == 0) { bars.lsum[row0] = l0; bars.lsum[row1] = l1; }
+        asm volatile("bar.sync 1, %0;" ::"n"(PF_SOFTMAX) : "memory");
         mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1);
         tc::fence_after();
         {
-            const float inv_l = 1.f / l;
+            // epilogue with the 32x32b shape: thread = tile row 32 quarter + lane,
+            // O columns 128 u .. 128 u + 127
+            const int row = 32 * quarter + lane, srow = q0 + row;
+            const uint32_t qoff = (uint32_t)(32 * quarter) << 16;
+            const float inv_l = 1.f / bars.lsum[row];
             const bool valid = srow < p.S;
             const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD;
             TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD;
 #pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 float o[32];
-                const int d0 = 64 * qr + 32 * c;
-                tc::ld32(tO + d0 + lane_off, o);
+                const int d0 = 128 * u + 32 * c;
+                tc::ld32(tO + d0 + qoff, o);
                 tc::wait_ld();
                 if (valid) {
 #pragma unroll
