@@ -38,7 +38,7 @@ constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 
 struct PfBars {
-    uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
+    uint64_t q_full, q_tmem, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
     uint32_t tmem_base;
     float lsum[PF_BM];        // final row sums for the epilogue
 };
@@ -78,6 +78,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
     if (threadIdx.x == 0) {
         mbar_init(&bars.q_full, 1);
+        mbar_init(&bars.q_tmem, PF_SOFTMAX);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars.k_full[i], 1);
             mbar_init(&bars.v_full[i], 1);
@@ -95,7 +96,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     tc::fence_after();
     const uint32_t tbase = bars.tmem_base;
-    const uint32_t tS0 = tbase, tO = tbase + 128;
+    const uint32_t tS0 = tbase, tO = tbase + 128, tQ = tbase + 384;   // S 2 x 64 | O 256 | Q 128 (bf16 pairs)
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producers
@@ -130,8 +131,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t ID_QK = tc::idesc_bf16(PF_BM, PF_BN, 0, 0);
             constexpr uint32_t ID_PV = tc::idesc_bf16(PF_BM, PF_HD, 0, 1);
-            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-            bool ok = mbar_wait(&bars.q_full, 0);
+            const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+            bool ok = mbar_wait(&bars.q_tmem, 0);       // Q copied into TMEM by the softmax warps
+            tc::fence_after();
             auto issue_pv = [&](int i) -> bool {
                 const int b = i & 1;
                 if (!mbar_wait(&bars.p_full[b], (i >> 1) & 1)) return false;
@@ -148,23 +150,31 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tc::commit(&bars.v_empty[b]);
                 return true;
             };
-            for (int j = 0; ok && j < nt; ++j) {
+            // S runs two tiles ahead of PV: S(j+2) is queued right behind
+            // PV(j), so the scores of tile j+1 are ready when the softmax
+            // finishes tile j, and the tensor pipe alternates PV and S
+            // without waiting for a P tile whose softmax just started.
+            auto issue_s = [&](int j) -> bool {
                 const int s = j & 1;
-                if (!mbar_wait(&bars.k_full[s], (j >> 1) & 1)) { ok = false; break; }
-                if (j >= 2 && !mbar_wait(&bars.s_free[s], ((j >> 1) - 1) & 1)) { ok = false; break; }
+                if (!mbar_wait(&bars.k_full[s], (j >> 1) & 1)) return false;
+                if (j >= 2 && !mbar_wait(&bars.s_free[s], ((j >> 1) - 1) & 1)) return false;
                 tc::fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_HD / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * (PF_BM * 128) + (kk & 3) * 32;
+                    // A = Q from TMEM: the S products read only K from shared memory
                     const uint32_t offk = (kk >> 2) * (PF_BN * 128) + (kk & 3) * 32;
-                    tc::mma_bf16(tS0 + s * PF_BN, tc::desc_k_sw128(aQ + off),
-                                 tc::desc_k_sw128(aK + s * PF_KV_BYTES + offk), ID_QK, kk > 0 ? 1u : 0u);
+                    tc::mma_bf16_ts(tS0 + s * PF_BN, tQ + kk * 8, tc::desc_k_sw128(aK + s * PF_KV_BYTES + offk),
+                                    ID_QK, kk > 0 ? 1u : 0u);
                 }
                 tc::commit(&bars.s_full[s]);
                 tc::commit(&bars.k_empty[s]);
-                if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+                return true;
+            };
+            for (int j = 0; ok && j < 2 && j < nt; ++j) ok = issue_s(j);
+            for (int j = 0; ok && j < nt; ++j) {
+                ok = issue_pv(j);
+                if (ok && j + 2 < nt) ok = issue_s(j + 2);
             }
-            if (ok) issue_pv(nt - 1);
         }
     } else {
         // ------------------------------------------------ softmax + epilogue
@@ -182,6 +192,27 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int row0 = rbase + g, row1 = row0 + 8;           // tile rows of this thread
         const int qpos0 = p.pos_base + q0 + row0, qpos1 = qpos0 + 8;
         const float sl2 = p.scale_log2;
+        {   // Q tile (shared memory, 128B-swizzled 64-column boxes) into TMEM as bf16
+            // pairs: thread = tile row 32 quarter + lane, head dims 128 u .. 128 u + 127
+            mbar_wait(&bars.q_full, 0);
+            const int row = 32 * quarter + lane;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                float v[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {          // 16-byte chunk: 8 head dims = 4 columns
+                    const int d = 128 * u + 64 * hh + 8 * c;
+                    const uint4 w = *reinterpret_cast<const uint4 *>(
+                        sQ + (d >> 6) * (PF_BM * 128) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
+                    v[4 * c] = __uint_as_float(w.x); v[4 * c + 1] = __uint_as_float(w.y);
+                    v[4 * c + 2] = __uint_as_float(w.z); v[4 * c + 3] = __uint_as_float(w.w);
+                }
+                tc::st32(tQ + 64 * u + 32 * hh + ((uint32_t)(32 * quarter) << 16), v);
+            }
+            tc::wait_st();
+            tc::fence_before();
+            mbar_arrive(&bars.q_tmem);
+        }
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
         for (int i = 0; i < nt; ++i) {
             const int b = i & 1;

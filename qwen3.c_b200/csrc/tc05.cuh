@@ -81,6 +81,20 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t 
           "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// D[tmem] (+)= A[tmem] . B[smem]^T, bf16 (A from tensor memory: lane = row,
+// 32-bit column c = the bf16 pair k = 2c, 2c+1; K = 16 per instruction = 8
+// columns); one thread.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate),
+          "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
 // Arrive once on `bar` when every MMA issued so far by this thread completes.
 __device__ __forceinline__ void commit(uint64_t *bar)
 {
