@@ -44,7 +44,7 @@ struct KvLayer {
     __nv_bfloat16 *k = nullptr, *v = nullptr;
     int batch = 0, KH = 0, max_t = 0, hd = 0;
     CUtensorMap tmK, tmV;      // 16-row boxes (decode)
-    CUtensorMap tmK64, tmV64;  // 64-row boxes (prefill)
+    CUtensorMap tmK64, tmV64;  // 128-row boxes (prefill key tiles)
     float *qnw = nullptr, *knw = nullptr;  // [hd] resident norm weights
 };
 
@@ -604,8 +604,8 @@ int coli_cuda_kv_ensure(int layer, int batch, int KH, int max_t, int hd)
     L.batch = batch; L.KH = KH; L.max_t = max_t; L.hd = hd;
     if (!make_kv_tmap(&L.tmK, L.k, batch * KH * max_t, hd)) return 0;
     if (!make_kv_tmap(&L.tmV, L.v, batch * KH * max_t, hd)) return 0;
-    if (!make_kv_tmap(&L.tmK64, L.k, batch * KH * max_t, hd, 64)) return 0;
-    if (!make_kv_tmap(&L.tmV64, L.v, batch * KH * max_t, hd, 64)) return 0;
+    if (!make_kv_tmap(&L.tmK64, L.k, batch * KH * max_t, hd, 128)) return 0;
+    if (!make_kv_tmap(&L.tmV64, L.v, batch * KH * max_t, hd, 128)) return 0;
     return 1;
 }
 

@@ -6,20 +6,26 @@
 // sigmoid(gate). The prologue (q/k norm, RoPE, K/V append) runs before this
 // kernel (gqa_prologue_kernel), so the new rows are already in the cache.
 //
-// One CTA = 128 query rows of one Q head. Warp roles (320 threads):
-//   warp 0      TMA producers (lane 0: Q once, then K; lane 1: V): 64-key
-//               tiles into separate 2-stage K and V rings (128B swizzle).
-//   warp 1      MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
-//               two TMEM score buffers (M=128, N=64, K=256), then
-//               O += P V (M=128, N=256, K=64) with V read MN-major.
-//   warps 2..9  softmax: 16 query rows per warp read with the 16x256b TMEM
-//               shape (a lane quad per row, so row max and sum are quad
-//               shuffles), causal mask, online softmax in the log2 domain
-//               with lazy rescaling (O is corrected in TMEM only when the
-//               running max grows by more than 2^8), P written to shared
-//               memory in the UMMA K-major layout; final epilogue O / l *
-//               sigmoid(gate).
-// TMEM: 2 x 64 columns of scores + 256 columns of O (512 allocated).
+// One CTA = 128 query rows of one Q head, 128-key tiles. A tcgen05.mma costs
+// about the same for N = 64 as for N = 128, so 128-key score tiles halve the
+// instruction count of S per key; the shared memory that this takes is freed
+// by holding Q in TMEM (the A operand of S) instead of shared memory.
+// Warp roles (320 threads):
+//   warp 0      TMA producers. Lane 0: Q (once, into the V buffer), then K
+//               tiles into a 2-stage ring. Lane 1: V tiles into one buffer,
+//               once Q has been moved into TMEM and each PV has read the last.
+//   warp 1      MMA issuer (one thread) and TMEM owner: S = Q K^T (M=128,
+//               N=128, K=256; A from TMEM), O += P V (M=128, N=256, K=128;
+//               V read MN-major). S(j+1) is issued before PV(j).
+//   warps 2..9  copy Q into TMEM, then the softmax: 16 query rows per warp read
+//               with the 16x256b TMEM shape (a lane quad per row, so row max
+//               and sum are quad shuffles), causal mask on the tile that
+//               crosses the diagonal, online softmax in the log2 domain with
+//               lazy rescaling (O is corrected in TMEM only when the running
+//               max grows by more than 2^8), P written to shared memory in the
+//               UMMA K-major layout; final epilogue O / l * sigmoid(gate).
+// TMEM (512 columns): scores 128 | O 256 | Q 128 (bf16 pairs).
+// Shared memory: K 2 x 64 KiB, V (and Q staging) 64 KiB, P 32 KiB.
 // Every wait is bounded (see mbar_wait); no cluster multicast.
 #include "common.cuh"
 #include "kernels.h"
@@ -27,18 +33,18 @@
 
 namespace coli {
 
-constexpr int PF_BM = 128, PF_BN = 64, PF_HD = 256;
-constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB
-constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 32 KiB per K (or V) tile
-constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 16 KiB
-constexpr int PF_DATA = PF_Q_BYTES + 4 * PF_KV_BYTES + PF_P_BYTES;  // 208 KiB
+constexpr int PF_BM = 128, PF_BN = 128, PF_HD = 256;
+constexpr int PF_Q_BYTES = PF_BM * PF_HD * 2;        // 64 KiB (staged in the V buffer)
+constexpr int PF_KV_BYTES = PF_BN * PF_HD * 2;       // 64 KiB per K (or V) tile
+constexpr int PF_P_BYTES = PF_BM * PF_BN * 2;        // 32 KiB
+constexpr int PF_DATA = 3 * PF_KV_BYTES + PF_P_BYTES;  // 224 KiB
 constexpr int PF_SOFTMAX = 256;                    // softmax / epilogue threads
 constexpr int PF_THREADS = 64 + PF_SOFTMAX;
 constexpr float PF_RESCALE_LOG2 = 8.0f;
-
+static_assert(PF_Q_BYTES <= PF_KV_BYTES, "Q is staged in the V buffer");
 
 struct PfBars {
-    uint64_t q_full, q_tmem, k_full[2], v_full[2], k_empty[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2];
+    uint64_t q_full, q_tmem, k_full[2], k_empty[2], v_full, v_empty, s_full, s_free, p_full, pv_done;
     uint32_t tmem_base;
     float lsum[PF_BM];        // final row sums for the epilogue
 };
@@ -54,11 +60,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // starts 1024-byte aligned as the 128B-swizzled TMA boxes and UMMA
     // descriptors need; checked below rather than padded (the budget is tight).
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = smem_raw;
-    uint8_t *sQ = smem;
-    uint8_t *sK = sQ + PF_Q_BYTES;              // [2][32 KiB]
-    uint8_t *sV = sK + 2 * PF_KV_BYTES;         // [2][32 KiB]
-    uint8_t *sP = sV + 2 * PF_KV_BYTES;         // 16 KiB P tile
+    uint8_t *sK = smem_raw;                     // [2][64 KiB]
+    uint8_t *sV = sK + 2 * PF_KV_BYTES;         // 64 KiB: Q first, then V tiles
+    uint8_t *sP = sV + PF_KV_BYTES;             // 32 KiB P tile (two 64-key atoms)
     PfBars &bars = *reinterpret_cast<PfBars *>(sP + PF_P_BYTES);
     if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA: nothing has started yet
         if (threadIdx.x == 0) raise_error(2);
@@ -79,16 +83,10 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (threadIdx.x == 0) {
         mbar_init(&bars.q_full, 1);
         mbar_init(&bars.q_tmem, PF_SOFTMAX);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars.k_full[i], 1);
-            mbar_init(&bars.v_full[i], 1);
-            mbar_init(&bars.k_empty[i], 1);
-            mbar_init(&bars.v_empty[i], 1);
-            mbar_init(&bars.s_full[i], 1);
-            mbar_init(&bars.s_free[i], PF_SOFTMAX);
-            mbar_init(&bars.p_full[i], PF_SOFTMAX);
-            mbar_init(&bars.pv_done[i], 1);
-        }
+        for (int i = 0; i < 2; ++i) { mbar_init(&bars.k_full[i], 1); mbar_init(&bars.k_empty[i], 1); }
+        mbar_init(&bars.v_full, 1); mbar_init(&bars.v_empty, 1);
+        mbar_init(&bars.s_full, 1); mbar_init(&bars.s_free, PF_SOFTMAX);
+        mbar_init(&bars.p_full, PF_SOFTMAX); mbar_init(&bars.pv_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) tc::alloc(&bars.tmem_base, 512);
@@ -96,17 +94,14 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     tc::fence_after();
     const uint32_t tbase = bars.tmem_base;
-    const uint32_t tS0 = tbase, tO = tbase + 128, tQ = tbase + 384;   // S 2 x 64 | O 256 | Q 128 (bf16 pairs)
+    const uint32_t tS = tbase, tO = tbase + 128, tQ = tbase + 384;   // S 128 | O 256 | Q 128 (bf16 pairs)
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producers
-        // Lane 0 streams K (a stage frees as soon as its S MMA completes),
-        // lane 1 streams V (freed after its PV MMA), so the next K tile is in
-        // flight while the current tile's softmax and PV still run.
         if (lane == 0) {
             tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
             mbar_expect_tx(&bars.q_full, PF_Q_BYTES);
-            for (int c = 0; c < 4; ++c) tma_load_3d(sQ + c * (PF_BM * 128), &tmQ, 64 * c, h, q0, &bars.q_full);
+            for (int c = 0; c < 4; ++c) tma_load_3d(sV + c * (PF_BM * 128), &tmQ, 64 * c, h, q0, &bars.q_full);
             for (int j = 0; j < nt; ++j) {
                 const int s = j & 1;
                 if (j >= 2 && !mbar_wait(&bars.k_empty[s], ((j >> 1) - 1) & 1)) break;
@@ -117,13 +112,14 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
         } else if (lane == 1) {
             tma_prefetch_desc(&tmV);
-            for (int j = 0; j < nt; ++j) {
-                const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&bars.v_empty[s], ((j >> 1) - 1) & 1)) break;
-                mbar_expect_tx(&bars.v_full[s], PF_KV_BYTES);
-                for (int c = 0; c < 4; ++c)
-                    tma_load_2d(sV + s * PF_KV_BYTES + c * (PF_BN * 128), &tmV, 64 * c,
-                                kvrow0 + j * PF_BN, &bars.v_full[s]);
+            // the V buffer holds Q until the softmax warps have moved it into TMEM
+            if (mbar_wait(&bars.q_tmem, 0)) {
+                for (int j = 0; j < nt; ++j) {
+                    if (j >= 1 && !mbar_wait(&bars.v_empty, (j - 1) & 1)) break;
+                    mbar_expect_tx(&bars.v_full, PF_KV_BYTES);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d(sV + c * (PF_BN * 128), &tmV, 64 * c, kvrow0 + j * PF_BN, &bars.v_full);
+                }
             }
         }
     } else if (warp == 1) {
@@ -133,58 +129,50 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             constexpr uint32_t ID_PV = tc::idesc_bf16(PF_BM, PF_HD, 0, 1);
             const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
             bool ok = mbar_wait(&bars.q_tmem, 0);       // Q copied into TMEM by the softmax warps
-            tc::fence_after();
-            auto issue_pv = [&](int i) -> bool {
-                const int b = i & 1;
-                if (!mbar_wait(&bars.p_full[b], (i >> 1) & 1)) return false;
-                if (!mbar_wait(&bars.v_full[b], (i >> 1) & 1)) return false;
-                tc::fence_after();
-#pragma unroll
-                for (int kk = 0; kk < PF_BN / 16; ++kk) {
-                    const uint64_t da = tc::desc_k_sw128(aP + kk * 32);
-                    const uint64_t db = tc::desc_mn_sw128(aV + b * PF_KV_BYTES + kk * 16 * 128,
-                                                          PF_BN * 128, 1024);
-                    tc::mma_bf16(tO, da, db, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc::commit(&bars.pv_done[b]);
-                tc::commit(&bars.v_empty[b]);
-                return true;
-            };
-            // S runs two tiles ahead of PV: S(j+2) is queued right behind
-            // PV(j), so the scores of tile j+1 are ready when the softmax
-            // finishes tile j, and the tensor pipe alternates PV and S
-            // without waiting for a P tile whose softmax just started.
             auto issue_s = [&](int j) -> bool {
                 const int s = j & 1;
                 if (!mbar_wait(&bars.k_full[s], (j >> 1) & 1)) return false;
-                if (j >= 2 && !mbar_wait(&bars.s_free[s], ((j >> 1) - 1) & 1)) return false;
+                if (j >= 1 && !mbar_wait(&bars.s_free, (j - 1) & 1)) return false;   // S(j-1) read out
                 tc::fence_after();
 #pragma unroll
                 for (int kk = 0; kk < PF_HD / 16; ++kk) {
-                    // A = Q from TMEM: the S products read only K from shared memory
                     const uint32_t offk = (kk >> 2) * (PF_BN * 128) + (kk & 3) * 32;
-                    tc::mma_bf16_ts(tS0 + s * PF_BN, tQ + kk * 8, tc::desc_k_sw128(aK + s * PF_KV_BYTES + offk),
-                                    ID_QK, kk > 0 ? 1u : 0u);
+                    tc::mma_bf16_ts(tS, tQ + kk * 8, tc::desc_k_sw128(aK + s * PF_KV_BYTES + offk), ID_QK,
+                                    kk > 0 ? 1u : 0u);
                 }
-                tc::commit(&bars.s_full[s]);
+                tc::commit(&bars.s_full);
                 tc::commit(&bars.k_empty[s]);
                 return true;
             };
-            for (int j = 0; ok && j < 2 && j < nt; ++j) ok = issue_s(j);
+            auto issue_pv = [&](int i) -> bool {
+                if (!mbar_wait(&bars.p_full, i & 1)) return false;
+                if (!mbar_wait(&bars.v_full, i & 1)) return false;
+                tc::fence_after();
+#pragma unroll
+                for (int kk = 0; kk < PF_BN / 16; ++kk) {
+                    const uint64_t da = tc::desc_k_sw128(aP + (kk >> 2) * (PF_BM * 128) + (kk & 3) * 32);
+                    const uint64_t db = tc::desc_mn_sw128(aV + kk * 16 * 128, PF_BN * 128, 1024);
+                    tc::mma_bf16(tO, da, db, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::commit(&bars.pv_done);
+                tc::commit(&bars.v_empty);
+                return true;
+            };
+            tc::fence_after();
+            if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < nt; ++j) {
-                ok = issue_pv(j);
-                if (ok && j + 2 < nt) ok = issue_s(j + 2);
+                if (j + 1 < nt) ok = issue_s(j + 1);
+                if (ok) ok = issue_pv(j);
             }
         }
     } else {
-        // ------------------------------------------------ softmax + epilogue
+        // ------------------------------------------------ Q to TMEM, softmax, epilogue
         // Warp w (2..9) owns 16 query rows, 32 (w % 4) + 16 u with u = (w - 2) / 4,
         // through the 16x256b TMEM shape: thread (g = lane / 4, tq = lane % 4)
         // holds rows g and g + 8 of the 16 and columns 8j + 2tq, +1 of every
         // 8-column block, so the four threads of a row are one lane quad and
-        // the row max and sum need two shuffles, no shared memory or barrier.
-        // Waits never break out of the loop (a time-out raises the error word
-        // and the loop runs on).
+        // the row max and sum need two shuffles. Waits never break out of the
+        // loop (a time-out raises the error word and the loop runs on).
         const int quarter = warp & 3, u = (warp - 2) >> 2;
         const int g = lane >> 2, tq = lane & 3;
         const int rbase = 32 * quarter + 16 * u;                // first TMEM lane (tile row) of the warp
@@ -192,8 +180,8 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int row0 = rbase + g, row1 = row0 + 8;           // tile rows of this thread
         const int qpos0 = p.pos_base + q0 + row0, qpos1 = qpos0 + 8;
         const float sl2 = p.scale_log2;
-        {   // Q tile (shared memory, 128B-swizzled 64-column boxes) into TMEM as bf16
-            // pairs: thread = tile row 32 quarter + lane, head dims 128 u .. 128 u + 127
+        {   // Q tile (staged in the V buffer, 128B-swizzled 64-column boxes) into TMEM
+            // as bf16 pairs: thread = tile row 32 quarter + lane, head dims 128 u ..
             mbar_wait(&bars.q_full, 0);
             const int row = 32 * quarter + lane;
 #pragma unroll
@@ -203,7 +191,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 for (int c = 0; c < 8; ++c) {          // 16-byte chunk: 8 head dims = 4 columns
                     const int d = 128 * u + 64 * hh + 8 * c;
                     const uint4 w = *reinterpret_cast<const uint4 *>(
-                        sQ + (d >> 6) * (PF_BM * 128) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
+                        sV + (d >> 6) * (PF_BM * 128) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
                     v[4 * c] = __uint_as_float(w.x); v[4 * c + 1] = __uint_as_float(w.y);
                     v[4 * c + 2] = __uint_as_float(w.z); v[4 * c + 3] = __uint_as_float(w.w);
                 }
@@ -211,24 +199,30 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             tc::wait_st();
             tc::fence_before();
-            mbar_arrive(&bars.q_tmem);
+            mbar_arrive(&bars.q_tmem);                 // also frees the V buffer
         }
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
         for (int i = 0; i < nt; ++i) {
-            const int b = i & 1;
-            mbar_wait(&bars.s_full[b], (i >> 1) & 1);
+            mbar_wait(&bars.s_full, i & 1);
             tc::fence_after();
-            float x[32];
-            tc::ld16x256_x8(tS0 + b * PF_BN + lane_off, x);
-            tc::wait_ld();
+            float x[64];                               // two 64-key halves of the 16x256b.x8 shape
+            {
+                float xa[32], xb[32];
+                tc::ld16x256_x8(tS + lane_off, xa);
+                tc::ld16x256_x8(tS + 64 + lane_off, xb);
+                tc::wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) { x[e] = xa[e]; x[32 + e] = xb[e]; }
+            }
             tc::fence_before();
-            mbar_arrive(&bars.s_free[b]);
-            // Raw scores; the log2-domain scale is applied inside the exponent
-            // (scale > 0, so the max commutes with it).
+            mbar_arrive(&bars.s_free);
+            // x[4j + 0/1]: row0, keys 8j + 2tq, +1 (j = 0..15 over the 128 keys);
+            // x[4j + 2/3]: row1. Raw scores; the log2-domain scale is applied
+            // inside the exponent (scale > 0, so the max commutes with it).
             const int key0 = i * PF_BN;
             if (key0 + PF_BN - 1 > qpos0) {                    // the tile crosses row0's diagonal
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < 16; ++j) {
                     const int k = key0 + 8 * j + 2 * tq;
                     if (k > qpos0) x[4 * j] = -INFINITY;
                     if (k + 1 > qpos0) x[4 * j + 1] = -INFINITY;
@@ -238,7 +232,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
                 mx0 = fmaxf(mx0, fmaxf(x[4 * j], x[4 * j + 1]));
                 mx1 = fmaxf(mx1, fmaxf(x[4 * j + 2], x[4 * j + 3]));
             }
@@ -253,7 +247,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const bool need0 = mn0 > m0 + PF_RESCALE_LOG2, need1 = mn1 > m1 + PF_RESCALE_LOG2;
                 if (__any_sync(0xffffffffu, need0 || need1)) {
                     // O must be complete up to tile i-1 before it is rescaled
-                    mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
+                    mbar_wait(&bars.pv_done, (i - 1) & 1);
                     tc::fence_after();
                     const float a0 = need0 ? exp2f(m0 - mn0) : 1.f, a1 = need1 ? exp2f(m1 - mn1) : 1.f;
 #pragma unroll 1
@@ -273,9 +267,9 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
             }
             const float mu0 = (m0 == -INFINITY) ? 0.f : m0, mu1 = (m1 == -INFINITY) ? 0.f : m1;
-            uint32_t pk0[8], pk1[8];
+            uint32_t pk0[16], pk1[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
                 const float p00 = ex2_approx(fmaf(x[4 * j], sl2, -mu0)), p01 = ex2_approx(fmaf(x[4 * j + 1], sl2, -mu0));
                 const float p10 = ex2_approx(fmaf(x[4 * j + 2], sl2, -mu1)), p11 = ex2_approx(fmaf(x[4 * j + 3], sl2, -mu1));
                 l0 += p00 + p01;
@@ -283,16 +277,17 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 pk0[j] = pack_bf16(p00, p01);
                 pk1[j] = pack_bf16(p10, p11);
             }
-            // the single P buffer was last read by PV(i-1)
-            if (i >= 1) mbar_wait(&bars.pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1);
-            // P row r: 128 B, 16-byte chunk j (keys 8j..8j+7) at (j ^ (r & 7)), pair tq at 4 tq
+            // the P buffer was last read by PV(i-1)
+            if (i >= 1) mbar_wait(&bars.pv_done, (i - 1) & 1);
+            // P row r, keys 8j..8j+7: atom j / 8 (64 keys), 16-byte chunk (j % 8) ^ (r & 7), pair tq at 4 tq
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                *reinterpret_cast<uint32_t *>(sP + row0 * 128 + ((j ^ (row0 & 7)) << 4) + 4 * tq) = pk0[j];
-                *reinterpret_cast<uint32_t *>(sP + row1 * 128 + ((j ^ (row1 & 7)) << 4) + 4 * tq) = pk1[j];
+            for (int j = 0; j < 16; ++j) {
+                const int at = (j >> 3) * (PF_BM * 128);
+                *reinterpret_cast<uint32_t *>(sP + at + row0 * 128 + (((j & 7) ^ (row0 & 7)) << 4) + 4 * tq) = pk0[j];
+                *reinterpret_cast<uint32_t *>(sP + at + row1 * 128 + (((j & 7) ^ (row1 & 7)) << 4) + 4 * tq) = pk1[j];
             }
             fence_proxy_async();
-            mbar_arrive(&bars.p_full[b]);
+            mbar_arrive(&bars.p_full);
         }
         // row sums: the quad's partial sums (same running max)
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -301,7 +296,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
         if (tq == 0) { bars.lsum[row0] = l0; bars.lsum[row1] = l1; }
         asm volatile("bar.sync 1, %0;" ::"n"(PF_SOFTMAX) : "memory");
-        mbar_wait(&bars.pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1);
+        mbar_wait(&bars.pv_done, (nt - 1) & 1);
         tc::fence_after();
         {
             // epilogue with the 32x32b shape: thread = tile row 32 quarter + lane,
