@@ -84,6 +84,174 @@ gqa_prologue_kernel(GqaPrologueArgs p)
     }
 }
 
+// Same arithmetic with one warp per head vector and one CTA per one to four query rows:
+// lane l owns dims [8l, 8l+8) (16-byte loads and stores), the sum of squares
+// is reduced across lanes in double, and the row's RoPE angles (which all its heads
+// share) are computed once per CTA into shared memory; each warp issues the
+// loads of three head vectors before it reduces any of them. Needs 16-byte aligned
+// row bases; the launcher falls back to the kernel above otherwise.
+template <typename TI>
+__device__ __forceinline__ void load8(const TI *src, float (&x)[8]);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16 *src, float (&x)[8])
+{
+    const uint4 u = *reinterpret_cast<const uint4 *>(src);
+    const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 f = __bfloat1622float2(b[i]); x[2 * i] = f.x; x[2 * i + 1] = f.y; }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float *src, float (&x)[8])
+{
+    const float4 a = reinterpret_cast<const float4 *>(src)[0], b = reinterpret_cast<const float4 *>(src)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+// eight raw input elements held packed until they are used
+template <typename TI> struct Raw8;
+template <> struct Raw8<__nv_bfloat16> {
+    uint4 u;
+    __device__ __forceinline__ void load(const __nv_bfloat16 *src) { u = *reinterpret_cast<const uint4 *>(src); }
+    __device__ __forceinline__ void unpack(float (&x)[8]) const
+    {
+        const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { const float2 f = __bfloat1622float2(b[i]); x[2 * i] = f.x; x[2 * i + 1] = f.y; }
+    }
+};
+template <> struct Raw8<float> {
+    float4 a, b;
+    __device__ __forceinline__ void load(const float *src)
+    {
+        a = reinterpret_cast<const float4 *>(src)[0]; b = reinterpret_cast<const float4 *>(src)[1];
+    }
+    __device__ __forceinline__ void unpack(float (&x)[8]) const
+    {
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+};
+__device__ __forceinline__ void store8(__nv_bfloat16 *dst, const float (&y)[8])
+{
+    uint4 u;
+    __nv_bfloat162 *b = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(dst) = u;
+}
+
+constexpr int GQA_PRO_ROWS = 4, GQA_PRO_WARPS = 8, GQA_PRO_U = 3;
+
+template <typename TI>
+__global__ void __launch_bounds__(GQA_PRO_WARPS * 32, 4)
+gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
+{
+    __shared__ float cs_t[GQA_PRO_ROWS][GQA_HD / 2], sn_t[GQA_PRO_ROWS][GQA_HD / 2];
+    __shared__ float vec[GQA_PRO_WARPS][GQA_HD];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * rpc, rows = min(rpc, p.nq - n0);
+    const int H = p.H, KH = p.KH, nv = H + KH;
+    const int Hin = p.Hin ? p.Hin : H, KHin = p.KHin ? p.KHin : KH;
+    const int half = p.rot >> 1;
+    // RoPE angles of these rows (c/qwen.c:570-579), shared by all their heads
+    for (int i = threadIdx.x; i < rows * half; i += blockDim.x) {
+        const int r = i / half, jj = i - r * half;
+        const float inv = powf(p.theta, -2.0f * jj / p.rot);
+        const float ang = (float)p.pos[n0 + r] * inv;
+        cs_t[r][jj] = cosf(ang); sn_t[r][jj] = sinf(ang);
+    }
+    __syncthreads();
+    const int d0 = lane * 8, total = rows * nv;
+    // RoPE partner of dim d is d +- half: when half is a multiple of 8 it sits in
+    // the same slot of lane +- half/8, else it goes through shared memory
+    const bool shfl_rope = (half & 7) == 0;
+    const int hl = half >> 3;
+    const int src_lane = lane < hl ? lane + hl : lane - hl;
+    const bool rope_lane = d0 < p.rot;
+    float *vw = vec[warp];
+    for (int b = warp; b < total; b += GQA_PRO_WARPS * GQA_PRO_U) {
+        // issue the loads of up to U head vectors before any arithmetic
+        Raw8<TI> raw[GQA_PRO_U];
+        int r = b / nv, j = b - r * nv;
+        const int r0 = r, j0 = j;
+#pragma unroll
+        for (int u = 0; u < GQA_PRO_U; ++u) {
+            if (r < rows) {
+                const int n = n0 + r;
+                if (j < H) raw[u].load(static_cast<const TI *>(p.qg) + ((size_t)n * Hin + p.h0 + j) * 2 * GQA_HD + d0);
+                else raw[u].load(static_cast<const TI *>(p.k) + ((size_t)n * KHin + p.kh0 + (j - H)) * GQA_HD + d0);
+            }
+            for (j += GQA_PRO_WARPS; j >= nv; j -= nv) ++r;
+        }
+        r = r0; j = j0;
+#pragma unroll
+        for (int u = 0; u < GQA_PRO_U; ++u) {
+            if (r >= rows) break;
+            const int n = n0 + r;
+            const bool isq = j < H;
+            float w[8], x[8];
+            load8<float>((isq ? p.qnw : p.knw) + d0, w);
+            raw[u].unpack(x);
+            // zero-centred RMSNorm (c/qwen.c:326-330): per-lane partial sums of
+            // squares in fp32, the cross-lane sum in double as the reference does
+            float sl = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sl = fmaf(x[i], x[i], sl);
+            double s2 = sl;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+            const float rs = 1.f / sqrtf((float)(s2 / GQA_HD) + p.eps);
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = x[i] * rs * (1.f + w[i]);
+            // partial NeoX RoPE on dims [0, rot)
+            if (shfl_rope) {
+                float q[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) q[i] = __shfl_sync(0xffffffffu, y[i], src_lane);
+                if (rope_lane) {
+                    const bool lo_half = d0 < half;
+                    const int jj0 = lo_half ? d0 : d0 - half;
+                    const float4 c0 = *reinterpret_cast<const float4 *>(&cs_t[r][jj0]);
+                    const float4 c1 = *reinterpret_cast<const float4 *>(&cs_t[r][jj0 + 4]);
+                    const float4 s0 = *reinterpret_cast<const float4 *>(&sn_t[r][jj0]);
+                    const float4 s1 = *reinterpret_cast<const float4 *>(&sn_t[r][jj0 + 4]);
+                    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        y[i] = lo_half ? y[i] * c[i] - q[i] * sn[i] : y[i] * c[i] + q[i] * sn[i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) vw[d0 + i] = y[i];
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int d = d0 + i;
+                    if (d < p.rot) {
+                        const int jj = d < half ? d : d - half;
+                        const float lo = vw[jj], hi = vw[jj + half];
+                        const float c = cs_t[r][jj], sn = sn_t[r][jj];
+                        y[i] = d < half ? lo * c - hi * sn : hi * c + lo * sn;
+                    }
+                }
+                __syncwarp();
+            }
+            if (isq) {
+                store8(p.qout + ((size_t)n * H + j) * GQA_HD + d0, y);
+            } else {
+                const int kh = j - H;
+                const int creq = p.creq ? p.creq[n] : n;
+                const size_t row = ((size_t)creq * KH + kh) * p.max_t + p.pos[n];
+                store8(p.kcache + row * GQA_HD + d0, y);
+                float v[8];
+                load8<TI>(static_cast<const TI *>(p.v) + ((size_t)n * KHin + p.kh0 + kh) * GQA_HD + d0, v);
+                store8(p.vcache + row * GQA_HD + d0, v);
+            }
+            for (j += GQA_PRO_WARPS; j >= nv; j -= nv) ++r;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ split-KV
 template <int WARPS, int STAGES>
 __global__ void __launch_bounds__(WARPS * 32, 1)
@@ -312,6 +480,16 @@ size_t gqa_split_smem_bytes()
 
 cudaError_t launch_gqa_prologue(const GqaPrologueArgs &a, int in_bf16, cudaStream_t st)
 {
+    const uintptr_t al = (uintptr_t)a.qg | (uintptr_t)a.k | (uintptr_t)a.v | (uintptr_t)a.qnw |
+                         (uintptr_t)a.knw | (uintptr_t)a.qout | (uintptr_t)a.kcache | (uintptr_t)a.vcache;
+    if ((al & 15) == 0) {
+        // rows per CTA: 4 once there are enough rows to fill the GPU, else 1 (latency)
+        const int rpc = a.nq >= 2048 ? GQA_PRO_ROWS : 1;
+        const int blocks = (a.nq + rpc - 1) / rpc;
+        if (in_bf16) gqa_prologue_warp_kernel<__nv_bfloat16><<<blocks, GQA_PRO_WARPS * 32, 0, st>>>(a, rpc);
+        else gqa_prologue_warp_kernel<float><<<blocks, GQA_PRO_WARPS * 32, 0, st>>>(a, rpc);
+        return cudaGetLastError();
+    }
     dim3 grid(a.nq, a.H + a.KH);
     if (in_bf16) gqa_prologue_kernel<__nv_bfloat16><<<grid, GQA_HD, 0, st>>>(a);
     else gqa_prologue_kernel<float><<<grid, GQA_HD, 0, st>>>(a);

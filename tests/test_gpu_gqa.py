@@ -132,6 +132,35 @@ def test_prefill_rows_vs_oracle(be, orc):
     assert_close(ctx, want, what="prefill")
 
 
+@pytest.mark.parametrize("rot", [2, 36, 64, 256])
+def test_prologue_rotary_widths(be, orc, rot):
+    """q/k norm + partial RoPE for rotary widths whose half is / is not a
+    multiple of 8 (lane-shuffle vs shared-memory partner exchange), at a row
+    count that takes the four-rows-per-CTA launch, then attention."""
+    cfg = f"gqa_rot{rot}"
+    S = 2050
+    be.kv_ensure(4, 1, KH, 2304)
+    qnw, knw = _norm_w(cfg)
+    be.gqa_norm_weight(4, qnw, knw)
+    qg = synth.normal(synth.seed_of(cfg, "qg"), (S, H, 2 * HD))
+    k = synth.normal(synth.seed_of(cfg, "k"), (S, KH, HD))
+    v = synth.normal(synth.seed_of(cfg, "v"), (S, KH, HD))
+    ctx = be.gqa_step(4, 0, 0, qg, k, v, rot=rot)
+    Kc = np.zeros((KH, 2304, HD), np.float32)
+    Vc = np.zeros_like(Kc)
+    q1, k1 = qg.copy(), k.copy()
+    orc.gqa_prologue(q1, k1, v.copy(), qnw, knw, 0, Kc, Vc, rot=rot)
+    # the cache rows carry the normed + roped k
+    for kh in range(KH):
+        kd, vd = be.kv_read(4, 0, kh * 2304, S)
+        assert_close(kd, Kc[kh, :S], what=f"rot {rot} k cache")
+        np.testing.assert_array_equal(vd, synth.bf16_round(v[:, kh]))
+    # the roped q, through attention: the first and the last 64 rows
+    Kb, Vb = synth.bf16_round(Kc), synth.bf16_round(Vc)
+    assert_close(ctx[:64], orc.gqa_attend(q1[:64], Kb, Vb, 0), what=f"rot {rot} head rows")
+    assert_close(ctx[S - 64:], orc.gqa_attend(q1[S - 64:], Kb, Vb, S - 64), what=f"rot {rot} tail rows")
+
+
 def test_bf16_device_path(be, orc):
     import torch
     cfg = "gqa_dev"
