@@ -23,7 +23,11 @@
 //               crosses the diagonal, online softmax in the log2 domain with
 //               lazy rescaling (O is corrected in TMEM only when the running
 //               max grows by more than 2^8), P written to shared memory in the
-//               UMMA K-major layout; final epilogue O / l * sigmoid(gate).
+//               UMMA K-major layout. Epilogue: O / l staged as fp32 rows in
+//               the (then idle) K buffers, then a warp per row applies
+//               sigmoid(gate) with 16-byte coalesced gate loads and ctx stores
+//               (a thread-per-row store pattern touches 32 rows per
+//               instruction and cost as much as 40 KV tiles per CTA).
 // TMEM (512 columns): scores 128 | O 256 | Q 128 (bf16 pairs).
 // Shared memory: K 2 x 64 KiB, V (and Q staging) 64 KiB, P 32 KiB.
 // Every wait is bounded (see mbar_wait); no cluster multicast.
@@ -50,6 +54,33 @@ struct PfBars {
 };
 constexpr int PF_SMEM = PF_DATA + (int)sizeof(PfBars);
 static_assert(PF_SMEM <= 232448, "prefill shared memory exceeds the 227 KiB per-CTA limit");
+
+// eight consecutive elements, 16-byte (bf16) or 2 x 16-byte (fp32) accesses
+__device__ __forceinline__ void load8v(const __nv_bfloat16 *src, float (&x)[8])
+{
+    const uint4 u = *reinterpret_cast<const uint4 *>(src);
+    const __nv_bfloat162 *b = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 f = __bfloat1622float2(b[i]); x[2 * i] = f.x; x[2 * i + 1] = f.y; }
+}
+__device__ __forceinline__ void load8v(const float *src, float (&x)[8])
+{
+    const float4 a = reinterpret_cast<const float4 *>(src)[0], b = reinterpret_cast<const float4 *>(src)[1];
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ void store8v(__nv_bfloat16 *dst, const float (&y)[8])
+{
+    uint4 u;
+    __nv_bfloat162 *b = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(dst) = u;
+}
+__device__ __forceinline__ void store8v(float *dst, const float (&y)[8])
+{
+    reinterpret_cast<float4 *>(dst)[0] = make_float4(y[0], y[1], y[2], y[3]);
+    reinterpret_cast<float4 *>(dst)[1] = make_float4(y[4], y[5], y[6], y[7]);
+}
 
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(PF_THREADS, 1)
@@ -299,25 +330,45 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_wait(&bars.pv_done, (nt - 1) & 1);
         tc::fence_after();
         {
-            // epilogue with the 32x32b shape: thread = tile row 32 quarter + lane,
-            // O columns 128 u .. 128 u + 127
-            const int row = 32 * quarter + lane, srow = q0 + row;
+            // epilogue, part 1: O / l through the 32x32b shape (thread = tile row
+            // 32 quarter + lane, O columns 128 u ..) into fp32 staging rows in the
+            // K buffers, which the last PV has finished with. 16-byte chunk c of
+            // row r sits at chunk c ^ (r & 7): a warp's 32 rows spread over all banks.
+            const int row = 32 * quarter + lane;
             const uint32_t qoff = (uint32_t)(32 * quarter) << 16;
             const float inv_l = 1.f / bars.lsum[row];
-            const bool valid = srow < p.S;
-            const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD;
-            TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD;
+            float *stage = reinterpret_cast<float *>(sK);
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
                 float o[32];
                 const int d0 = 128 * u + 32 * c;
                 tc::ld32(tO + d0 + qoff, o);
                 tc::wait_ld();
-                if (valid) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        out[d0 + e] = from_f32<TO>(o[e] * inv_l * sigmoidf_(to_f32(gate[d0 + e])));
+                for (int e = 0; e < 8; ++e) {
+                    const int ch = (d0 >> 2) + e;
+                    *reinterpret_cast<float4 *>(stage + row * PF_HD + ((ch ^ (row & 7)) << 2)) =
+                        make_float4(o[4 * e] * inv_l, o[4 * e + 1] * inv_l, o[4 * e + 2] * inv_l, o[4 * e + 3] * inv_l);
                 }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(PF_SOFTMAX) : "memory");
+            // part 2: a warp per row, lane = 8 head dims: coalesced gate loads and
+            // ctx stores, ctx = O / l * sigmoid(gate)
+            const int w = warp - 2;
+#pragma unroll 1
+            for (int r = w; r < PF_BM; r += PF_SOFTMAX / 32) {
+                const int srow = q0 + r;
+                if (srow >= p.S) break;
+                const float4 a0 = *reinterpret_cast<const float4 *>(stage + r * PF_HD + (((2 * lane) ^ (r & 7)) << 2));
+                const float4 a1 = *reinterpret_cast<const float4 *>(stage + r * PF_HD + (((2 * lane + 1) ^ (r & 7)) << 2));
+                const float o[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD + 8 * lane;
+                TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD + 8 * lane;
+                float gv[8], y[8];
+                load8v(gate, gv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = o[e] * sigmoidf_(gv[e]);
+                store8v(out, y);
             }
         }
     }
@@ -332,6 +383,8 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st)
 {
+    // the epilogue reads the gate and writes ctx with 16-byte vectors
+    if (((uintptr_t)a.qg | (uintptr_t)a.ctx) & 15) return cudaErrorMisalignedAddress;
     dim3 grid(a.n_qtiles * a.H), block(PF_THREADS);
     auto run = [&](auto kern) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
