@@ -47,9 +47,17 @@ int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, 
     if (splits > 1) {
         la.part = (float *)scratch(S_LPART, (size_t)splits * S * t->O * 4);
         if (!la.part) return 0;
+        // per-tile arrival counters (used when bn == 16): zeroed when the slot is (re)allocated, and
+        // the last split of each tile puts its counter back to zero
+        const size_t need = (size_t)tiles * sizeof(int);
+        if (G.slot_bytes[S_LCNT] < need) {
+            if (!scratch(S_LCNT, need)) return 0;
+            CK(cudaMemsetAsync(G.slot[S_LCNT], 0, G.slot_bytes[S_LCNT], stream()));
+        }
+        la.tile_cnt = (int *)G.slot[S_LCNT];
     }
     CK(launch_linear(t->tm, tx, la, bn, splits, stream()));
-    g_launches += splits > 1 ? 2 : 1;
+    g_launches += (splits > 1 && bn > 16) ? 2 : 1;
     return 1;
 }
 

@@ -120,6 +120,8 @@ struct LinearArgs {
     int S, I, O;
     int kchunks;          // 64-element K chunks per split (set by launch_linear)
     int y_bf16;
+    int *tile_cnt;        // split-K arrival counters, one per output tile, zero between
+                          // launches (nullptr = a separate reduce kernel adds the splits)
 };
 cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
                           cudaStream_t st);

@@ -4,10 +4,12 @@
 //
 // One CTA = 128 output features x BN tokens (BN = 16..256 by S, so decode with
 // a handful of tokens is a weight-streaming pass), K walked in 64-element
-// (128 B) steps through a 4-stage TMA ring. W is the M operand (K-major rows),
+// (128 B) steps through a TMA ring of 4 (BN = 256) to 12 (BN = 16) stages. W is the M operand (K-major rows),
 // x the N operand (K-major rows); both 128B-swizzled. When the output tiles
 // cannot fill the GPU (decode), K is split over blockIdx.z and the partial sums
-// are added in split order by linear_reduce_kernel (deterministic).
+// are added in split order (deterministic): for up to 16 tokens by the last
+// split of each output tile to arrive (an atomic counter per tile), with no
+// second launch; for more tokens by linear_reduce_kernel.
 // Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 = epilogue
 // (TMEM lane = output feature; stores are contiguous along o for each token).
 #include "common.cuh"
@@ -16,13 +18,17 @@
 
 namespace coli {
 
-constexpr int LN_BM = 128, LN_BK = 64, LN_STAGES = 4;
+constexpr int LN_BM = 128, LN_BK = 64;
 constexpr int LN_A_BYTES = LN_BM * LN_BK * 2;   // 16 KiB
 
 template <int BN> struct LinSmem {
     static constexpr int B_BYTES = BN * LN_BK * 2;
     static constexpr int STAGE = LN_A_BYTES + B_BYTES;
-    static constexpr int TOTAL = LN_STAGES * STAGE + 1024;
+    // as many ring stages as ~220 KiB holds (at most 12): a weight-streaming
+    // decode pass needs many bytes in flight per SM to cover HBM latency
+    static constexpr int STAGES_FIT = (220 * 1024) / STAGE;
+    static constexpr int STAGES = STAGES_FIT > 12 ? 12 : (STAGES_FIT < 2 ? 2 : STAGES_FIT);
+    static constexpr int TOTAL = STAGES * STAGE + 1024;
     static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
@@ -30,10 +36,12 @@ template <int BN>
 __global__ void __launch_bounds__(192, 1)
 linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, LinearArgs a)
 {
+    constexpr int LN_STAGES = LinSmem<BN>::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[LN_STAGES], empty[LN_STAGES], done;
     __shared__ uint32_t tmem_base;
+    __shared__ int last_split;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int o0 = blockIdx.x * LN_BM, s0 = blockIdx.y * BN, z = blockIdx.z;
     const int nk = (a.I + LN_BK - 1) / LN_BK;
@@ -53,9 +61,19 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     if (warp == 0) {
         if (lane == 0) {
             tma_prefetch_desc(&tmW); tma_prefetch_desc(&tmX);
-            for (int i = 0; i < cnt; ++i) {
+            // the weights do not depend on the previous kernel: the first ring's
+            // worth streams in while that kernel finishes (programmatic launch)
+            const int pre = min(cnt, LN_STAGES);
+            for (int i = 0; i < pre; ++i) {
+                mbar_expect_tx(&full[i], LinSmem<BN>::STAGE);
+                tma_load_2d(sm + i * LinSmem<BN>::STAGE, &tmW, (k0 + i) * LN_BK, o0, &full[i]);
+            }
+            griddep_wait();
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(sm + i * LinSmem<BN>::STAGE + LN_A_BYTES, &tmX, (k0 + i) * LN_BK, s0, &full[i]);
+            for (int i = pre; i < cnt; ++i) {
                 const int st = i % LN_STAGES;
-                if (i >= LN_STAGES) mbar_wait(&empty[st], ((i / LN_STAGES) + 1) & 1);
+                mbar_wait(&empty[st], ((i / LN_STAGES) + 1) & 1);
                 uint8_t *sA = sm + st * LinSmem<BN>::STAGE, *sB = sA + LN_A_BYTES;
                 mbar_expect_tx(&full[st], LinSmem<BN>::STAGE);
                 tma_load_2d(sA, &tmW, (k0 + i) * LN_BK, o0, &full[st]);
@@ -82,10 +100,12 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     } else {
         const int q = warp & 3, o = o0 + q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        griddep_wait();                       // y / partials / counters may still be in use
         if (cnt > 0) {
             mbar_wait(&done, 0);
             tc::fence_after();
         }
+        griddep_launch();
         for (int c0 = 0; c0 < BN; c0 += 16) {
             float v[16];
             if (cnt > 0) {
@@ -108,6 +128,40 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
             }
         }
         tc::fence_before();
+        if (BN == 16 && a.part && a.tile_cnt) {
+            // split-K: the last split of this output tile to arrive adds the
+            // partials in split order (the same sum as linear_reduce_kernel)
+            __threadfence();
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            const int tile = blockIdx.x + gridDim.x * blockIdx.y;
+            if (threadIdx.x == 64) last_split = atomicAdd(&a.tile_cnt[tile], 1) == (int)gridDim.z - 1;
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (last_split) {
+                __threadfence();
+                const size_t n = (size_t)a.S * a.O;
+                if (o < a.O) {
+                    // up to 16 token rows: each split's loads go out together
+                    const int rows = min(a.S - s0, min(BN, 16));
+                    float acc[16];
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+                    for (int zz = 0; zz < (int)gridDim.z; ++zz) {
+                        const float *pz = a.part + zz * n + (size_t)s0 * a.O + o;
+#pragma unroll
+                        for (int r = 0; r < 16; ++r)
+                            if (r < rows) acc[r] += __ldcg(pz + (size_t)r * a.O);
+                    }
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) {
+                        if (r >= rows) break;
+                        const size_t idx = (size_t)(s0 + r) * a.O + o;
+                        if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[idx] = __float2bfloat16_rn(acc[r]);
+                        else static_cast<float *>(a.y)[idx] = acc[r];
+                    }
+                }
+                if (threadIdx.x == 64) a.tile_cnt[tile] = 0;
+            }
+        }
     }
     __syncthreads();
     if (warp == 1) {
@@ -152,23 +206,34 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
 {
     const int nk = (a.I + LN_BK - 1) / LN_BK;
     a.kchunks = (nk + splits - 1) / splits;
+    splits = (nk + a.kchunks - 1) / a.kchunks;   // no split without K chunks
+    if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
     dim3 grid((a.O + LN_BM - 1) / LN_BM, (a.S + bn - 1) / bn, splits);
-    auto run = [&](auto kern, int smem) -> cudaError_t {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        kern<<<grid, 192, smem, st>>>(tmW, tmX, a);
-        return cudaGetLastError();
+    static bool attr_set[5] = {};   // the shared-memory opt-in, once per instantiation
+    auto run = [&](auto kern, int smem, int which) -> cudaError_t {
+        if (!attr_set[which]) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            attr_set[which] = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid; cfg.blockDim = dim3(192); cfg.dynamicSmemBytes = smem; cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr; cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, tmW, tmX, a);
     };
     cudaError_t e;
     switch (bn) {
-    case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL); break;
-    case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL); break;
-    case 64: e = run(linear_kernel<64>, LinSmem<64>::TOTAL); break;
-    case 128: e = run(linear_kernel<128>, LinSmem<128>::TOTAL); break;
-    case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL); break;
+    case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL, 0); break;
+    case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL, 1); break;
+    case 64: e = run(linear_kernel<64>, LinSmem<64>::TOTAL, 2); break;
+    case 128: e = run(linear_kernel<128>, LinSmem<128>::TOTAL, 3); break;
+    case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL, 4); break;
     default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess || splits == 1) return e;
+    if (e != cudaSuccess || splits == 1 || (bn == 16 && a.tile_cnt)) return e;
     const size_t n = (size_t)a.S * a.O;
     linear_reduce_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(a, splits);
     return cudaGetLastError();
