@@ -413,7 +413,7 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     p.Qh = (float *)scratch(S_GQ, (size_t)KH * S * 128 * 4);
     p.Kh = (float *)scratch(S_GK, (size_t)KH * S * 128 * 4);
     p.KT = (float *)scratch(S_GKT, (size_t)KH * nch * 64 * 128 * 4);
-    p.Vh = (float *)scratch(S_GV, (size_t)VH * S * 128 * 4);
+    p.VT = (float *)scratch(S_GV, (size_t)VH * nch * 64 * 128 * 4);
     p.GL = (float *)scratch(S_GL, (size_t)VH * S * 4);
     p.BETA = (float *)scratch(S_GB, (size_t)VH * S * 4);
     p.W = (float *)scratch(S_GW, (size_t)nch * VH * 64 * 128 * 4);
@@ -435,12 +435,12 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
         p.XS = (float *)scratch(S_GXS, (size_t)(p.nseg - 1) * VH * 128 * 256 * 4);
         if (!p.Hs || !p.XS) return 0;
     }
-    if (!p.Qh || !p.Kh || !p.KT || !p.Vh || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
+    if (!p.Qh || !p.Kh || !p.KT || !p.VT || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
     p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
     GdnPrefillMaps m;
     if (!make_f32_3d(&m.Q, p.Qh, 128, S, KH, 32, 64) || !make_f32_3d(&m.K, p.Kh, 128, S, KH, 32, 64) ||
-        !make_f32_3d(&m.V, p.Vh, 128, S, VH, 32, 64) ||
+        !make_f32_3d(&m.V, p.VT, 64, 128, nch * VH, 32, 128) ||
         !make_f32_3d(&m.W, p.W, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||

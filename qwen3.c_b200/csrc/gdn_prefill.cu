@@ -17,13 +17,14 @@
 // Kernels
 //   gdn_pf_prologue_kernel  per (64-token run, K head): sliding conv4 (history
 //                           carried in from the previous call) + SiLU,
-//                           q/k L2 norm, gates -> Q, K, V (fp32, head-major),
-//                           K also transposed per chunk, log-decay and beta
-//                           per V head.
+//                           q/k L2 norm, gates -> Q, K (fp32, head-major),
+//                           K^T and V^T per chunk (the B operands of W and U),
+//                           log-decay and beta per V head.
 //   gdn_pf_hist_kernel      carries the last 3 pre-conv rows out as history.
 //   gdn_pf_prep_kernel      per (chunk, V head), fully parallel: K K^T and
-//                           Q K^T on tf32 mma.sync, T by forward substitution
-//                           in fp32, then W, U and the decay-masked M.
+//                           Q K^T on tcgen05 (kind::tf32), T by blocked
+//                           forward substitution in fp32, then W and U on
+//                           tcgen05, and the decay-masked M.
 //   gdn_pf_scan_kernel      per (V head, 64-column block of the state, segment
 //                           of chunks): walks the chunks in order with the
 //                           state slice in TMEM, products on tcgen05
@@ -188,15 +189,18 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
     // K of this chunk also goes out transposed ([dk][64 tokens], tokens past S
     // zero), the A operand of the scan's state update; 4 tokens per store.
     float *kt = p.KT + (((size_t)kh * gridDim.x + blockIdx.x) * PFG_D + t) * PFG_C;
+    // V^T likewise, per V head ([dv][64 tokens], tf32-rounded: the B operand of U)
+    float *vt0 = p.VT + (((size_t)(2 * kh) * gridDim.x + blockIdx.x) * PFG_D + t) * PFG_C;
+    float *vt1 = vt0 + (size_t)gridDim.x * PFG_D * PFG_C;
     float xn[4];                                   // next token's inputs, loaded one token ahead
 #pragma unroll
     for (int c = 0; c < 4; ++c) xn[c] = to_f32(x[(size_t)s_begin * CD + ch[c]]);
     for (int s4 = s_begin; s4 < s_end; s4 += 4) {
-        float kb[4];
+        float kb[4], vb[2][4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int s = s4 + u;
-            kb[u] = 0.f;
+            kb[u] = 0.f; vb[0][u] = 0.f; vb[1][u] = 0.f;
             if (s >= s_end) continue;              // uniform across the CTA
             const int par = s & 1;
             float xv[4], out[4];
@@ -232,21 +236,29 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const int vh = kh * 2 + j, vg = kg * 2 + j;  // local / input-layout V head
-                p.Vh[((size_t)vh * S + s) * PFG_D + t] = out[2 + j];
+                vb[j][u] = tf32r(out[2 + j]);
                 if (t == j) gdn_gates(p, s, vh, vg, VHin, static_cast<const TI *>(p.a), static_cast<const TI *>(p.b));
             }
         }
         *reinterpret_cast<float4 *>(kt + (s4 - s_begin)) = make_float4(kb[0], kb[1], kb[2], kb[3]);
+        *reinterpret_cast<float4 *>(vt0 + (s4 - s_begin)) = make_float4(vb[0][0], vb[0][1], vb[0][2], vb[0][3]);
+        *reinterpret_cast<float4 *>(vt1 + (s4 - s_begin)) = make_float4(vb[1][0], vb[1][1], vb[1][2], vb[1][3]);
     }
-    for (int i = (s_end - s_begin + 3) & ~3; i < PRO_T; i += 4)
+    for (int i = (s_end - s_begin + 3) & ~3; i < PRO_T; i += 4) {
         *reinterpret_cast<float4 *>(kt + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(vt0 + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(vt1 + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 }
 
 // bf16 inputs: the same prologue with the CTA's whole input tile (64 tokens x
 // the 512 channels of one K head: q, k and its two V heads) brought into
 // shared memory with wide loads first, then 8 warps x 8 tokens; the q/k norm
 // is a warp reduction (lane = 4 q, 4 k and 8 v channels), and K^T leaves
-// through a shared-memory transpose as contiguous rows.
+// through a shared-memory transpose as contiguous rows. V goes back into the
+// token's own input row (1 KiB: 512 bf16 in, 256 fp32 out, word c stored at
+// c ^ (token % 32) so that both the row writes and the column reads are
+// conflict-free) and leaves as V^T rows after the token loop.
 constexpr int PRT_CH = 512;                  // channels of one K head's q|k|v0|v1
 constexpr int PRT_KT_LD = PRO_T + 1;
 size_t gdn_prologue_tile_smem()
@@ -303,6 +315,7 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
         const int lc = j * 32 + lane;
         h0[j] = xin(r0 - 3, lc); h1[j] = xin(r0 - 2, lc); h2[j] = xin(r0 - 1, lc);
     }
+    __syncthreads();                         // halo rows read before their owners overwrite them with V
     for (int rr = 0; rr < PRO_T / 8; ++rr) {
         const int r = r0 + rr, s = s_begin + r;
         if (r >= nrow) break;                // warp-uniform
@@ -335,11 +348,10 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
             p.Kh[((size_t)kh * S + s) * PFG_D + c] = kv;
             sKT[c * PRT_KT_LD + r] = kv;
         }
+        __syncwarp();                        // every lane has read row r
+        float *vrow = reinterpret_cast<float *>(sX + r * PRT_CH);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int vh = kh * 2 + (j >> 2);
-            p.Vh[((size_t)vh * S + s) * PFG_D + (j & 3) * 32 + lane] = out[8 + j];
-        }
+        for (int j = 0; j < 8; ++j) vrow[(j * 32 + lane) ^ (r & 31)] = out[8 + j];
         if (lane < 2)   // local / input-layout V head
             gdn_gates(p, s, kh * 2 + lane, kg * 2 + lane, VHin, static_cast<const __nv_bfloat16 *>(p.a),
                       static_cast<const __nv_bfloat16 *>(p.b));
@@ -355,6 +367,15 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
         v.z = t4 + 2 < nrow ? sKT[d * PRT_KT_LD + t4 + 2] : 0.f;
         v.w = t4 + 3 < nrow ? sKT[d * PRT_KT_LD + t4 + 3] : 0.f;
         *reinterpret_cast<float4 *>(kt + d * PFG_C + t4) = v;
+    }
+    // V^T of the chunk per V head ([dv][64 tokens], tokens past S zero, tf32):
+    // a warp writes 32 consecutive tokens of one row
+    float *vt = p.VT + ((size_t)(2 * kh) * gridDim.x + blockIdx.x) * PFG_D * PFG_C;
+    for (int e = tid; e < 2 * PFG_D * PFG_C; e += 256) {
+        const int c = e >> 6, t = e & 63;     // c = local V channel (head c / 128)
+        const float *vrow = reinterpret_cast<const float *>(sX + t * PRT_CH);
+        const float v = t < nrow ? tf32r(vrow[c ^ (t & 31)]) : 0.f;
+        vt[(size_t)(c >> 7) * gridDim.x * PFG_D * PFG_C + (c & 127) * PFG_C + t] = v;
     }
 }
 
@@ -379,8 +400,21 @@ __global__ void gdn_pf_hist_kernel(GdnPrefillArgs p)
 // ---------------------------------------------------------------- chunk prep
 constexpr int PREP_LD = 68;  // padded row stride (floats) of A / T in shared memory
 
-// 8 warps: warp w owns token rows 16 (w % 4).. of K K^T (w < 4) or Q K^T
-// (w >= 4), and later the same rows of W (w < 4) or U (w >= 4).
+// Byte offset of element (row r, k) in a K-major 128B-swizzled fp32 tile with
+// `rows` rows per k-atom (32 fp32 of k per 128 B row, 8-row groups 1 KiB apart).
+__device__ __forceinline__ uint32_t kmaj_off(int rows, int r, int k)
+{
+    return (uint32_t)((k >> 5) * rows * 128 + r * 128 + ((((k & 31) >> 2) ^ (r & 7)) << 4) + (k & 3) * 4);
+}
+
+// The four products run on tcgen05 (kind::tf32, M = 64, one issuing thread,
+// accumulators in 256 TMEM columns): K K^T and Q K^T (N = 64, K = 128 dk),
+// then W = (T diag(beta gamma)) K and U = (T diag(beta)) V (N = 128 dk/dv,
+// K = 64 tokens) with K^T / V^T from the prologue as the K-major B operands
+// and the scaled T written K-major by the threads. The M = 64 accumulator
+// puts row 16 q + i in TMEM lane 32 q + i, so warp w reads rows 16 (w % 4)..
+// through the 16x256b shape, which is the mma.sync fragment layout.
+// Warps 0-3 own the K K^T / W rows, warps 4-7 the Q K^T / U rows.
 constexpr int PREP_THREADS = 256;
 __global__ void __launch_bounds__(PREP_THREADS)
 gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -389,13 +423,14 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 {
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *sQV = base;                          // Q chunk, later V chunk [64 x 128] swizzled
+    float *sQV = base;                          // Q chunk [64 x 128], later V^T [128 x 64] swizzled
     float *sK = sQV + PFG_C * PFG_D;            // K chunk, later K^T [128 x 64] swizzled
-    float *sA = sK + PFG_C * PFG_D;             // [64][68] strictly lower A
-    float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1
+    float *sA = sK + PFG_C * PFG_D;             // [64][68] strictly lower A; later T diag(beta gamma), K-major
+    float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1; later T diag(beta), K-major
     float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
     __shared__ float G[PFG_C], bet[PFG_C], bgam[PFG_C];   // bgam = beta e^G
-    __shared__ __align__(8) uint64_t bar_qk, bar_v;
+    __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_mma;
+    __shared__ uint32_t tmem_base;
 
     const int n = blockIdx.x, h = blockIdx.y, kh = h >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
@@ -403,9 +438,15 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (tid == 0) {
         mbar_init(&bar_qk, 1);
         mbar_init(&bar_v, 1);
+        mbar_init(&bar_mma, 1);
         fence_mbar_init();
     }
+    if (warp == 0) tc::alloc(&tmem_base, 256);
+    tc::fence_before();
     __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = tmem_base;
+    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     if (tid == 0) {
         mbar_expect_tx(&bar_qk, 2 * PFG_C * PFG_D * 4);
         for (int c = 0; c < 4; ++c) {
@@ -421,29 +462,32 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     __syncthreads();
     if (tid < PFG_C) bgam[tid] = bet[tid] * expf(G[tid]);   // read after later barriers
-    mbar_wait(&bar_qk, 0);  // a time-out raises the device error word
-
-    // K K^T (warps 0-3) or Q K^T (warps 4-7) for this warp's 16 rows, all 64 columns
-    const int r0 = (warp & 3) * 16, second = warp >> 2;
-    {
-        float acc[8][4];
+    if (tid == 0) {
+        // K K^T -> columns 0..63, Q K^T -> 64..127 (Q and K are tf32 from the prologue)
+        const bool ok = mbar_wait(&bar_qk, 0);
+        tc::fence_after();
+        if (ok) {
+            constexpr uint32_t ID = tc::idesc_tf32(64, 64);
+            const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQV);
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-        // Q and K were rounded to tf32 by the prologue: ldmatrix feeds them as is
-        const uint32_t aKs = smem_u32(sK), aAs = second ? smem_u32(sQV) : aKs;
-#pragma unroll 2
-        for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            uint32_t a[4];
-            lda_sw(aAs, r0, ks, lane, a);
-#pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-                uint32_t b0, b1;
-                ldb_sw(aKs, nt * 8, ks, lane, b0, b1);
-                mma_tf32(acc[nt], a[0], a[1], a[2], a[3], b0, b1);
+            for (int ks = 0; ks < PFG_D / 8; ++ks) {
+                const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+                tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aK + off), ID, ks > 0);
+                tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aK + off), ID, ks > 0);
             }
         }
+        tc::commit(&bar_mma);
+    }
+    mbar_wait(&bar_mma, 0);   // a time-out raises the device error word
+    tc::fence_after();
+
+    // this warp's 16 rows of K K^T (w < 4) or Q K^T (w >= 4), all 64 columns:
+    // the decay-masked A to shared memory, M to global
+    const int r0 = (warp & 3) * 16, second = warp >> 2;
+    {
+        float acc[32];
+        tc::ld16x256_x8(tbase + lane_off + (second ? 64u : 0u), acc);
+        tc::wait_ld();
         float *Mg = p.M + ((size_t)n * p.VH + h) * PFG_C * PFG_C;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
@@ -452,7 +496,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const int i = r0 + g + 8 * hr, j = nt * 8 + 2 * tq;
                 const float d0 = ex2_approx((G[i] - G[j]) * 1.4426950408889634f);
                 const float d1 = ex2_approx((G[i] - G[j + 1]) * 1.4426950408889634f);
-                const float v0 = acc[nt][2 * hr], v1 = acc[nt][2 * hr + 1];
+                const float v0 = acc[4 * nt + 2 * hr], v1 = acc[4 * nt + 2 * hr + 1];
                 if (second) {
                     *reinterpret_cast<float2 *>(Mg + i * PFG_C + j) =
                         make_float2(j <= i ? tf32r(d0 * v0) : 0.f, j + 1 <= i ? tf32r(d1 * v1) : 0.f);
@@ -463,13 +507,14 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
         }
     }
+    tc::fence_before();
     __syncthreads();
-    // V replaces Q and K^T replaces K in shared memory while T is solved
+    // V^T replaces Q and K^T replaces K in shared memory while T is solved
+    // (the product MMAs that read them have completed)
     if (tid == 0) {
-        fence_proxy_async();
         mbar_expect_tx(&bar_v, 2 * PFG_C * PFG_D * 4);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sQV + c * PFG_C * 32, &tmV, 32 * c, s0, h, &bar_v);
         const int nch = (p.S + PFG_C - 1) / PFG_C;
+        for (int c = 0; c < 2; ++c) tma_load_3d(sQV + c * PFG_D * 32, &tmV, 32 * c, 0, h * nch + n, &bar_v);
         for (int c = 0; c < 2; ++c) tma_load_3d(sK + c * PFG_D * 32, &tmKT, 32 * c, 0, kh * nch + n, &bar_v);
     }
     // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
@@ -526,60 +571,73 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     }
     __syncthreads();
-    mbar_wait(&bar_v, 0);
-
-    // W = (T diag(beta gamma)) K (warps 0-3; K^T rows by ldmatrix) or
-    // U = T (diag(beta) V) (warps 4-7) for this warp's 16 rows, 128 columns
-    // in two halves
-    float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
-    const uint32_t aKT = smem_u32(sK);
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-        float w[8][4];
+    // T diag(beta gamma) and T diag(beta) as K-major tf32 A operands, over A and T
+    {
+        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        float t[16];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(sT + i * PREP_LD + j0 + 4 * q);
+            t[4 * q] = v.x; t[4 * q + 1] = v.y; t[4 * q + 2] = v.z; t[4 * q + 3] = v.w;
+        }
+        __syncthreads();
+        uint8_t *aw = reinterpret_cast<uint8_t *>(sA), *au = reinterpret_cast<uint8_t *>(sT);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) w[nt][e] = 0.f;
-        if (!second) {
-#pragma unroll 2
+        for (int q = 0; q < 4; ++q) {
+            const int j = j0 + 4 * q;
+            *reinterpret_cast<float4 *>(aw + kmaj_off(PFG_C, i, j)) =
+                make_float4(tf32r(t[4 * q] * bgam[j]), tf32r(t[4 * q + 1] * bgam[j + 1]),
+                            tf32r(t[4 * q + 2] * bgam[j + 2]), tf32r(t[4 * q + 3] * bgam[j + 3]));
+            *reinterpret_cast<float4 *>(au + kmaj_off(PFG_C, i, j)) =
+                make_float4(tf32r(t[4 * q] * bet[j]), tf32r(t[4 * q + 1] * bet[j + 1]),
+                            tf32r(t[4 * q + 2] * bet[j + 2]), tf32r(t[4 * q + 3] * bet[j + 3]));
+        }
+        fence_proxy_async();
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        // W -> columns 0..127, U -> 128..255 (K^T / V^T rows are the B operands)
+        const bool ok = mbar_wait(&bar_v, 0);
+        tc::fence_after();
+        if (ok) {
+            constexpr uint32_t ID = tc::idesc_tf32(64, 128);
+            const uint32_t aW = smem_u32(sA), aU = smem_u32(sT), aKT = smem_u32(sK), aVT = smem_u32(sQV);
+#pragma unroll
             for (int ks = 0; ks < PFG_C / 8; ++ks) {
-                const int c0 = ks * 8 + tq, c1 = c0 + 4;
-                const float s0 = bgam[c0], s1 = bgam[c1];
-                const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0] * s0), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0] * s0);
-                const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1] * s1), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1] * s1);
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-                    uint32_t b0, b1;   // K was rounded to tf32 by the prologue
-                    ldb_sw_rows(aKT, PFG_D, half * 64 + nt * 8, ks, lane, b0, b1);
-                    mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
-                }
-            }
-        } else {
-#pragma unroll 2
-            for (int ks = 0; ks < PFG_C / 8; ++ks) {
-                const int c0 = ks * 8 + tq, c1 = c0 + 4;
-                const uint32_t a0 = f2tf32(sT[(r0 + g) * PREP_LD + c0]), a1 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c0]);
-                const uint32_t a2 = f2tf32(sT[(r0 + g) * PREP_LD + c1]), a3 = f2tf32(sT[(r0 + g + 8) * PREP_LD + c1]);
-                const float s0 = bet[c0], s1 = bet[c1];
-#pragma unroll
-                for (int nt = 0; nt < 8; ++nt) {
-                    const int col = half * 64 + nt * 8 + g;
-                    const uint32_t b0 = f2tf32(s0 * sw_ld(sQV, PFG_C, c0, col));
-                    const uint32_t b1 = f2tf32(s1 * sw_ld(sQV, PFG_C, c1, col));
-                    mma_tf32(w[nt], a0, a1, a2, a3, b0, b1);
-                }
+                const uint32_t oa = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+                const uint32_t ob = (ks >> 2) * (PFG_D * 128) + (ks & 3) * 32;
+                tc::mma_tf32(tbase, tc::desc_k_sw128(aW + oa), tc::desc_k_sw128(aKT + ob), ID, ks > 0);
+                tc::mma_tf32(tbase + 128, tc::desc_k_sw128(aU + oa), tc::desc_k_sw128(aVT + ob), ID, ks > 0);
             }
         }
+        tc::commit(&bar_mma);
+    }
+    mbar_wait(&bar_mma, 1);
+    tc::fence_after();
+    // this warp's 16 rows of W (w < 4) or U (w >= 4), 128 columns in two halves
+    float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+        float w[32];
+        tc::ld16x256_x8(tbase + lane_off + (second ? 128u : 0u) + 64 * half, w);
+        tc::wait_ld();
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int col = half * 64 + nt * 8 + 2 * tq;
             const int ra = r0 + g, rb = ra + 8;
             // W feeds the walk's tensor core as is: rounded to tf32 here
-            const float x0 = second ? w[nt][0] : tf32r(w[nt][0]), x1 = second ? w[nt][1] : tf32r(w[nt][1]);
-            const float x2 = second ? w[nt][2] : tf32r(w[nt][2]), x3 = second ? w[nt][3] : tf32r(w[nt][3]);
+            const float x0 = second ? w[4 * nt] : tf32r(w[4 * nt]), x1 = second ? w[4 * nt + 1] : tf32r(w[4 * nt + 1]);
+            const float x2 = second ? w[4 * nt + 2] : tf32r(w[4 * nt + 2]), x3 = second ? w[4 * nt + 3] : tf32r(w[4 * nt + 3]);
             *reinterpret_cast<float2 *>(Og + ra * PFG_D + col) = make_float2(x0, x1);
             *reinterpret_cast<float2 *>(Og + rb * PFG_D + col) = make_float2(x2, x3);
         }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        tc::dealloc(tbase, 256);
     }
 }
 
@@ -627,12 +685,6 @@ template <int NC> struct ScanSmem {
     static_assert(TOTAL + 1024 <= 232448, "scan shared memory");
 };
 
-// Byte offset of element (row r, k) in a K-major 128B-swizzled fp32 tile with
-// `rows` rows per k-atom (32 fp32 of k per 128 B row, 8-row groups 1 KiB apart).
-__device__ __forceinline__ uint32_t kmaj_off(int rows, int r, int k)
-{
-    return (uint32_t)((k >> 5) * rows * 128 + r * 128 + ((((k & 31) >> 2) ^ (r & 7)) << 4) + (k & 3) * 4);
-}
 
 // Grid: blockIdx.x = (seg * VH + h) * NB + blk, NB = 128 / NC state blocks
 // (replay) or 256 / NC blocks of [Phi | Psi] (TRANS, segments 0 .. nseg-2).

@@ -87,7 +87,7 @@ struct GdnPrefillArgs {
     void *y;                              // [S][VH*VD]
     float *Qh, *Kh;                       // scratch [KH][S][128]
     float *KT;                            // scratch [KH][nchunks][128][64] (K^T per chunk)
-    float *Vh;                            // scratch [VH][S][128]
+    float *VT;                            // scratch [VH][nchunks][128][64] (V^T per chunk, tf32)
     float *GL, *BETA;                     // scratch [VH][S]
     float *W, *U;                         // scratch [nchunks][VH][64][128]
     float *M;                             // scratch [nchunks][VH][64][64]
