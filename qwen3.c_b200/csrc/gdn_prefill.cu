@@ -520,9 +520,9 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
     // diagonal blocks by forward substitution (one column per thread), then
     // T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one block diagonal at a time.
+    // The blocks above the diagonal are never written: the operand build
+    // below treats them as zero.
     {
-        for (int e = tid; e < PFG_C * PFG_C; e += PREP_THREADS) sT[(e >> 6) * PREP_LD + (e & 63)] = 0.f;
-        __syncthreads();
         if (tid < 64) {   // column c of diagonal block o, kept in registers
             const int o = (tid >> 4) * 16, c = tid & 15;
             float t[16];
@@ -577,7 +577,8 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         float t[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float4 v = *reinterpret_cast<const float4 *>(sT + i * PREP_LD + j0 + 4 * q);
+            const float4 v = (j0 >> 4) > (i >> 4) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                  : *reinterpret_cast<const float4 *>(sT + i * PREP_LD + j0 + 4 * q);
             t[4 * q] = v.x; t[4 * q + 1] = v.y; t[4 * q + 2] = v.z; t[4 * q + 3] = v.w;
         }
         __syncthreads();
