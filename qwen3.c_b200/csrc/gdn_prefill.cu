@@ -1014,6 +1014,20 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         for (int c = 0; c < 2; ++c) tma_load_3d(sDT + c * PFG_D * 32, &tmDt, 32 * c, 0, n * VH + h, &bar);
         for (int c = 0; c < 2; ++c) tma_load_3d(sQT + c * PFG_D * 32, &tmQH, 32 * c, 0, n * VH + h, &bar);
     }
+    // the gate rows this thread stores at the end, loaded now so that their
+    // latency overlaps the tile loads and the products (item e = tid + 256 k:
+    // token e / 16, 8 columns from 8 (e % 16))
+    const TI *z = static_cast<const TI *>(p.z);
+    constexpr int ZW = sizeof(TI) == 2 ? 1 : 2;          // 16-byte pieces per 8 gate values
+    uint4 zpre[4][ZW];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = tid + 256 * k, tok = n * PFG_C + (e >> 4);
+        const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + (e & 15) * 8;
+#pragma unroll
+        for (int w = 0; w < ZW; ++w)
+            zpre[k][w] = tok < S ? reinterpret_cast<const uint4 *>(zr)[w] : make_uint4(0u, 0u, 0u, 0u);
+    }
     // warp w: token rows 16 (w % 4).., value columns 64 (w / 4)..
     const int r0 = (warp & 3) * 16, cq = (warp >> 2) * 64;
     __shared__ float rsum[2][PFG_C];
@@ -1063,22 +1077,22 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         *reinterpret_cast<float2 *>(sY + (r0 + g + 8) * YLD + col) = make_float2(y[nt][2] * rb_ * g0, y[nt][3] * rb_ * g1);
     }
     __syncthreads();
-    const TI *z = static_cast<const TI *>(p.z);
     TO *out = static_cast<TO *>(p.y);
-    for (int e = tid; e < PFG_C * (PFG_D / 8); e += 256) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = tid + 256 * k;
         const int row = e >> 4, c8 = (e & 15) * 8, tok = n * PFG_C + row;
         if (tok >= S) continue;
-        const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + c8;
         TO *orow = out + (size_t)tok * VH * VD + h * VD + c8;
         float zv[8], v[8];
         if constexpr (sizeof(TI) == 2) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(zr);
-            const __nv_bfloat16 *zb = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+            const __nv_bfloat16 *zb = reinterpret_cast<const __nv_bfloat16 *>(&zpre[k][0]);
 #pragma unroll
             for (int j = 0; j < 8; ++j) zv[j] = to_f32(zb[j]);
         } else {
-            const float4 z0 = *reinterpret_cast<const float4 *>(zr), z1 = *reinterpret_cast<const float4 *>(zr + 4);
-            zv[0] = z0.x; zv[1] = z0.y; zv[2] = z0.z; zv[3] = z0.w; zv[4] = z1.x; zv[5] = z1.y; zv[6] = z1.z; zv[7] = z1.w;
+            const float *zf = reinterpret_cast<const float *>(&zpre[k][0]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) zv[j] = zf[j];
         }
         const float4 y0 = *reinterpret_cast<const float4 *>(sY + row * YLD + c8);
         const float4 y1 = *reinterpret_cast<const float4 *>(sY + row * YLD + c8 + 4);
