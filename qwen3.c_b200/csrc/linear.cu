@@ -170,6 +170,115 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     }
 }
 
+// Persistent variant for large token counts (BN = 128 / 256, no K split): one
+// CTA per SM walks the output tiles (tile t = blockIdx.x + k gridDim.x, output
+// features fastest) with two TMEM accumulators, so the epilogue of tile j
+// overlaps the MMAs of tile j + 1 and the TMA ring never drains between tiles.
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+linear_persistent_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                         LinearArgs a)
+{
+    constexpr int ST = LinSmem<BN>::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[ST], empty[ST], tfull[2], tempty[2];
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntx = (a.O + LN_BM - 1) / LN_BM, nty = (a.S + BN - 1) / BN, ntiles = ntx * nty;
+    const int nk = (a.I + LN_BK - 1) / LN_BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
+        fence_mbar_init();
+    }
+    if (warp == 1) tc::alloc(&tmem_base, 2 * BN);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tD = tmem_base;
+    griddep_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmW); tma_prefetch_desc(&tmX);
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+                const int o0 = (t % ntx) * LN_BM, s0 = (t / ntx) * BN;
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int st = it % ST;
+                    if (it >= ST && !mbar_wait(&empty[st], ((it / ST) + 1) & 1)) { ok = false; break; }
+                    uint8_t *sA = sm + st * LinSmem<BN>::STAGE, *sB = sA + LN_A_BYTES;
+                    mbar_expect_tx(&full[st], LinSmem<BN>::STAGE);
+                    tma_load_2d(sA, &tmW, k * LN_BK, o0, &full[st]);
+                    tma_load_2d(sB, &tmX, k * LN_BK, s0, &full[st]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_bf16(LN_BM, BN, 0, 0);
+            const uint32_t base = smem_u32(sm);
+            int it = 0, j = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++j) {
+                const int acc = j & 1;
+                if (j >= 2 && !mbar_wait(&tempty[acc], ((j >> 1) + 1) & 1)) break;   // epilogue drained it
+                tc::fence_after();
+                const uint32_t d = tD + acc * BN;
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int st = it % ST;
+                    if (!mbar_wait(&full[st], (it / ST) & 1)) { ok = false; break; }
+                    tc::fence_after();
+                    const uint32_t aA = base + st * LinSmem<BN>::STAGE, aB = aA + LN_A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < LN_BK / 16; ++kk)
+                        tc::mma_bf16(d, tc::desc_k_sw128(aA + kk * 32), tc::desc_k_sw128(aB + kk * 32), idesc,
+                                     (k > 0 || kk > 0) ? 1u : 0u);
+                    tc::commit(&empty[st]);
+                }
+                tc::commit(&tfull[acc]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        int j = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j) {
+            const int acc = j & 1;
+            const int o = (t % ntx) * LN_BM + q * 32 + lane, s0 = (t / ntx) * BN;
+            if (!mbar_wait(&tfull[acc], (j >> 1) & 1)) break;
+            tc::fence_after();
+            const uint32_t d = tD + acc * BN + lane_off;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                tc::ld16(d + c0, v);
+                tc::wait_ld();
+                if (o < a.O) {
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int s = s0 + c0 + jj;
+                        if (s >= a.S) break;
+                        const size_t idx = (size_t)s * a.O + o;
+                        if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[idx] = __float2bfloat16_rn(v[jj]);
+                        else static_cast<float *>(a.y)[idx] = v[jj];
+                    }
+                }
+            }
+            tc::fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+        griddep_launch();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after();
+        tc::dealloc(tmem_base, 2 * BN);
+    }
+}
+
 // y = sum over splits of the partials, in split order.
 __global__ void linear_reduce_kernel(LinearArgs a, int splits)
 {
@@ -209,7 +318,7 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
     splits = (nk + a.kchunks - 1) / a.kchunks;   // no split without K chunks
     if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
     dim3 grid((a.O + LN_BM - 1) / LN_BM, (a.S + bn - 1) / bn, splits);
-    static bool attr_set[5] = {};   // the shared-memory opt-in, once per instantiation
+    static bool attr_set[7] = {};   // the shared-memory opt-in, once per instantiation
     auto run = [&](auto kern, int smem, int which) -> cudaError_t {
         if (!attr_set[which]) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -225,6 +334,15 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
         return cudaLaunchKernelEx(&cfg, kern, tmW, tmX, a);
     };
     cudaError_t e;
+    if (splits == 1 && bn >= 128) {
+        // persistent: one CTA per SM over all output tiles
+        const int tiles = grid.x * grid.y;
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        grid = dim3(std::min(tiles, std::max(sms, 1)), 1, 1);
+        if (bn == 128) return run(linear_persistent_kernel<128>, LinSmem<128>::TOTAL, 5);
+        return run(linear_persistent_kernel<256>, LinSmem<256>::TOTAL, 6);
+    }
     switch (bn) {
     case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL, 0); break;
     case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL, 1); break;
