@@ -610,14 +610,16 @@ def run_linear(be, args, st, peak_hbm):
 
 def run_stack_prefill(be, args, st, peak_tc):
     """BASELINE config 5 (ii): prefill of one 32k-token prompt through the
-    40-layer mixer stack, heads sharded over the GPUs, each layer's output
-    all-gathered over NCCL."""
+    40-layer mixer stack, heads sharded over the GPUs; each layer's output is
+    gathered by the output kernels' peer stores over NVLink (or, with
+    --nccl-gather, by an NCCL all-gather after the layer)."""
     import torch
     pkg = _pkg()
     ws, rank = _dist()
     S = int(args.lengths.split(",")[-1])
     stack = pkg.stack.MixerStack(be, seed=7)
-    stack.setup_prefill(S, ws, rank)
+    fused = ws > 1 and not args.nccl_gather
+    stack.setup_prefill(S, ws, rank, fused=fused)
     stack.prefill()
     torch.cuda.synchronize()
     barrier(ws)
@@ -631,11 +633,14 @@ def run_stack_prefill(be, args, st, peak_tc):
     torch.cuda.synchronize()
     ms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1) / reps)
     flops, gdn_bytes = stack.prefill_flops_bytes()
+    stack.close_prefill()
     return {"stack_prefill": {
         "metric": "40-layer mixer stack prefill tok/s", "S": S, "n_gpus": ws,
         "value": S / (ms / 1e3), "unit": "tok/s", "ms": ms,
         "gqa_TFLOP": flops / 1e12, "gdn_GB": gdn_bytes / 1e9,
-        "parallelism": f"heads sharded over {ws} GPU(s) + NCCL all-gather per layer"}}
+        "parallelism": f"heads sharded over {ws} GPU(s); layer outputs gathered by "
+                       + ("peer stores in the output kernels + a device barrier per layer" if fused
+                          else "NCCL all-gather per layer")}}
 
 
 def main():
@@ -656,6 +661,8 @@ def main():
     ap.add_argument("--gdn-kheads", type=int, default=0,
                     help="GDN prefill leg: K heads owned by this GPU (e.g. 2 = one rank of an 8-way head shard)")
     ap.add_argument("--stack-batch", type=int, default=256, help="stack decode requests (all GPUs)")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="stack prefill: gather layer outputs with NCCL instead of the fused peer stores")
     args = ap.parse_args()
     globals()["B_REQ"], globals()["T_CTX"] = args.requests, args.context
     if args.quick:

@@ -211,6 +211,34 @@ int  coli_cuda_gdn_prefill_heads_dev(int layer, int req, int S, const void *qkv,
                                      const void *a, const void *b, void *y, int KH, int KD,
                                      int VH, int VD, float eps, int dtype, int kh0, int nkh);
 
+/* ---- New: head-sharded prefill with the all-gather fused into the output
+ * kernels (no reference counterpart: the reference runs on one device). The
+ * caller's per-layer NCCL all-gather of the rank outputs (rank-major
+ * [world][S][cols], cols = nh*hd or 2*nkh*VD) is replaced by the kernels'
+ * epilogues storing this rank's block into every rank's gathered buffer
+ * through peer pointers (NVLink); dst[r] is rank r's buffer as mapped in
+ * this process (dst[rank] is the local one), world <= 8, bf16 only.
+ * A layer ends with coli_cuda_peer_barrier on every rank before any rank
+ * reads the gathered output.
+ *   coli_cuda_ipc_alloc   cudaMalloc + zero + IPC handle (64 bytes) of a buffer
+ *   coli_cuda_ipc_open    map a peer's buffer from its handle (_close unmaps)
+ *   coli_cuda_peer_barrier  flags[r] = rank r's [world] uint32 flag array
+ *                         (IPC mapped); epoch increases by one per call; a
+ *                         wait longer than ~2 s sets the device error word. */
+int  coli_cuda_ipc_alloc(size_t bytes, void **dptr, void *handle);
+int  coli_cuda_ipc_free(void *dptr, size_t bytes);
+int  coli_cuda_ipc_open(const void *handle, void **dptr);
+int  coli_cuda_ipc_close(void *dptr);
+int  coli_cuda_peer_barrier(void *const *flags, int world, int rank, unsigned epoch);
+int  coli_cuda_gqa_prefill_heads_gather_dev(int layer, int req, int S, int pos_base, const void *qg,
+                                            const void *k, const void *v, void *const *dst,
+                                            int world, int rank, int H, int KH, int hd, int rot,
+                                            float eps, float theta, int dtype, int h0, int nh);
+int  coli_cuda_gdn_prefill_heads_gather_dev(int layer, int req, int S, const void *qkv,
+                                            const void *z, const void *a, const void *b,
+                                            void *const *dst, int world, int rank, int KH, int KD,
+                                            int VH, int VD, float eps, int dtype, int kh0, int nkh);
+
 /* ==== Block level: projections + mixer + out-projection ====
  * Resident dense weights, W [O][I] row-major as the engine stores it, held on
  * the device in bf16. Replaces coli_vk_tensor_ensure / _free / _bytes

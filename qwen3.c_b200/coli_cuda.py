@@ -55,6 +55,15 @@ SIGNATURES = {
     "coli_cuda_gqa_decode_noalloc": ([_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 4 + [_f, _f, _i], _i),
     "coli_cuda_gqa_prefill_heads_dev": ([_i] * 4 + [_vp] * 4 + [_i] * 4 + [_f, _f, _i, _i, _i], _i),
     "coli_cuda_gdn_prefill_heads_dev": ([_i, _i, _i] + [_vp] * 5 + [_i] * 4 + [_f, _i, _i, _i], _i),
+    "coli_cuda_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(_vp), _vp], _i),
+    "coli_cuda_ipc_free": ([_vp, ctypes.c_size_t], _i),
+    "coli_cuda_ipc_open": ([_vp, ctypes.POINTER(_vp)], _i),
+    "coli_cuda_ipc_close": ([_vp], _i),
+    "coli_cuda_peer_barrier": ([ctypes.POINTER(_vp), _i, _i, ctypes.c_uint], _i),
+    "coli_cuda_gqa_prefill_heads_gather_dev": ([_i] * 4 + [_vp] * 3 + [ctypes.POINTER(_vp), _i, _i] + [_i] * 4
+                                               + [_f, _f, _i, _i, _i], _i),
+    "coli_cuda_gdn_prefill_heads_gather_dev": ([_i, _i, _i] + [_vp] * 4 + [ctypes.POINTER(_vp), _i, _i]
+                                               + [_i] * 4 + [_f, _i, _i, _i], _i),
     "coli_cuda_gdn_state_ensure": ([_i] * 5, _i),
     "coli_cuda_gdn_conv_ensure": ([_i] * 4, _i),
     "coli_cuda_gdn_conv_weight": ([_i, _fp, _i, _i], _i),
@@ -254,6 +263,48 @@ class Backend:
         self._ok(self.lib.coli_cuda_gqa_prefill_heads_dev(layer, req, S, pos_base, qg, k, v, ctx, H,
                                                           KH, hd, rot, eps, theta, dtype, h0, nh),
                  "gqa_prefill_heads_dev")
+
+    # ---- head-sharded prefill with the all-gather fused into the output kernels
+    IPC_HANDLE_BYTES = 64
+
+    def ipc_alloc(self, nbytes):
+        """cudaMalloc'd, zeroed device buffer and its IPC handle (bytes)."""
+        ptr = _vp()
+        handle = ctypes.create_string_buffer(self.IPC_HANDLE_BYTES)
+        self._ok(self.lib.coli_cuda_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "ipc_alloc")
+        return ptr.value, handle.raw
+
+    def ipc_free(self, ptr, nbytes):
+        self._ok(self.lib.coli_cuda_ipc_free(ptr, nbytes), "ipc_free")
+
+    def ipc_open(self, handle):
+        ptr = _vp()
+        buf = ctypes.create_string_buffer(bytes(handle), self.IPC_HANDLE_BYTES)
+        self._ok(self.lib.coli_cuda_ipc_open(buf, ctypes.byref(ptr)), "ipc_open")
+        return ptr.value
+
+    def ipc_close(self, ptr):
+        self._ok(self.lib.coli_cuda_ipc_close(ptr), "ipc_close")
+
+    @staticmethod
+    def _ptr_array(ptrs):
+        return (_vp * len(ptrs))(*ptrs)
+
+    def peer_barrier(self, flags, rank, epoch):
+        self._ok(self.lib.coli_cuda_peer_barrier(self._ptr_array(flags), len(flags), rank, epoch),
+                 "peer_barrier")
+
+    def gqa_prefill_heads_gather_dev(self, layer, req, S, pos_base, qg, k, v, dsts, rank, h0, nh, H=16,
+                                     KH=2, hd=256, rot=64, eps=1e-6, theta=1e7, dtype=1):
+        self._ok(self.lib.coli_cuda_gqa_prefill_heads_gather_dev(
+            layer, req, S, pos_base, qg, k, v, self._ptr_array(dsts), len(dsts), rank, H, KH, hd, rot,
+            eps, theta, dtype, h0, nh), "gqa_prefill_heads_gather_dev")
+
+    def gdn_prefill_heads_gather_dev(self, layer, req, S, qkv, z, a, b, dsts, rank, kh0, nkh, KH=16,
+                                     KD=128, VH=32, VD=128, eps=1e-6, dtype=1):
+        self._ok(self.lib.coli_cuda_gdn_prefill_heads_gather_dev(
+            layer, req, S, qkv, z, a, b, self._ptr_array(dsts), len(dsts), rank, KH, KD, VH, VD, eps,
+            dtype, kh0, nkh), "gdn_prefill_heads_gather_dev")
 
     def gdn_prefill_heads_dev(self, layer, req, S, qkv, z, a, b, y, kh0, nkh, KH=16, KD=128,
                               VH=32, VD=128, eps=1e-6, dtype=1):

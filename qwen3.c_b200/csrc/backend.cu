@@ -387,7 +387,8 @@ int make_f32_3d(CUtensorMap *m, void *base, int d0, int d1, int d2, int box0, in
 constexpr int GDN_CHUNK_MIN_ROWS = 64;
 int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *z, const void *a,
                         const void *b, void *y, int KHin, int KD, int VHin, int VD, float eps,
-                        int dtype, int kh0 = 0, int nkh = -1, const float *params = nullptr)
+                        int dtype, int kh0 = 0, int nkh = -1, const float *params = nullptr,
+                        const PeerGather *gather = nullptr)
 {
     GdnLayer &L = G.gdn[layer];
     if (nkh < 0) nkh = KHin;
@@ -438,6 +439,10 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
     if (!p.Qh || !p.Kh || !p.KT || !p.VT || !p.GL || !p.BETA || !p.W || !p.U || !p.M || !p.Dt || !p.QH) return 0;
     p.S = S; p.KH = KH; p.VH = VH; p.eps = eps;
     p.kh0 = kh0; p.KHin = KHin; p.VHin = VHin;
+    if (gather) {
+        p.gather = *gather;
+        p.gather.block = (long long)S * VH * VD;
+    }
     GdnPrefillMaps m;
     if (!make_f32_3d(&m.Q, p.Qh, 128, S, KH, 32, 64) || !make_f32_3d(&m.K, p.Kh, 128, S, KH, 32, 64) ||
         !make_f32_3d(&m.V, p.VT, 64, 128, nch * VH, 32, 128) ||
@@ -817,10 +822,22 @@ int coli_cuda_gqa_decode_dev(int layer, int B, const void *qg, const void *k, co
                     dtype, dtype);
 }
 
+static int gqa_prefill_heads(int layer, int req, int S, int pos_base, const void *qg, const void *k,
+                             const void *v, void *ctx, int H, int KH, int hd, int rot, float eps,
+                             float theta, int dtype, int h0, int nh, const PeerGather *gather);
+
 int coli_cuda_gqa_prefill_heads_dev(int layer, int req, int S, int pos_base, const void *qg,
                                     const void *k, const void *v, void *ctx, int H, int KH,
                                     int hd, int rot, float eps, float theta, int dtype, int h0,
                                     int nh)
+{
+    return gqa_prefill_heads(layer, req, S, pos_base, qg, k, v, ctx, H, KH, hd, rot, eps, theta, dtype,
+                             h0, nh, nullptr);
+}
+
+static int gqa_prefill_heads(int layer, int req, int S, int pos_base, const void *qg, const void *k,
+                             const void *v, void *ctx, int H, int KH, int hd, int rot, float eps,
+                             float theta, int dtype, int h0, int nh, const PeerGather *gather)
 {
     READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
@@ -853,6 +870,10 @@ int coli_cuda_gqa_prefill_heads_dev(int layer, int req, int S, int pos_base, con
     a.pos_base = pos_base; a.n_qtiles = (S + 127) / 128;
     a.scale_log2 = (1.f / sqrtf((float)hd)) * 1.4426950408889634f;
     a.h0 = h0; a.kh0 = kh0; a.Hin = H;
+    if (gather) {
+        a.gather = *gather;
+        a.gather.block = (long long)S * nh * hd;
+    }
     kt_mark(COLI_K_GQA_PREFILL);
     CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, dtype, dtype, stream()));
     kt_mark(COLI_K_GQA_PREFILL);
@@ -1107,3 +1128,4 @@ int coli_cuda_gdn_prefill(int layer, int req, int S, const float *qkv, const flo
 #include "noalloc.cu"
 #include "block.cu"
 #include "container.cu"
+#include "peer.cu"

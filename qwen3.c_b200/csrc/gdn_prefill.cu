@@ -1083,7 +1083,7 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         const int e = tid + 256 * k;
         const int row = e >> 4, c8 = (e & 15) * 8, tok = n * PFG_C + row;
         if (tok >= S) continue;
-        TO *orow = out + (size_t)tok * VH * VD + h * VD + c8;
+        const size_t ooff = (size_t)tok * VH * VD + h * VD + c8;
         float zv[8], v[8];
         if constexpr (sizeof(TI) == 2) {
             const __nv_bfloat16 *zb = reinterpret_cast<const __nv_bfloat16 *>(&zpre[k][0]);
@@ -1099,15 +1099,22 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         v[0] = y0.x; v[1] = y0.y; v[2] = y0.z; v[3] = y0.w; v[4] = y1.x; v[5] = y1.y; v[6] = y1.z; v[7] = y1.w;
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] *= siluf_(zv[j]);
-        if constexpr (sizeof(TO) == 2) {
-            uint4 o;
-            o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]); o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
-            *reinterpret_cast<uint4 *>(orow) = o;
-        } else {
-            *reinterpret_cast<float4 *>(orow) = make_float4(v[0], v[1], v[2], v[3]);
-            *reinterpret_cast<float4 *>(orow + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        const int ndst = p.gather.world ? p.gather.world : 1;
+        for (int r = 0; r < ndst; ++r) {
+            // the local output, or every rank's gathered buffer (this rank's block)
+            TO *orow = p.gather.world ? static_cast<TO *>(p.gather.dst[r]) + (size_t)p.gather.rank * p.gather.block + ooff
+                                      : out + ooff;
+            if constexpr (sizeof(TO) == 2) {
+                uint4 o;
+                o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]); o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
+                *reinterpret_cast<uint4 *>(orow) = o;
+            } else {
+                *reinterpret_cast<float4 *>(orow) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(orow + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
         }
     }
+    if (p.gather.world) __threadfence_system();   // peer stores visible before the cross-rank barrier
 }
 
 // ---------------------------------------------------------------- launch

@@ -363,13 +363,19 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const float4 a1 = *reinterpret_cast<const float4 *>(stage + r * PF_HD + (((2 * lane + 1) ^ (r & 7)) << 2));
                 const float o[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 const TI *gate = static_cast<const TI *>(p.qg) + ((size_t)srow * Hin + p.h0 + h) * 2 * PF_HD + PF_HD + 8 * lane;
-                TO *out = static_cast<TO *>(p.ctx) + ((size_t)srow * H + h) * PF_HD + 8 * lane;
+                const size_t off = ((size_t)srow * H + h) * PF_HD + 8 * lane;
                 float gv[8], y[8];
                 load8v(gate, gv);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) y[e] = o[e] * sigmoidf_(gv[e]);
-                store8v(out, y);
+                if (p.gather.world == 0) {
+                    store8v(static_cast<TO *>(p.ctx) + off, y);
+                } else {   // every rank's gathered buffer, this rank's block (peer stores over NVLink)
+                    const size_t boff = (size_t)p.gather.rank * p.gather.block + off;
+                    for (int r = 0; r < p.gather.world; ++r) store8v(static_cast<TO *>(p.gather.dst[r]) + boff, y);
+                }
             }
+            if (p.gather.world) __threadfence_system();   // peer stores visible before the cross-rank barrier
         }
     }
     tc::fence_before();

@@ -26,6 +26,17 @@ cudaError_t launch_gdn_decode(const GdnDecodeArgs &a, int in_bf16, int out_bf16,
                               cudaStream_t st);
 
 // ---------------------------------------------------------------- GQA decode
+// Output of a head-sharded prefill written straight into every rank's
+// gathered buffer (rank-major [world][rows][cols], the all-gather layout)
+// through peer (NVLink) pointers, so the transfer overlaps the kernel instead
+// of following it. dst[r] is rank r's buffer as mapped in this process.
+constexpr int PEER_MAX = 8;
+struct PeerGather {
+    void *dst[PEER_MAX];
+    int world, rank;      // world 0 = write the local output as usual
+    long long block;      // elements of one rank's block (rows x cols)
+};
+
 struct GqaPrologueArgs {
     const void *qg;       // [nq][H][2*hd] raw q | gate
     const void *k, *v;    // [nq][KH][hd] raw
@@ -72,6 +83,7 @@ struct GqaPrefillArgs {
     int S, H, KH, max_t, req, pos_base, n_qtiles;
     float scale_log2;
     int h0, kh0, Hin;  // head-sharded prefill (see GqaPrologueArgs); 0 = unsharded
+    PeerGather gather; // world > 0: ctx goes to every rank's gathered buffer instead
 };
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
@@ -80,6 +92,7 @@ cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, con
 namespace coli {
 // ---------------------------------------------------------------- GDN prefill
 struct GdnPrefillArgs {
+    PeerGather gather;                    // world > 0: y goes to every rank's gathered buffer instead
     const void *qkv, *z, *a, *b;          // [S][CD], [S][VH*VD], [S][VH], [S][VH]
     const float *conv_w, *A_log, *dt_bias, *gnorm;
     float *hist;                          // [3][CD] of the request (read, then rewritten)

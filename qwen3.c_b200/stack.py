@@ -11,12 +11,14 @@ Two modes, each on one GPU of a multi-GPU job (one process per GPU):
   decode   a batch of requests, each rank owning its own block of requests
            (sharding.request_shard); no collective on the data path.
   prefill  one long prompt, each rank computing a block of heads of every
-           layer (sharding.head_shard) followed by an NCCL all-gather of the
-           layer output.
+           layer (sharding.head_shard); the layer outputs are gathered either
+           by the output kernels themselves, storing into every rank's
+           buffer over NVLink (fused=True, peer.PeerBuffer, one device-side
+           barrier per layer), or by an NCCL all-gather after each layer.
 """
 import torch
 
-from . import sharding
+from . import peer, sharding
 
 H, KH, HD, ROT, EPS, THETA = 16, 2, 256, 64, 1e-6, 1e7
 GKH, GKD, GVH, GVD = 16, 128, 32, 128
@@ -112,9 +114,12 @@ class MixerStack:
         return n_gqa * (2048 * self.T + 2048 + 16384 + 8192) + n_gdn * 4_423_808
 
     # ------------------------------------------------------------ prefill
-    def setup_prefill(self, S, world=1, rank=0):
-        """One prompt of S tokens; this rank computes heads of its shard."""
+    def setup_prefill(self, S, world=1, rank=0, fused=False):
+        """One prompt of S tokens; this rank computes heads of its shard.
+        fused: gather the layer outputs in the kernels (peer stores) rather
+        than with NCCL."""
         self.S, self.world, self.rank = S, world, rank
+        self.fused = fused and world > 1
         self.h0, self.h1 = sharding.head_shard(H, world, rank)
         self.k0, self.k1 = sharding.kv_heads_for(self.h0, self.h1, H // KH)
         self.g0, self.g1 = sharding.head_shard(GKH, world, rank)
@@ -139,9 +144,25 @@ class MixerStack:
         nh, nv = self.h1 - self.h0, 2 * (self.g1 - self.g0)
         self.pctx = torch.empty(S, nh, HD, dtype=torch.bfloat16, device="cuda")
         self.py = torch.empty(S, nv * GVD, dtype=torch.bfloat16, device="cuda")
-        self.ctx_all = torch.empty(world, S, nh, HD, dtype=torch.bfloat16, device="cuda")
-        self.y_all = torch.empty(world, S, nv * GVD, dtype=torch.bfloat16, device="cuda")
+        if self.fused:
+            # two buffers per kind, alternating by layer: a rank may store layer
+            # L+1 while a slower peer still reads layer L's output; the barrier
+            # after every layer keeps ranks within one layer of each other
+            self.gq_bufs = [peer.PeerBuffer(be, world * S * nh * HD * 2, world, rank) for _ in range(2)]
+            self.gd_bufs = [peer.PeerBuffer(be, world * S * nv * GVD * 2, world, rank) for _ in range(2)]
+            self.pbar = peer.PeerBarrier(be, world, rank)
+        else:
+            self.ctx_all = torch.empty(world, S, nh, HD, dtype=torch.bfloat16, device="cuda")
+            self.y_all = torch.empty(world, S, nv * GVD, dtype=torch.bfloat16, device="cuda")
         be.sync()
+
+    def close_prefill(self):
+        """Release the peer buffers of a fused setup (collective)."""
+        if getattr(self, "fused", False):
+            for b in self.gq_bufs + self.gd_bufs:
+                b.close()
+            self.pbar.close()
+            self.fused = False
 
     def prefill(self, gather=True):
         """All layers' mixers over the prompt; with world > 1 each layer's
@@ -152,18 +173,30 @@ class MixerStack:
         kvi = gi = 0
         for kind in self.kinds:
             if kind == "gqa":
-                if sharded:
+                if self.fused:
+                    be.gqa_prefill_heads_gather_dev(KV_BASE + kvi, 0, S, 0, self.pqg.data_ptr(),
+                                                    self.pk.data_ptr(), self.pv.data_ptr(),
+                                                    self.gq_bufs[kvi % 2].ptrs, self.rank, self.h0,
+                                                    self.h1 - self.h0)
+                    self.pbar()
+                elif sharded:
                     be.gqa_prefill_heads_dev(KV_BASE + kvi, 0, S, 0, self.pqg.data_ptr(),
                                              self.pk.data_ptr(), self.pv.data_ptr(),
                                              self.pctx.data_ptr(), self.h0, self.h1 - self.h0)
                 else:
                     be.gqa_step_dev(KV_BASE + kvi, 0, S, 0, self.pqg.data_ptr(), self.pk.data_ptr(),
                                     self.pv.data_ptr(), self.pctx.data_ptr())
-                if sharded and gather:
+                if sharded and gather and not self.fused:
                     dist.all_gather_into_tensor(self.ctx_all, self.pctx)
                 kvi += 1
             else:
-                if sharded:
+                if self.fused:
+                    be.gdn_prefill_heads_gather_dev(GDN_BASE + gi, 0, S, self.pqkv.data_ptr(),
+                                                    self.pz.data_ptr(), self.pa.data_ptr(),
+                                                    self.pb.data_ptr(), self.gd_bufs[gi % 2].ptrs,
+                                                    self.rank, self.g0, self.g1 - self.g0)
+                    self.pbar()
+                elif sharded:
                     be.gdn_prefill_heads_dev(GDN_BASE + gi, 0, S, self.pqkv.data_ptr(),
                                              self.pz.data_ptr(), self.pa.data_ptr(),
                                              self.pb.data_ptr(), self.py.data_ptr(), self.g0,
@@ -171,7 +204,7 @@ class MixerStack:
                 else:
                     be.gdn_prefill_dev(GDN_BASE + gi, 0, S, self.pqkv.data_ptr(), self.pz.data_ptr(),
                                        self.pa.data_ptr(), self.pb.data_ptr(), self.py.data_ptr())
-                if sharded and gather:
+                if sharded and gather and not self.fused:
                     dist.all_gather_into_tensor(self.y_all, self.py)
                 gi += 1
 
