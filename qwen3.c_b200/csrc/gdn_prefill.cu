@@ -91,24 +91,8 @@ __device__ __forceinline__ void lda_sw(uint32_t tile, int row0, int ks, int lane
     const int chunk = ((ks & 3) << 1) + (mat >> 1);
     ldsm_x4(tile + (ks >> 2) * (PFG_C * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
 }
-// B fragment (n rows n0..n0+7, k columns 8ks..) of a row-major [n][k] tile.
-__device__ __forceinline__ void ldb_rm(uint32_t tile, int ld, int n0, int ks, int lane, uint32_t &b0,
-                                       uint32_t &b1)
-{
-    const int mat = (lane >> 3) & 1;
-    ldsm_x2(tile + ((n0 + (lane & 7)) * ld + ks * 8 + mat * 4) * 4, b0, b1);
-}
-
-// B fragment (n rows n0..n0+7, k columns 8ks..) of a 64-row swizzled tile
-// whose rows are the n index (e.g. K rows for K K^T).
-__device__ __forceinline__ void ldb_sw(uint32_t tile, int n0, int ks, int lane, uint32_t &b0, uint32_t &b1)
-{
-    const int mat = (lane >> 3) & 1, row = n0 + (lane & 7);
-    const int chunk = ((ks & 3) << 1) + mat;
-    ldsm_x2(tile + (ks >> 2) * (PFG_C * 128) + row * 128 + ((chunk ^ (row & 7)) << 4), b0, b1);
-}
-
-// Same for a swizzled tile of `rows` rows (regions rows x 128 bytes).
+// B fragment (n rows n0..n0+7, k columns 8ks..) of a swizzled tile of `rows`
+// rows whose rows are the n index (regions rows x 128 bytes).
 __device__ __forceinline__ void ldb_sw_rows(uint32_t tile, int rows, int n0, int ks, int lane, uint32_t &b0,
                                             uint32_t &b1)
 {

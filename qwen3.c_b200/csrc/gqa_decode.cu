@@ -6,8 +6,12 @@
 // attention over rows 0..pos with scale 1/sqrt(hd), then ctx *= sigmoid(gate).
 //
 // Kernels
-//   gqa_prologue_kernel  q/k norm + RoPE; bf16 q to scratch; k/v rows appended
-//                        to the cache (one CTA per head vector).
+//   gqa_prologue_warp_kernel  q/k norm + RoPE; bf16 q to scratch; k/v rows
+//                        appended to the cache (a warp per head vector, 1-4
+//                        query rows per CTA, 16-byte accesses);
+//                        gqa_prologue_kernel is the same arithmetic for
+//                        inputs that are not 16-byte aligned (a CTA per
+//                        head vector).
 //   gqa_split_kernel     one CTA per (query row, KV head, KV split). Each warp
 //                        streams 16-token K/V tiles through its own TMA ring
 //                        (128B-swizzled boxes, mbarrier completion) and runs

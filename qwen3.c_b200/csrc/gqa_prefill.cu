@@ -4,7 +4,7 @@
 // (c/qwen.c:638-663): query row s (position pos_base+s) attends to cache rows
 // 0..pos_base+s of its KV head (h / 8) with scale 1/sqrt(256); ctx is gated by
 // sigmoid(gate). The prologue (q/k norm, RoPE, K/V append) runs before this
-// kernel (gqa_prologue_kernel), so the new rows are already in the cache.
+// kernel (gqa_prologue_warp_kernel), so the new rows are already in the cache.
 //
 // One CTA = 128 query rows of one Q head, 128-key tiles. A tcgen05.mma costs
 // about the same for N = 64 as for N = 128, so 128-key score tiles halve the
