@@ -201,6 +201,22 @@ int make_q_tmap(CUtensorMap *m, void *base, int S, int H, int hd)
     return 1;
 }
 
+// Maps of the prefill kernel's TMA epilogue: gate = the second half of each
+// head's 2 hd values in qg [S][Hin][2 hd], ctx [S][H][hd]; 64 x 1 x 128 boxes.
+int make_pf_epi_maps(PfEpiMaps *em, const void *qg, void *ctx, int S, int H, int Hin, int hd)
+{
+    if (!make_q_tmap(&em->ctx, ctx, S, H, hd)) return 0;
+    cuuint64_t dims[3] = {(cuuint64_t)(2 * hd), (cuuint64_t)Hin, (cuuint64_t)S};
+    cuuint64_t strides[2] = {(cuuint64_t)2 * hd * 2, (cuuint64_t)Hin * 2 * hd * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = G.encode(&em->gate, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(qg), dims, strides,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled (gate) failed (%d)", (int)r);
+    return 1;
+}
+
 // fp32 host -> device staging (optionally converted to bf16 by the kernels'
 // templated loads; the host API keeps fp32 end to end for parity).
 void *upload(Slot s, const void *host, size_t bytes)
@@ -324,8 +340,11 @@ int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void
     GqaPrefillArgs a{};
     a.qg = qg; a.ctx = ctx; a.S = S; a.H = H; a.KH = L.KH; a.max_t = L.max_t; a.req = req;
     a.pos_base = pos_base; a.n_qtiles = (S + 127) / 128; a.scale_log2 = scale * 1.4426950408889634f;
+    PfEpiMaps em;
+    const bool tma_epi = in_bf16 && out_bf16;
+    if (tma_epi && !make_pf_epi_maps(&em, qg, ctx, S, H, H, L.hd)) return 0;
     kt_mark(COLI_K_GQA_PREFILL);
-    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, in_bf16, out_bf16, stream()));
+    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, in_bf16, out_bf16, stream(), tma_epi ? &em : nullptr));
     kt_mark(COLI_K_GQA_PREFILL);
     g_launches += 1;
     return 1;
@@ -874,8 +893,11 @@ static int gqa_prefill_heads(int layer, int req, int S, int pos_base, const void
         a.gather = *gather;
         a.gather.block = (long long)S * nh * hd;
     }
+    PfEpiMaps em;
+    const bool tma_epi = dtype && !gather;
+    if (tma_epi && !make_pf_epi_maps(&em, qg, ctx, S, nh, H, hd)) return 0;
     kt_mark(COLI_K_GQA_PREFILL);
-    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, dtype, dtype, stream()));
+    CK(launch_gqa_prefill(tq, L.tmK64, L.tmV64, a, dtype, dtype, stream(), tma_epi ? &em : nullptr));
     kt_mark(COLI_K_GQA_PREFILL);
     g_launches += 3;
     return 1;

@@ -95,6 +95,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0,
         " [%0], [%1, {%2, %3}], [%4];"
         ::"r"(smem_u32(dst)), "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
 }
+// 3D tiled store of a shared-memory box (bulk group; coordinates >= 0, rows
+// past the tensor's extent are not written).
+__device__ __forceinline__ void tma_store_3d(const void *tmap, const void *src, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+        ::"l"(tmap), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void tma_store_commit_wait() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int c0, int c1, int c2,
                                             uint64_t *bar) {
     asm volatile(

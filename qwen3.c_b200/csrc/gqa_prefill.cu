@@ -48,7 +48,7 @@ constexpr float PF_RESCALE_LOG2 = 8.0f;
 static_assert(PF_Q_BYTES <= PF_KV_BYTES, "Q is staged in the V buffer");
 
 struct PfBars {
-    uint64_t q_full, q_tmem, k_full[2], k_empty[2], v_full, v_empty, s_full, s_free, p_full, pv_done;
+    uint64_t q_full, q_tmem, k_full[2], k_empty[2], v_full, v_empty, s_full, s_free, p_full, pv_done, g_full;
     uint32_t tmem_base;
     float lsum[PF_BM];        // final row sums for the epilogue
 };
@@ -85,7 +85,8 @@ __device__ __forceinline__ void store8v(float *dst, const float (&y)[8])
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, GqaPrefillArgs p)
+                   const __grid_constant__ CUtensorMap tmV, GqaPrefillArgs p,
+                   const __grid_constant__ PfEpiMaps em)
 {
     // All shared memory is dynamic (no static __shared__), so the window
     // starts 1024-byte aligned as the 128B-swizzled TMA boxes and UMMA
@@ -118,6 +119,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_init(&bars.v_full, 1); mbar_init(&bars.v_empty, 1);
         mbar_init(&bars.s_full, 1); mbar_init(&bars.s_free, PF_SOFTMAX);
         mbar_init(&bars.p_full, PF_SOFTMAX); mbar_init(&bars.pv_done, 1);
+        mbar_init(&bars.g_full, 1);
         fence_mbar_init();
     }
     if (warp == 1) tc::alloc(&bars.tmem_base, 512);
@@ -133,13 +135,27 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tma_prefetch_desc(&tmQ); tma_prefetch_desc(&tmK);
             mbar_expect_tx(&bars.q_full, PF_Q_BYTES);
             for (int c = 0; c < 4; ++c) tma_load_3d(sV + c * (PF_BM * 128), &tmQ, 64 * c, h, q0, &bars.q_full);
+            bool kok = true;
             for (int j = 0; j < nt; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&bars.k_empty[s], ((j >> 1) - 1) & 1)) break;
+                if (j >= 2 && !mbar_wait(&bars.k_empty[s], ((j >> 1) - 1) & 1)) { kok = false; break; }
                 mbar_expect_tx(&bars.k_full[s], PF_KV_BYTES);
                 for (int c = 0; c < 4; ++c)
                     tma_load_2d(sK + s * PF_KV_BYTES + c * (PF_BN * 128), &tmK, 64 * c,
                                 kvrow0 + j * PF_BN, &bars.k_full[s]);
+            }
+            if (p.tma_epi && kok) {
+                // the gate tile into the second K buffer as soon as the last S
+                // that reads that buffer (odd tile j1) is done; it lands while
+                // the last tiles' softmax and PV run
+                const int j1 = (nt - 1) & 1 ? nt - 1 : nt - 2;
+                if (j1 < 1 || mbar_wait(&bars.k_empty[1], (j1 >> 1) & 1)) {
+                    tma_prefetch_desc(&em.gate);
+                    mbar_expect_tx(&bars.g_full, PF_BM * PF_HD * 2);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_3d(sK + PF_KV_BYTES + c * (PF_BM * 128), &em.gate, PF_HD + 64 * c, p.h0 + h, q0,
+                                    &bars.g_full);
+                }
             }
         } else if (lane == 1) {
             tma_prefetch_desc(&tmV);
@@ -329,7 +345,43 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         asm volatile("bar.sync 1, %0;" ::"n"(PF_SOFTMAX) : "memory");
         mbar_wait(&bars.pv_done, (nt - 1) & 1);
         tc::fence_after();
-        {
+        if (p.tma_epi) {
+            // TMA epilogue (bf16): thread = tile row 32 quarter + lane, O columns
+            // 128 u ..; the gate tile (loaded by TMA into the second K buffer)
+            // and the bf16 ctx tile (staged in the first) share the layout of
+            // the 128B-swizzled 64 x 128 boxes, and one thread stores the tile
+            // with four TMA box stores (rows past S are not written).
+            const int row = 32 * quarter + lane;
+            const uint32_t qoff = (uint32_t)(32 * quarter) << 16;
+            const float inv_l = 1.f / bars.lsum[row];
+            uint8_t *stage = sK;
+            const uint8_t *gt = sK + PF_KV_BYTES;
+            mbar_wait(&bars.g_full, 0);
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                const int d0 = 128 * u + 32 * c;
+                tc::ld32(tO + d0 + qoff, o);
+                tc::wait_ld();
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int chunk = ((d0 & 63) >> 3) + k;
+                    const uint32_t off = (d0 >> 6) * (PF_BM * 128) + row * 128 + ((chunk ^ (row & 7)) << 4);
+                    float gv[8];
+                    load8v(reinterpret_cast<const __nv_bfloat16 *>(gt + off), gv);
+                    float y[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = o[8 * k + e] * inv_l * sigmoidf_(gv[e]);
+                    store8v(reinterpret_cast<__nv_bfloat16 *>(stage + off), y);
+                }
+            }
+            fence_proxy_async();                   // the staged tile visible to the TMA
+            asm volatile("bar.sync 1, %0;" ::"n"(PF_SOFTMAX) : "memory");
+            if (warp == 2 && lane == 0) {
+                for (int c = 0; c < 4; ++c) tma_store_3d(&em.ctx, stage + c * (PF_BM * 128), 64 * c, h, q0);
+                tma_store_commit_wait();
+            }
+        } else {
             // epilogue, part 1: O / l through the 32x32b shape (thread = tile row
             // 32 quarter + lane, O columns 128 u ..) into fp32 staging rows in the
             // K buffers, which the last PV has finished with. 16-byte chunk c of
@@ -372,7 +424,7 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     store8v(static_cast<TO *>(p.ctx) + off, y);
                 } else {   // every rank's gathered buffer, this rank's block (peer stores over NVLink)
                     const size_t boff = (size_t)p.gather.rank * p.gather.block + off;
-                    for (int r = 0; r < p.gather.world; ++r) store8v(static_cast<TO *>(p.gather.dst[r]) + boff, y);
+                    for (int rk = 0; rk < p.gather.world; ++rk) store8v(static_cast<TO *>(p.gather.dst[rk]) + boff, y);
                 }
             }
             if (p.gather.world) __threadfence_system();   // peer stores visible before the cross-rank barrier
@@ -387,15 +439,21 @@ gqa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 }
 
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
-                               const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st)
+                               const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st,
+                               const PfEpiMaps *em)
 {
     // the epilogue reads the gate and writes ctx with 16-byte vectors
     if (((uintptr_t)a.qg | (uintptr_t)a.ctx) & 15) return cudaErrorMisalignedAddress;
     dim3 grid(a.n_qtiles * a.H), block(PF_THREADS);
+    GqaPrefillArgs args = a;
+    PfEpiMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    args.tma_epi = (em && in_bf16 && out_bf16 && a.gather.world == 0) ? 1 : 0;
+    if (args.tma_epi) maps = *em;
     auto run = [&](auto kern) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
         if (e != cudaSuccess) return e;
-        kern<<<grid, block, PF_SMEM, st>>>(tq, tk, tv, a);
+        kern<<<grid, block, PF_SMEM, st>>>(tq, tk, tv, args, maps);
         return cudaGetLastError();
     };
     if (in_bf16 && out_bf16) return run(gqa_prefill_kernel<__nv_bfloat16, __nv_bfloat16>);

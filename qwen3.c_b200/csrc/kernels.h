@@ -84,9 +84,16 @@ struct GqaPrefillArgs {
     float scale_log2;
     int h0, kh0, Hin;  // head-sharded prefill (see GqaPrologueArgs); 0 = unsharded
     PeerGather gather; // world > 0: ctx goes to every rank's gathered buffer instead
+    int tma_epi;       // 1: gate tile loaded and ctx tile stored by TMA (bf16, no gather)
+};
+// Tensor maps of the TMA epilogue: the gate half of qg ([S][Hin][2 hd], boxes
+// of 64 x 1 x 128 at x = hd + 64 c) and ctx ([S][H][hd], same boxes).
+struct PfEpiMaps {
+    CUtensorMap gate, ctx;
 };
 cudaError_t launch_gqa_prefill(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
-                               const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st);
+                               const GqaPrefillArgs &a, int in_bf16, int out_bf16, cudaStream_t st,
+                               const PfEpiMaps *em = nullptr);
 }  // namespace coli
 
 namespace coli {
