@@ -23,11 +23,15 @@
 //               crosses the diagonal, online softmax in the log2 domain with
 //               lazy rescaling (O is corrected in TMEM only when the running
 //               max grows by more than 2^8), P written to shared memory in the
-//               UMMA K-major layout. Epilogue: O / l staged as fp32 rows in
-//               the (then idle) K buffers, then a warp per row applies
-//               sigmoid(gate) with 16-byte coalesced gate loads and ctx stores
-//               (a thread-per-row store pattern touches 32 rows per
-//               instruction and cost as much as 40 KV tiles per CTA).
+//               UMMA K-major layout. Epilogue, bf16: the gate tile arrives
+//               by TMA in the second K buffer (issued by warp 0 once the last
+//               S reading it is done), ctx = O / l * sigmoid(gate) is staged
+//               as bf16 boxes in the first and written by TMA box stores.
+//               Otherwise (fp32, peer gather): O / l staged as fp32 rows in
+//               the K buffers, then a warp per row applies sigmoid(gate) with
+//               16-byte coalesced gate loads and ctx stores (a thread-per-row
+//               store pattern touches 32 rows per instruction and cost as
+//               much as 40 KV tiles per CTA).
 // TMEM (512 columns): scores 128 | O 256 | Q 128 (bf16 pairs).
 // Shared memory: K 2 x 64 KiB, V (and Q staging) 64 KiB, P 32 KiB.
 // Every wait is bounded (see mbar_wait); no cluster multicast.
