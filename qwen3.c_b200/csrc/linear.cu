@@ -318,12 +318,16 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
     splits = (nk + a.kchunks - 1) / a.kchunks;   // no split without K chunks
     if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
     dim3 grid((a.O + LN_BM - 1) / LN_BM, (a.S + bn - 1) / bn, splits);
-    static bool attr_set[7] = {};   // the shared-memory opt-in, once per instantiation
+    // the shared-memory opt-in, once per instantiation and device
+    static bool attr_set[16][7] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    bool *set = attr_set[dev & 15];
     auto run = [&](auto kern, int smem, int which) -> cudaError_t {
-        if (!attr_set[which]) {
+        if (!set[which] || dev >= 16) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return e;
-            attr_set[which] = true;
+            set[which] = true;
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = grid; cfg.blockDim = dim3(192); cfg.dynamicSmemBytes = smem; cfg.stream = st;
@@ -338,7 +342,7 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
         // persistent: one CTA per SM over all output tiles
         const int tiles = grid.x * grid.y;
         int sms = 0;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         grid = dim3(std::min(tiles, std::max(sms, 1)), 1, 1);
         if (bn == 128) return run(linear_persistent_kernel<128>, LinSmem<128>::TOTAL, 5);
         return run(linear_persistent_kernel<256>, LinSmem<256>::TOTAL, 6);
