@@ -61,6 +61,48 @@ int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, 
     return 1;
 }
 
+// Several projections of the same x (S <= 16 rows: decode) in one launch;
+// larger S runs them one by one (each already fills the GPU).
+int linear_dev_multi(const ColiCudaTensor *const *t, int nw, const __nv_bfloat16 *x, int S, void *const *y,
+                     int y_bf16)
+{
+    if (S > 16 || nw > LIN_MAXW) {
+        for (int i = 0; i < nw; ++i)
+            if (!linear_dev(t[i], x, S, y[i], y_bf16)) return 0;
+        return 1;
+    }
+    const CUtensorMap *maps[LIN_MAXW];
+    int O[LIN_MAXW];
+    int tiles = 0, Osum = 0;
+    for (int i = 0; i < nw; ++i) {
+        if (!t[i] || !t[i]->w) return fail("dense tensor not uploaded");
+        if (t[i]->I != t[0]->I) return fail("projections of one launch need the same input width");
+        maps[i] = &t[i]->tm; O[i] = t[i]->O;
+        tiles += (O[i] + 127) / 128; Osum += O[i];
+    }
+    CUtensorMap tx;
+    if (!make_bf16_2d(&tx, x, t[0]->I, S, 64, 16)) return 0;
+    const int nk = (t[0]->I + 63) / 64;
+    int splits = 1;
+    if (2 * tiles <= G.num_sms) splits = std::max(1, std::min(G.num_sms / tiles, nk / 4));
+    LinearArgs la;
+    memset(&la, 0, sizeof(la));
+    la.S = S; la.I = t[0]->I; la.O = Osum; la.y_bf16 = y_bf16;
+    if (splits > 1) {
+        la.part = (float *)scratch(S_LPART, (size_t)splits * S * Osum * 4);
+        if (!la.part) return 0;
+        const size_t need = (size_t)tiles * sizeof(int);
+        if (G.slot_bytes[S_LCNT] < need) {
+            if (!scratch(S_LCNT, need)) return 0;
+            CK(cudaMemsetAsync(G.slot[S_LCNT], 0, G.slot_bytes[S_LCNT], stream()));
+        }
+        la.tile_cnt = (int *)G.slot[S_LCNT];
+    }
+    CK(launch_linear_multi(maps, O, y, nw, tx, la, splits, stream()));
+    g_launches += 1;
+    return 1;
+}
+
 // Host fp32 [n] -> device bf16 (through an fp32 staging slot).
 const __nv_bfloat16 *upload_bf16(const float *x, size_t n)
 {
@@ -174,8 +216,11 @@ int gqa_block_dev(int layer, const __nv_bfloat16 *xb, int D, ColiCudaTensor *gq_
     auto *v = (__nv_bfloat16 *)scratch(S_PV, (size_t)S * KH * hd * 2);
     auto *ctx = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * H * hd * 2);
     if (!qg || !k || !v || !ctx) return 0;
-    if (!linear_dev(gq_t, xb, S, qg, 1) || !linear_dev(gk_t, xb, S, k, 1) || !linear_dev(gv_t, xb, S, v, 1))
-        return 0;
+    {
+        const ColiCudaTensor *ts[3] = {gq_t, gk_t, gv_t};
+        void *ys[3] = {qg, k, v};
+        if (!linear_dev_multi(ts, 3, xb, S, ys, 1)) return 0;
+    }
     if (!coli_cuda_gqa_step_dev(layer, 0, S, pos_base, qg, k, v, ctx, H, KH, hd, rot, eps, theta, 1)) return 0;
     return linear_dev(out_t, ctx, S, od, 0);
 }
@@ -197,7 +242,11 @@ int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTens
     auto *z = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * VH * VD * 2);
     auto *y = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * VH * VD * 2);
     if (!qkv || !z || !y) return 0;
-    if (!linear_dev(gqkv_t, xb, S, qkv, 1) || !linear_dev(gz_t, xb, S, z, 1)) return 0;
+    {
+        const ColiCudaTensor *ts[2] = {gqkv_t, gz_t};
+        void *ys[2] = {qkv, z};
+        if (!linear_dev_multi(ts, 2, xb, S, ys, 1)) return 0;
+    }
     if (S >= GDN_CHUNK_MIN_ROWS) {
         if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, y, KH, KD, VH, VD, eps, 1, 0, -1, pd))
             return 0;

@@ -145,6 +145,12 @@ struct LinearArgs {
 };
 cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
                           cudaStream_t st);
+// Up to LIN_MAXW projections of the same x ([S][I], S <= 16) in one launch:
+// weight w has O[w] outputs into y[w]; the output tiles of all weights share
+// the grid (and the split-K plan, with the reduction in the kernel).
+constexpr int LIN_MAXW = 4;
+cudaError_t launch_linear_multi(const CUtensorMap *const *tmW, const int *O, void *const *y, int nw,
+                                const CUtensorMap &tmX, LinearArgs a, int splits, cudaStream_t st);
 cudaError_t launch_f32_to_bf16(const float *x, __nv_bfloat16 *y, size_t n, cudaStream_t st);
 int linear_pick_bn(int S);
 cudaError_t launch_rmsnorm_zc_rows(const float *x, const float *delta, const float *w, float *sum_out,

@@ -32,9 +32,20 @@ template <int BN> struct LinSmem {
     static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
+// The weights of one launch: w[i] covers output tiles [tile_end[i-1], tile_end[i])
+// of blockIdx.x, has O[i] outputs into y[i], and its split-K partials start
+// part_off[i] floats into LinearArgs::part.
+struct LinWeights {
+    CUtensorMap w[LIN_MAXW];
+    int tile_end[LIN_MAXW], O[LIN_MAXW];
+    void *y[LIN_MAXW];
+    size_t part_off[LIN_MAXW];
+    int nw;
+};
+
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
-linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, LinearArgs a)
+linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUtensorMap tmX, LinearArgs a)
 {
     constexpr int LN_STAGES = LinSmem<BN>::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -43,7 +54,13 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
     __shared__ uint32_t tmem_base;
     __shared__ int last_split;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o0 = blockIdx.x * LN_BM, s0 = blockIdx.y * BN, z = blockIdx.z;
+    int wi = 0;                                // this CTA's weight
+    while (wi + 1 < lw.nw && (int)blockIdx.x >= lw.tile_end[wi]) ++wi;
+    const CUtensorMap *tmW = &lw.w[wi];
+    const int O = lw.O[wi];
+    void *const yout = lw.y[wi];
+    float *const part = a.part ? a.part + lw.part_off[wi] : nullptr;
+    const int o0 = ((int)blockIdx.x - (wi ? lw.tile_end[wi - 1] : 0)) * LN_BM, s0 = blockIdx.y * BN, z = blockIdx.z;
     const int nk = (a.I + LN_BK - 1) / LN_BK;
     const int k0 = z * a.kchunks, k1 = min(nk, k0 + a.kchunks), cnt = max(0, k1 - k0);
 
@@ -60,13 +77,13 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
 
     if (warp == 0) {
         if (lane == 0) {
-            tma_prefetch_desc(&tmW); tma_prefetch_desc(&tmX);
+            tma_prefetch_desc(tmW); tma_prefetch_desc(&tmX);
             // the weights do not depend on the previous kernel: the first ring's
             // worth streams in while that kernel finishes (programmatic launch)
             const int pre = min(cnt, LN_STAGES);
             for (int i = 0; i < pre; ++i) {
                 mbar_expect_tx(&full[i], LinSmem<BN>::STAGE);
-                tma_load_2d(sm + i * LinSmem<BN>::STAGE, &tmW, (k0 + i) * LN_BK, o0, &full[i]);
+                tma_load_2d(sm + i * LinSmem<BN>::STAGE, tmW, (k0 + i) * LN_BK, o0, &full[i]);
             }
             griddep_wait();
             for (int i = 0; i < pre; ++i)
@@ -76,7 +93,7 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
                 mbar_wait(&empty[st], ((i / LN_STAGES) + 1) & 1);
                 uint8_t *sA = sm + st * LinSmem<BN>::STAGE, *sB = sA + LN_A_BYTES;
                 mbar_expect_tx(&full[st], LinSmem<BN>::STAGE);
-                tma_load_2d(sA, &tmW, (k0 + i) * LN_BK, o0, &full[st]);
+                tma_load_2d(sA, tmW, (k0 + i) * LN_BK, o0, &full[st]);
                 tma_load_2d(sB, &tmX, (k0 + i) * LN_BK, s0, &full[st]);
             }
         }
@@ -115,20 +132,20 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = 0.f;
             }
-            if (o < a.O) {
+            if (o < O) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int s = s0 + c0 + j;
                     if (s >= a.S) break;
-                    const size_t idx = (size_t)s * a.O + o;
-                    if (a.part) a.part[(size_t)z * a.S * a.O + idx] = v[j];
-                    else if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[idx] = __float2bfloat16_rn(v[j]);
-                    else static_cast<float *>(a.y)[idx] = v[j];
+                    const size_t idx = (size_t)s * O + o;
+                    if (part) part[(size_t)z * a.S * O + idx] = v[j];
+                    else if (a.y_bf16) static_cast<__nv_bfloat16 *>(yout)[idx] = __float2bfloat16_rn(v[j]);
+                    else static_cast<float *>(yout)[idx] = v[j];
                 }
             }
         }
         tc::fence_before();
-        if (BN == 16 && a.part && a.tile_cnt) {
+        if (BN == 16 && part && a.tile_cnt) {
             // split-K: the last split of this output tile to arrive adds the
             // partials in split order (the same sum as linear_reduce_kernel)
             __threadfence();
@@ -138,25 +155,25 @@ linear_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ C
             asm volatile("bar.sync 2, 128;" ::: "memory");
             if (last_split) {
                 __threadfence();
-                const size_t n = (size_t)a.S * a.O;
-                if (o < a.O) {
+                const size_t n = (size_t)a.S * O;
+                if (o < O) {
                     // up to 16 token rows: each split's loads go out together
                     const int rows = min(a.S - s0, min(BN, 16));
                     float acc[16];
 #pragma unroll
                     for (int r = 0; r < 16; ++r) acc[r] = 0.f;
                     for (int zz = 0; zz < (int)gridDim.z; ++zz) {
-                        const float *pz = a.part + zz * n + (size_t)s0 * a.O + o;
+                        const float *pz = part + zz * n + (size_t)s0 * O + o;
 #pragma unroll
                         for (int r = 0; r < 16; ++r)
-                            if (r < rows) acc[r] += __ldcg(pz + (size_t)r * a.O);
+                            if (r < rows) acc[r] += __ldcg(pz + (size_t)r * O);
                     }
 #pragma unroll
                     for (int r = 0; r < 16; ++r) {
                         if (r >= rows) break;
-                        const size_t idx = (size_t)(s0 + r) * a.O + o;
-                        if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[idx] = __float2bfloat16_rn(acc[r]);
-                        else static_cast<float *>(a.y)[idx] = acc[r];
+                        const size_t idx = (size_t)(s0 + r) * O + o;
+                        if (a.y_bf16) static_cast<__nv_bfloat16 *>(yout)[idx] = __float2bfloat16_rn(acc[r]);
+                        else static_cast<float *>(yout)[idx] = acc[r];
                     }
                 }
                 if (threadIdx.x == 64) a.tile_cnt[tile] = 0;
@@ -323,7 +340,10 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
     int dev = 0;
     cudaGetDevice(&dev);
     bool *set = attr_set[dev & 15];
-    auto run = [&](auto kern, int smem, int which) -> cudaError_t {
+    LinWeights lw;
+    memset(&lw, 0, sizeof(lw));
+    lw.w[0] = tmW; lw.tile_end[0] = grid.x; lw.O[0] = a.O; lw.y[0] = a.y; lw.nw = 1;
+    auto run = [&](auto kern, int smem, int which, const auto &wts) -> cudaError_t {
         if (!set[which] || dev >= 16) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return e;
@@ -335,7 +355,7 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr; cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, kern, tmW, tmX, a);
+        return cudaLaunchKernelEx(&cfg, kern, wts, tmX, a);
     };
     cudaError_t e;
     if (splits == 1 && bn >= 128) {
@@ -344,21 +364,60 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
         int sms = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         grid = dim3(std::min(tiles, std::max(sms, 1)), 1, 1);
-        if (bn == 128) return run(linear_persistent_kernel<128>, LinSmem<128>::TOTAL, 5);
-        return run(linear_persistent_kernel<256>, LinSmem<256>::TOTAL, 6);
+        if (bn == 128) return run(linear_persistent_kernel<128>, LinSmem<128>::TOTAL, 5, tmW);
+        return run(linear_persistent_kernel<256>, LinSmem<256>::TOTAL, 6, tmW);
     }
     switch (bn) {
-    case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL, 0); break;
-    case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL, 1); break;
-    case 64: e = run(linear_kernel<64>, LinSmem<64>::TOTAL, 2); break;
-    case 128: e = run(linear_kernel<128>, LinSmem<128>::TOTAL, 3); break;
-    case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL, 4); break;
+    case 16: e = run(linear_kernel<16>, LinSmem<16>::TOTAL, 0, lw); break;
+    case 32: e = run(linear_kernel<32>, LinSmem<32>::TOTAL, 1, lw); break;
+    case 64: e = run(linear_kernel<64>, LinSmem<64>::TOTAL, 2, lw); break;
+    case 128: e = run(linear_kernel<128>, LinSmem<128>::TOTAL, 3, lw); break;
+    case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL, 4, lw); break;
     default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess || splits == 1 || (bn == 16 && a.tile_cnt)) return e;
     const size_t n = (size_t)a.S * a.O;
     linear_reduce_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(a, splits);
     return cudaGetLastError();
+}
+
+cudaError_t launch_linear_multi(const CUtensorMap *const *tmW, const int *O, void *const *y, int nw,
+                                const CUtensorMap &tmX, LinearArgs a, int splits, cudaStream_t st)
+{
+    if (nw < 1 || nw > LIN_MAXW || a.S > 16) return cudaErrorInvalidValue;
+    const int nk = (a.I + LN_BK - 1) / LN_BK;
+    a.kchunks = (nk + splits - 1) / splits;
+    splits = (nk + a.kchunks - 1) / a.kchunks;
+    if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
+    if (splits > 1 && (!a.part || !a.tile_cnt)) return cudaErrorInvalidValue;
+    LinWeights lw;
+    memset(&lw, 0, sizeof(lw));
+    int tiles = 0;
+    size_t off = 0;
+    for (int i = 0; i < nw; ++i) {
+        lw.w[i] = *tmW[i];
+        tiles += (O[i] + LN_BM - 1) / LN_BM;
+        lw.tile_end[i] = tiles; lw.O[i] = O[i]; lw.y[i] = y[i]; lw.part_off[i] = off;
+        off += (size_t)splits * a.S * O[i];
+    }
+    lw.nw = nw;
+    static bool attr_set[16] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 16 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(linear_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             LinSmem<16>::TOTAL);
+        if (e != cudaSuccess) return e;
+        if (dev < 16) attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles, 1, splits); cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = LinSmem<16>::TOTAL; cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_kernel<16>, lw, tmX, a);
 }
 
 }  // namespace coli
