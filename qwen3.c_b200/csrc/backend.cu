@@ -106,7 +106,16 @@ void kt_mark(int k)  // call before and after the launch of kernel k
     KT.ev[k].push_back(e);
 }
 
-cudaStream_t stream() { return G.user_stream_set ? G.user_stream : G.stream; }
+// The device error word as read by the last download(), valid until the next
+// stream() use (any later launch or copy may raise it again).
+int g_err_host = 0;
+bool g_err_fresh = false;
+
+cudaStream_t stream()
+{
+    g_err_fresh = false;
+    return G.user_stream_set ? G.user_stream : G.stream;
+}
 
 int fail(const char *fmt, ...)
 {
@@ -230,18 +239,28 @@ void *upload(Slot s, const void *host, size_t bytes)
     return d;
 }
 
+// The result and the device error word come back in one synchronisation.
 int download(void *host, const void *dev, size_t bytes)
 {
-    CK(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, stream()));
-    CK(cudaStreamSynchronize(stream()));
+    cudaStream_t st = stream();
+    CK(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyFromSymbolAsync(&g_err_host, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    g_err_fresh = true;
     return 1;
 }
 
 int check_dev_error()
 {
     int h = 0;
-    CK(cudaMemcpyFromSymbolAsync(&h, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream()));
-    CK(cudaStreamSynchronize(stream()));
+    if (g_err_fresh) {   // read by the download that just finished, nothing launched since
+        h = g_err_host;
+        g_err_fresh = false;
+    } else {
+        cudaStream_t st = stream();
+        CK(cudaMemcpyFromSymbolAsync(&h, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+    }
     if (h) {
         G.ready = 0;
         return fail("device error word %d (%s)", h, h == 1 ? "pipeline wait timed out" : "kernel fault");
