@@ -39,7 +39,7 @@ def _worker(rank, world, port, out):
 def test_max_over_ranks_gloo():
     import random
     port = random.randint(20000, 40000)
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
         res = dict(out)
