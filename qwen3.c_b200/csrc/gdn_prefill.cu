@@ -213,9 +213,9 @@ gdn_pf_prologue_kernel(GdnPrefillArgs p)
             sk = (red[par][1][0] + red[par][1][1]) + (red[par][1][2] + red[par][1][3]);
             const float rq = 1.f / sqrtf(sq + p.eps) / sqrtf((float)PFG_D);
             const float rk = 1.f / sqrtf(sk + p.eps);
-            const float kv = tf32r(out[1] * rk);
-            kb[u] = kv;
-            p.Qh[((size_t)kh * S + s) * PFG_D + t] = tf32r(out[0] * rq);
+            const float kv = out[1] * rk;
+            kb[u] = tf32r(kv);
+            p.Qh[((size_t)kh * S + s) * PFG_D + t] = out[0] * rq;   // full fp32: split by the consumers
             p.Kh[((size_t)kh * S + s) * PFG_D + t] = kv;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -327,10 +327,10 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int c = j * 32 + lane;
-            const float kv = tf32r(out[4 + j] * rk);
-            p.Qh[((size_t)kh * S + s) * PFG_D + c] = tf32r(out[j] * rq);
+            const float kv = out[4 + j] * rk;
+            p.Qh[((size_t)kh * S + s) * PFG_D + c] = out[j] * rq;   // full fp32: split by the consumers
             p.Kh[((size_t)kh * S + s) * PFG_D + c] = kv;
-            sKT[c * PRT_KT_LD + r] = kv;
+            sKT[c * PRT_KT_LD + r] = tf32r(kv);
         }
         __syncwarp();                        // every lane has read row r
         float *vrow = reinterpret_cast<float *>(sX + r * PRT_CH);
@@ -413,7 +413,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1; later T diag(beta), K-major
     float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
     __shared__ float G[PFG_C], bet[PFG_C], bgam[PFG_C];   // bgam = beta e^G
-    __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_mma;
+    __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_mma, bar_k2;
     __shared__ uint32_t tmem_base;
 
     const int n = blockIdx.x, h = blockIdx.y, kh = h >> 1;
@@ -423,6 +423,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_init(&bar_qk, 1);
         mbar_init(&bar_v, 1);
         mbar_init(&bar_mma, 1);
+        mbar_init(&bar_k2, 1);
         fence_mbar_init();
     }
     if (warp == 0) tc::alloc(&tmem_base, 256);
@@ -446,23 +447,67 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     __syncthreads();
     if (tid < PFG_C) bgam[tid] = bet[tid] * expf(G[tid]);   // read after later barriers
+    // Q and K arrive in full fp32. Q K^T becomes M, which carries the outputs
+    // (for a fast-decaying head almost all of y_t is M_tt d_t), so it runs as
+    // three tf32 products, hi.hi + lo.hi + hi.lo (the split-tf32 scheme; a
+    // product of plain tf32 roundings misses the output tolerance there).
+    // K K^T only enters through the T solve and uses the rounded operands.
+    // Q_lo lives in the A / T area (free until these products complete), then
+    // K is loaded there again for K_lo.
+    float *sLo = sA;                            // [64 x 128] swizzled like sQV / sK (32 KiB over sA, sT)
+    mbar_wait(&bar_qk, 0);
+    for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
+        const float q = sQV[i], qh = tf32r(q);
+        sQV[i] = qh;
+        sLo[i] = tf32r(q - qh);
+        sK[i] = tf32r(sK[i]);
+    }
+    fence_proxy_async();                        // generic-proxy writes visible to the tensor core
+    tc::fence_before();
+    __syncthreads();
+    constexpr uint32_t IDP = tc::idesc_tf32(64, 64);
+    const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQV), aLo = smem_u32(sLo);
     if (tid == 0) {
-        // K K^T -> columns 0..63, Q K^T -> 64..127 (Q and K are tf32 from the prologue)
-        const bool ok = mbar_wait(&bar_qk, 0);
+        // K K^T -> columns 0..63, Q K^T -> 64..127
         tc::fence_after();
-        if (ok) {
-            constexpr uint32_t ID = tc::idesc_tf32(64, 64);
-            const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQV);
+#pragma unroll
+        for (int ks = 0; ks < PFG_D / 8; ++ks) {
+            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aK + off), IDP, ks > 0);
+            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aK + off), IDP, ks > 0);
+        }
+#pragma unroll
+        for (int ks = 0; ks < PFG_D / 8; ++ks) {
+            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aLo + off), tc::desc_k_sw128(aK + off), IDP, 1);
+        }
+        tc::commit(&bar_mma);
+        // full K again, over Q_lo, once the products above have read it
+        if (mbar_wait(&bar_mma, 0)) {
+            mbar_expect_tx(&bar_k2, PFG_C * PFG_D * 4);
+            for (int c = 0; c < 4; ++c) tma_load_3d(sLo + c * PFG_C * 32, &tmK, 32 * c, s0, kh, &bar_k2);
+        }
+    }
+    const bool k2 = mbar_wait(&bar_k2, 0);
+    for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
+        const float k = sLo[i];
+        sLo[i] = tf32r(k - tf32r(k));
+    }
+    fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        tc::fence_after();
+        if (k2) {
 #pragma unroll
             for (int ks = 0; ks < PFG_D / 8; ++ks) {
                 const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
-                tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aK + off), ID, ks > 0);
-                tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aK + off), ID, ks > 0);
+                tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aLo + off), IDP, 1);
             }
         }
         tc::commit(&bar_mma);
     }
-    mbar_wait(&bar_mma, 0);   // a time-out raises the device error word
+    mbar_wait(&bar_mma, 1);   // a time-out raises the device error word
     tc::fence_after();
 
     // this warp's 16 rows of K K^T (w < 4) or Q K^T (w >= 4), all 64 columns:
@@ -483,7 +528,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const float v0 = acc[4 * nt + 2 * hr], v1 = acc[4 * nt + 2 * hr + 1];
                 if (second) {
                     *reinterpret_cast<float2 *>(Mg + i * PFG_C + j) =
-                        make_float2(j <= i ? tf32r(d0 * v0) : 0.f, j + 1 <= i ? tf32r(d1 * v1) : 0.f);
+                        make_float2(j <= i ? d0 * v0 : 0.f, j + 1 <= i ? d1 * v1 : 0.f);
                 } else {
                     sA[i * PREP_LD + j] = j < i ? bet[i] * d0 * v0 : 0.f;
                     sA[i * PREP_LD + j + 1] = j + 1 < i ? bet[i] * d1 * v1 : 0.f;
@@ -598,7 +643,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
         tc::commit(&bar_mma);
     }
-    mbar_wait(&bar_mma, 1);
+    mbar_wait(&bar_mma, 0);   // third completion
     tc::fence_after();
     // this warp's 16 rows of W (w < 4) or U (w >= 4), 128 columns in two halves
     float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
@@ -862,7 +907,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 if (!TRANS) {  // D^T for the output kernel, off the critical path
                     float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cl) * PFG_C + t;
 #pragma unroll
-                    for (int j = 0; j < EC; ++j) dt[j * PFG_C] = tf32r(pv[j]);
+                    for (int j = 0; j < EC; ++j) dt[j * PFG_C] = pv[j];
                 }
             } else if (!TRANS) {                    // QH^T, same layout as D^T
                 float *qh = p.QH + (((size_t)n * VH + h) * PFG_D + cl) * PFG_C + t;
@@ -1025,15 +1070,28 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         y[nt][2] = sw_ld(sQT, PFG_D, col, r0 + g + 8); y[nt][3] = sw_ld(sQT, PFG_D, col + 1, r0 + g + 8);
     }
     const uint32_t aM = smem_u32(sM), aD = smem_u32(sDT);
+    // M D in split tf32 (M and D arrive in full fp32; each fragment is split
+    // into hi = tf32(x) and lo = tf32(x - hi), and hi.hi + lo.hi + hi.lo is
+    // accumulated), so the outputs keep about fp32 accuracy
 #pragma unroll
     for (int ks = 0; ks < PFG_C / 8; ++ks) {
-        uint32_t a[4];
+        uint32_t a[4], ah[4], al[4];
         lda_sw(aM, r0, ks, lane, a);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            ah[i] = f2tf32(__uint_as_float(a[i]));
+            al[i] = f2tf32(__uint_as_float(a[i]) - __uint_as_float(ah[i]));
+        }
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             uint32_t b0, b1;
             ldb_sw_rows(aD, PFG_D, cq + nt * 8, ks, lane, b0, b1);
-            mma_tf32(y[nt], a[0], a[1], a[2], a[3], b0, b1);
+            const uint32_t bh0 = f2tf32(__uint_as_float(b0)), bh1 = f2tf32(__uint_as_float(b1));
+            const uint32_t bl0 = f2tf32(__uint_as_float(b0) - __uint_as_float(bh0));
+            const uint32_t bl1 = f2tf32(__uint_as_float(b1) - __uint_as_float(bh1));
+            mma_tf32(y[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+            mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+            mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
         }
     }
     float sa = 0.f, sb = 0.f;

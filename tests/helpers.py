@@ -59,3 +59,14 @@ def gdn_state0(cfg, req=0):
     ring = synth.normal(synth.seed_of(cfg, "ring0", req), (CONVK, CD))
     ring[0] = 0.0  # dead slot: overwritten before any use
     return state, ring
+
+
+def record(what, value):
+    """Append a measured error to the file named by COLI_PARITY_LOG (if set),
+    one JSON object per line, so a GPU run leaves the actual margins behind."""
+    import json
+    import os
+    path = os.environ.get("COLI_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({what: value}) + "\n")

@@ -7,7 +7,7 @@ import pytest
 
 from conftest import load_pkg
 from helpers import (CD, CONVK, KD, KH, KH_G, H, HD, VD, VH_G, assert_close, gdn_params, gdn_state0,
-                     rel_l2)
+                     record, rel_l2)
 from oracle import Oracle, Reference
 import synth
 
@@ -130,7 +130,13 @@ def test_gdn_block_vs_oracle(be, orc, S):
                     r_ref, s_ref, KH=KH_G, KD=KD)
     want = y.reshape(S, VH_G * VD) @ Wo.T
     assert_close(got, want, what=f"gdn block S={S}")
-    assert rel_l2(be.gdn_state_get(layer, 0), s_ref) <= 1e-2
+    # The block's projections run on bf16 weights and activations while the
+    # oracle here is fed fp32 projections, so the state difference includes the
+    # projections' bf16 rounding; the recurrence's own bound (rel-L2 1e-3) is
+    # asserted with identical inputs in test_gpu_gdn.py / test_gpu_bench_configs.py.
+    err = rel_l2(be.gdn_state_get(layer, 0), s_ref)
+    record(f"gdn block S={S} state rel-L2 (bf16 projections)", err)
+    assert err <= 1e-2, err
     for t in (tqkv, tz, to):
         t.free()
 
