@@ -78,7 +78,10 @@ int  coli_cuda_gdn_full_available(void);
  * (c/backend_vulkan.h:114-116, impl c/backend_vulkan.c:1705-1743) with a
  * request dimension. `row` = kh*max_t + pos, as in the reference. Host rows
  * are fp32 and stored as bf16. kv_ensure zero-fills a new cache; calling it
- * again with the same geometry keeps the contents. kv_reset drops all layers. */
+ * again with the same geometry keeps the contents. kv_reset drops all layers.
+ * A one-request cache may be declared as rows, KH = 1 and max_t = KH*max_t
+ * (all coli_vk_kv_ensure knows); the first attention call naming (KH, max_t)
+ * with the same row count adopts that split, rows keep their addresses. */
 int  coli_cuda_kv_ensure(int layer, int batch, int KH, int max_t, int hd);
 int  coli_cuda_kv_row(int layer, int req, int row, const float *k, const float *v);
 /* New: n consecutive rows starting at row0 (bulk upload / read-back). */
@@ -260,6 +263,19 @@ int  coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const v
 /* Device-pointer form: x bf16 [S][I] (16-byte aligned), y [S][O] fp32
  * (y_bf16 = 0) or bf16 (1), asynchronous on the backend stream. */
 int  coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, void *y, int y_bf16);
+
+/* Attention + resident o_proj in one call, ctx staying on the device:
+ * coli_vk_gqa_project (c/backend_vulkan.h:165-170; called at c/qwen.c:623).
+ * Same q / cache contract as coli_cuda_gqa; out [S][Dout] fp32 host. */
+int  coli_cuda_gqa_project(int layer, const float *q, ColiCudaTensor *ot, float *out, int S, int H,
+                           int KH, int hd, int max_t, int st0, int T, float scale, int Dout);
+/* Delta rule + gated RMSNorm + resident out_proj in one call, y staying on
+ * the device: coli_vk_gdn_project (c/backend_vulkan.h:256-260; called at
+ * c/qwen.c:734). Same inputs as coli_cuda_gdn; out [Dout] fp32 host. */
+int  coli_cuda_gdn_project(int layer, const float *qn, const float *kn, const float *v,
+                           const float *z, const float *decay, const float *beta,
+                           const float *gnorm, ColiCudaTensor *ot, float *out, int KH, int KD,
+                           int VH, int VD, float eps, int Dout);
 
 /* Whole gated-GQA block for S rows of request 0 (coli_vk_gqa_full,
  * c/backend_vulkan.h:173-177; CPU c/qwen.c:595-665): q|gate, k, v

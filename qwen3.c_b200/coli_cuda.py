@@ -83,6 +83,8 @@ SIGNATURES = {
     "coli_cuda_tensor_bytes": ([_vp], ctypes.c_size_t),
     "coli_cuda_matmul": ([ctypes.POINTER(_vp), _fp, _fp, _vp, _fp] + [_i] * 5, _i),
     "coli_cuda_matmul_dev": ([_vp, _vp, _i, _vp, _i], _i),
+    "coli_cuda_gqa_project": ([_i, _fp, _vp, _fp] + [_i] * 7 + [_f, _i], _i),
+    "coli_cuda_gdn_project": ([_i] + [_fp] * 7 + [_vp, _fp] + [_i] * 4 + [_f, _i], _i),
     "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
     "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),

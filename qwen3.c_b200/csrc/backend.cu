@@ -313,6 +313,19 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     return 1;
 }
 
+// A one-request cache may have been declared as plain rows (KH = 1, max_t =
+// KH * max_t: what coli_vk_kv_ensure(layer, KH*max_t, hd, hd) passes, which
+// names no head count). Row kh*max_t + pos is the same address under either
+// split, so the first call that names (KH, max_t) with the same row count
+// adopts that split; the tensor maps cover all rows and stay valid.
+void kv_adopt_split(KvLayer &L, int KH, int max_t)
+{
+    if (L.k && L.batch == 1 && KH > 0 && max_t > 0 && L.KH != KH && (long long)L.KH * L.max_t == (long long)KH * max_t) {
+        L.KH = KH;
+        L.max_t = max_t;
+    }
+}
+
 int gqa_shape_ok(KvLayer &L, int H, int KH, int hd)
 {
     if (!L.k) return fail("KV cache of this layer not allocated (coli_cuda_kv_ensure)");
@@ -378,7 +391,6 @@ int gdn_shape_ok(GdnLayer &L, int KH, int KD, int VH, int VD, int need_conv)
     if (need_conv) {
         if (!L.hist || !L.conv_w) return fail("GDN conv history/weights not set for this layer");
         if (L.conv_k != 4 || L.conv_dim != 2 * KH * KD + VH * VD) return fail("GDN conv geometry mismatch");
-        if (!L.A_log) return fail("GDN A_log/dt_bias/gnorm not set (coli_cuda_gdn_params)");
     }
     return 1;
 }
@@ -396,7 +408,10 @@ int gdn_decode_run(int layer, int B, int req0, const void *qkv, const void *z, c
     ga.conv_w = L.conv_w; ga.A_log = L.A_log; ga.dt_bias = L.dt_bias; ga.gnorm = L.gnorm;
     ga.pdecay = pdecay; ga.pbeta = pbeta;
     if (pgnorm) ga.gnorm = pgnorm;
-    if (!pdecay && !L.A_log) return fail("GDN A_log/dt_bias/gnorm not set");
+    // gates from a / b need the layer's A_log / dt_bias; engine-packed params
+    // (decay | beta | gnorm) carry everything
+    if ((!pdecay && !L.A_log) || (!pgnorm && !L.gnorm))
+        return fail("GDN A_log/dt_bias/gnorm not set (coli_cuda_gdn_params)");
     ga.hist = L.hist + (size_t)req0 * 3 * L.conv_dim;
     ga.state = L.state + (size_t)req0 * VH * KD * VD;
     ga.y = y;
@@ -754,12 +769,17 @@ int coli_cuda_gqa_norm_weight(int layer, const float *qnw, const float *knw, int
 }
 
 // ------------------------------------------------------------------ GQA
-int coli_cuda_gqa(int layer, const float *q, float *ctx, int S, int H, int KH, int hd, int max_t,
-                  int st0, int T, float scale)
+}  // extern "C"
+
+// The attention core of coli_cuda_gqa / coli_cuda_gqa_project: S roped query
+// rows (host fp32) of request 0 at positions T-S .. T-1; ctx [S][H][hd] into
+// device memory, fp32 or bf16.
+static int gqa_core(int layer, const float *q, void *ctx_d, int out_bf16, int S, int H, int KH, int hd,
+                    int max_t, int st0, int T, float scale)
 {
-    READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
     KvLayer &L = G.kv[layer];
+    kv_adopt_split(L, KH, max_t);
     if (!gqa_shape_ok(L, H, KH, hd)) return 0;
     if (st0 != 0) return fail("st0 != 0 is not supported");
     if (max_t != L.max_t || S < 1 || T < S || T > L.max_t) return fail("bad S/T/max_t");
@@ -769,18 +789,25 @@ int coli_cuda_gqa(int layer, const float *q, float *ctx, int S, int H, int KH, i
     int *pos_d = (int *)scratch(S_POS, (size_t)S * 4);
     int *creq_d = (int *)scratch(S_CREQ, (size_t)S * 4);
     __nv_bfloat16 *qb = (__nv_bfloat16 *)scratch(S_Q, (size_t)S * H * hd * 2);
-    float *out = (float *)scratch(S_OUT, (size_t)S * H * hd * 4);
-    if (!pos_d || !creq_d || !qb || !out) return 0;
+    if (!pos_d || !creq_d || !qb) return 0;
     iota_kernel<<<(S + 255) / 256, 256, 0, stream()>>>(pos_d, creq_d, S, T - S, 0);
     CK(cudaGetLastError());
     split_q_kernel<<<S * H, hd, 0, stream()>>>(qd, qb, S * H, hd);
     CK(cudaGetLastError());
     g_launches += 2;
-    if (S >= PREFILL_MIN_ROWS) {
-        if (!gqa_prefill_rows(L, 0, S, T - S, H, qd, out, 0, 0, scale)) return 0;
-    } else if (!gqa_attend(L, S, H, pos_d, creq_d, T, qd, out, 0, 0, scale)) {
-        return 0;
-    }
+    if (S >= PREFILL_MIN_ROWS) return gqa_prefill_rows(L, 0, S, T - S, H, qd, ctx_d, 0, out_bf16, scale);
+    return gqa_attend(L, S, H, pos_d, creq_d, T, qd, ctx_d, 0, out_bf16, scale);
+}
+
+extern "C" {
+
+int coli_cuda_gqa(int layer, const float *q, float *ctx, int S, int H, int KH, int hd, int max_t,
+                  int st0, int T, float scale)
+{
+    READY();
+    float *out = (float *)scratch(S_OUT, (size_t)(S > 0 ? S : 1) * H * hd * 4);
+    if (!out) return 0;
+    if (!gqa_core(layer, q, out, 0, S, H, KH, hd, max_t, st0, T, scale)) return 0;
     if (!download(ctx, out, (size_t)S * H * hd * 4)) return 0;
     return check_dev_error();
 }
@@ -1053,11 +1080,14 @@ int coli_cuda_gdn_conv_set(int layer, int req, const float *ring)
 }
 
 // ------------------------------------------------------------------ GDN compute
-int coli_cuda_gdn(int layer, const float *qn, const float *kn, const float *v, const float *z,
-                  const float *decay, const float *beta, const float *gnorm, float *y, int KH,
-                  int KD, int VH, int VD, float eps)
+}  // extern "C"
+
+// The recurrence of coli_cuda_gdn / coli_cuda_gdn_project on pre-normalised
+// host inputs; y [VH*VD] fp32 into device memory.
+static int gdn_core(int layer, const float *qn, const float *kn, const float *v, const float *z,
+                    const float *decay, const float *beta, const float *gnorm, float *y_d, int KH, int KD,
+                    int VH, int VD, float eps)
 {
-    READY();
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
     GdnLayer &L = G.gdn[layer];
     if (!gdn_shape_ok(L, KH, KD, VH, VD, 0)) return 0;
@@ -1065,8 +1095,7 @@ int coli_cuda_gdn(int layer, const float *qn, const float *kn, const float *v, c
     float *in = (float *)scratch(S_IN0, (size_t)stride * 4);
     float *zd = (float *)upload(S_IN1, z, (size_t)VH * VD * 4);
     float *pd = (float *)scratch(S_P0, (size_t)(2 * VH + VD) * 4);
-    float *out = (float *)scratch(S_OUT, (size_t)VH * VD * 4);
-    if (!in || !zd || !pd || !out) return 0;
+    if (!in || !zd || !pd) return 0;
     CK(cudaMemcpyAsync(in, qn, (size_t)key_dim * 4, cudaMemcpyHostToDevice, stream()));
     CK(cudaMemcpyAsync(in + key_dim, kn, (size_t)key_dim * 4, cudaMemcpyHostToDevice, stream()));
     CK(cudaMemcpyAsync(in + 2 * key_dim, v, (size_t)VH * VD * 4, cudaMemcpyHostToDevice, stream()));
@@ -1076,10 +1105,23 @@ int coli_cuda_gdn(int layer, const float *qn, const float *kn, const float *v, c
     GdnDecodeArgs ga;
     memset(&ga, 0, sizeof(ga));
     ga.qkv = in; ga.z = zd; ga.decay = pd; ga.beta = pd + VH; ga.gnorm = pd + 2 * VH;
-    ga.state = L.state; ga.y = out;
+    ga.state = L.state; ga.y = y_d;
     ga.B = 1; ga.KH = KH; ga.KD = KD; ga.VH = VH; ga.VD = VD; ga.in_stride = stride; ga.eps = eps;
     CK(launch_gdn_decode(ga, 0, 0, 1, stream()));
     g_launches += 1;
+    return 1;
+}
+
+extern "C" {
+
+int coli_cuda_gdn(int layer, const float *qn, const float *kn, const float *v, const float *z,
+                  const float *decay, const float *beta, const float *gnorm, float *y, int KH,
+                  int KD, int VH, int VD, float eps)
+{
+    READY();
+    float *out = (float *)scratch(S_OUT, (size_t)VH * VD * 4);
+    if (!out) return 0;
+    if (!gdn_core(layer, qn, kn, v, z, decay, beta, gnorm, out, KH, KD, VH, VD, eps)) return 0;
     if (!download(y, out, (size_t)VH * VD * 4)) return 0;
     return check_dev_error();
 }

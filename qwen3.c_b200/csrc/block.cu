@@ -207,6 +207,7 @@ int gqa_block_dev(int layer, const __nv_bfloat16 *xb, int D, ColiCudaTensor *gq_
     if (S < 1 || pos_base < 0) return fail("bad S/pos_base");
     KvLayer &L = G.kv[layer];
     if (!L.k) return fail("KV layer %d not allocated", layer);
+    kv_adopt_split(L, KH, max_t);
     if (max_t > L.max_t || pos_base + S > L.max_t) return fail("positions beyond the cache (max_t %d)", L.max_t);
     if (!tensor_shape(gq_t, D, H * 2 * hd, "q|gate") || !tensor_shape(gk_t, D, KH * hd, "k") ||
         !tensor_shape(gv_t, D, KH * hd, "v") || !tensor_shape(out_t, H * hd, Dout, "o_proj"))
@@ -400,6 +401,43 @@ int coli_cuda_gdn_full_route(int layer, const float *x_in, const float *resid, i
     if (!gdn_block_dev(layer, xb, 1, D, gqkv_t, gz_t, pd, out_t, od, KH, KD, VH, VD, conv_dim, conv_k, eps, Dout))
         return 0;
     return route_tail(rd, od, router, ln_layer, resid_out, nrm_out, pr_out, 1, D, E, eps);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int coli_cuda_gqa_project(int layer, const float *q, ColiCudaTensor *ot, float *out, int S, int H, int KH, int hd,
+                          int max_t, int st0, int T, float scale, int Dout)
+{
+    READY();
+    if (S < 1) return fail("bad S");
+    if (!tensor_shape(ot, H * hd, Dout, "o_proj")) return 0;
+    auto *ctx = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * H * hd * 2);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!ctx || !od) return 0;
+    if (!gqa_core(layer, q, ctx, 1, S, H, KH, hd, max_t, st0, T, scale)) return 0;
+    if (!linear_dev(ot, ctx, S, od, 0)) return 0;
+    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
+    return check_dev_error();
+}
+
+int coli_cuda_gdn_project(int layer, const float *qn, const float *kn, const float *v, const float *z,
+                          const float *decay, const float *beta, const float *gnorm, ColiCudaTensor *ot, float *out,
+                          int KH, int KD, int VH, int VD, float eps, int Dout)
+{
+    READY();
+    if (!tensor_shape(ot, VH * VD, Dout, "out_proj")) return 0;
+    float *yd = (float *)scratch(S_OUT, (size_t)VH * VD * 4);
+    auto *yb = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)VH * VD * 2);
+    float *od = (float *)scratch(S_PY, (size_t)Dout * 4);
+    if (!yd || !yb || !od) return 0;
+    if (!gdn_core(layer, qn, kn, v, z, decay, beta, gnorm, yd, KH, KD, VH, VD, eps)) return 0;
+    CK(launch_f32_to_bf16(yd, yb, (size_t)VH * VD, stream()));
+    g_launches += 1;
+    if (!linear_dev(ot, yb, 1, od, 0)) return 0;
+    if (!download(out, od, (size_t)Dout * 4)) return 0;
+    return check_dev_error();
 }
 
 }  // extern "C"

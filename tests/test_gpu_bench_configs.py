@@ -162,6 +162,7 @@ def test_gqa_decode_headline_config(be, orc):
 
     for r in range(B):
         c = cache(r)
+        torch.cuda.synchronize()   # c is drawn on torch's stream, the copies run on the backend's
         for kh in range(KH):
             be.kv_rows_dev(layer, r, kh * T, int(pos[r]), c[0, kh].data_ptr(), c[1, kh].data_ptr(), dtype=1)
         be.sync()   # the copies run on the backend's stream: finish them before c is freed
