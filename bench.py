@@ -50,58 +50,70 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons of this process's GPU, polled through
+    NVML every ~2 ms from a thread while the timed region runs (so even a
+    region of a few milliseconds gets samples); nvidia-smi at 100 ms when
+    NVML is unavailable."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index):
-        self.idx = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, local_rank):
+        self.local = local_rank
+        self.sm, self.reasons, self.smax = [], set(), None
+        self._stop = threading.Event()
+        self.t = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        # NVML numbers every GPU of the machine; find this process's device by
+        # its PCI bus id (NVML writes the domain with 8 digits, CUDA with 4)
+        want = str(getattr(torch.cuda.get_device_properties(self.local), "pci_bus_id", "")).lower()
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            bus = pynvml.nvmlDeviceGetPciInfo(h).busId
+            bus = (bus.decode() if isinstance(bus, bytes) else str(bus)).lower()
+            if want and bus.endswith(want.split(":", 1)[-1]):
+                return h
+        return pynvml.nvmlDeviceGetHandleByIndex(self.local)
+
+    def _poll(self, h):
+        import pynvml
+        bits = [(n, getattr(pynvml, c, 0)) for n, c in self.REASONS]
+        while not self._stop.is_set():
+            try:
+                self.sm.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for n, b in bits:
+                    if r & b:
+                        self.reasons.add(n)
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            h = self._handle()
+            self.smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, args=(h,), daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception:
+            self.t = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.t:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                smax = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:7]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.smax,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 2 ms polling"}
 
 
 def dist_setup():
@@ -133,6 +145,16 @@ def max_over_ranks(ws, x):
 
 
 # ----------------------------------------------------------------- CPU legs
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_port_baseline(n_req=8):
     """Oracle port (c/qwen.c:598-663 restated) on the host cores: one decode
     token per request at context T_CTX, requests one after another (the
@@ -151,9 +173,23 @@ def cpu_port_baseline(n_req=8):
         orc.gqa_prologue(qg, k, v, qn, kn, T_CTX - 1, Kc, Vc)
         orc.gqa_attend(qg, Kc, Vc, T_CTX - 1)
     dt = time.perf_counter() - t0
-    return {"value": n_req / dt, "unit": "tok/s", "cores": orc.threads(), "kind": "port",
+    cores = orc.threads()
+    # the same work on one thread (the reference's shipped build has no OpenMP)
+    orc.set_threads(1)
+    n1 = 2
+    t1 = time.perf_counter()
+    for r in range(n1):
+        qg = synth.normal(10 + r, (1, H, 2 * HD))
+        k, v = synth.normal(100 + r, (1, KH, HD)), synth.normal(200 + r, (1, KH, HD))
+        orc.gqa_prologue(qg, k, v, qn, kn, T_CTX - 1, Kc, Vc)
+        orc.gqa_attend(qg, Kc, Vc, T_CTX - 1)
+    one = n1 / (time.perf_counter() - t1)
+    orc.set_threads(cores)
+    return {"value": n_req / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(), "value_1_thread": one,
             "sample": f"{n_req} requests x 1 decode token at context {T_CTX} (oracle/oracle.c "
-                      f"prologue+attend, OpenMP over heads as in c/qwen.c:640)"}
+                      f"prologue+attend, OpenMP over heads as in c/qwen.c:640); 1-thread figure "
+                      f"from {n1} requests"}
 
 
 def reference_arm(args):
@@ -297,9 +333,21 @@ def run_ours(args, ws, rank, local):
     secondary = {}
     if not args.quick:
         be.kv_reset()
-        secondary.update(run_gdn_secondary(be, args, st, peak_hbm))
-        secondary.update(run_prefill_secondary(be, args, st, peak_tc))
-        secondary.update(run_gdn_prefill_secondary(be, args, st, peak_hbm))
+        legs = [("gdn_decode", lambda: run_gdn_secondary(be, args, st, peak_hbm)),
+                ("gqa_prefill", lambda: run_prefill_secondary(be, args, st, peak_tc)),
+                ("gdn_prefill", lambda: run_gdn_prefill_secondary(be, args, st, peak_hbm)),
+                ("gqa_decode_grid", lambda: run_gqa_grid(be, args, st, peak_hbm)),
+                ("gdn_decode_grid", lambda: run_gdn_grid(be, args, st, peak_hbm))]
+        if not args.no_stack:
+            legs += [("stack_decode", lambda: run_stack_decode(be, args, st, peak_hbm)),
+                     ("stack_prefill", lambda: run_stack_prefill(be, args, st, peak_tc))]
+        for name, fn in legs:
+            try:
+                secondary.update(fn())
+            except Exception as e:   # a failed leg is reported, the headline line still prints
+                secondary[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            be.kv_reset()
+            be.gdn_reset()
 
     if rank != 0:
         return
@@ -416,6 +464,92 @@ def run_gdn_secondary(be, args, st, peak_hbm):
                            "achieved_GBs": bytes_ / (kavg / 1e3) / 1e9,
                            "frac_of_hbm": bytes_ / (kavg / 1e3) / 1e9 / peak_hbm,
                            "bytes_per_step": bytes_}}
+
+
+def _time(st, fn, n):
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def run_gqa_grid(be, args, st, peak_hbm):
+    """BASELINE config 2's grid: GQA decode at batch {1, 16, 64} x context
+    {4096, 32768} (one layer, bf16 cache; the headline is the 64 x 32768 point)."""
+    import torch
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(5)
+    layer = 5
+    for T in (4096, 32768):
+        for B in (1, 16, 64):
+            be.kv_ensure(layer, B, KH, T)
+            be.gqa_norm_weight(layer, (0.1 * torch.randn(HD, generator=g, device="cuda")).cpu().numpy(),
+                               (0.1 * torch.randn(HD, generator=g, device="cuda")).cpu().numpy())
+            rows = torch.randn(KH * T, HD, generator=g, device="cuda").bfloat16()
+            for r in range(B):
+                be.kv_rows_dev(layer, r, 0, KH * T, rows.data_ptr(), rows.data_ptr(), 1)
+            qg = torch.randn(B, H, 2 * HD, generator=g, device="cuda").bfloat16()
+            k = torch.randn(B, KH, HD, generator=g, device="cuda").bfloat16()
+            v = (torch.randn(B, KH, HD, generator=g, device="cuda") / 16).bfloat16()
+            pos = torch.full((B,), T - 1, dtype=torch.int32, device="cuda")
+            ctx = torch.empty(B, H, HD, dtype=torch.bfloat16, device="cuda")
+            be.sync()
+
+            def step():
+                be.gqa_decode_dev(layer, B, qg.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(),
+                                  ctx.data_ptr(), H, KH, HD, ROT, EPS, THETA, 1)
+            for _ in range(5):
+                step()
+            be.sync()
+            n = 50 if B * T >= 64 * 4096 else 200
+            ms = _time(st, step, n)
+            bytes_ = B * (2048 * T + 2048 + 16384 + 8192)
+            out[f"gqa_decode_B{B}_T{T}"] = {"value": B / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+                                            "GBs": bytes_ / (ms / 1e3) / 1e9,
+                                            "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm,
+                                            "l2_note": "inputs larger than L2" if bytes_ > 126e6 else
+                                            "working set fits L2 (repeated steps re-read it from L2)"}
+            del rows
+            be.kv_reset()
+    return {"gqa_decode_grid": out}
+
+
+def run_gdn_grid(be, args, st, peak_hbm):
+    """BASELINE config 3's grid: GatedDeltaNet decode at batch {1, 64, 256}."""
+    import torch
+    KHg, KD, VHg, VD = 16, 128, 32, 128
+    CD = 2 * KHg * KD + VHg * VD
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(6)
+    for B in (1, 64, 256):
+        be.gdn_setup(6, B, (torch.randn(CD, 4, generator=g, device="cuda") * 0.3).cpu().numpy(),
+                     (torch.rand(VHg, generator=g, device="cuda") * 2.77).cpu().numpy(),
+                     torch.randn(VHg, generator=g, device="cuda").cpu().numpy(),
+                     (1 + 0.1 * torch.randn(VD, generator=g, device="cuda")).cpu().numpy())
+        qkv = torch.randn(B, CD, generator=g, device="cuda").bfloat16()
+        z = torch.randn(B, VHg * VD, generator=g, device="cuda").bfloat16()
+        a = torch.randn(B, VHg, generator=g, device="cuda").bfloat16()
+        b = torch.randn(B, VHg, generator=g, device="cuda").bfloat16()
+        y = torch.empty(B, VHg * VD, dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            be.gdn_decode_dev(6, B, qkv.data_ptr(), z.data_ptr(), a.data_ptr(), b.data_ptr(), y.data_ptr(),
+                              16, 128, 32, 128, 1e-6, 1)
+        for _ in range(5):
+            step()
+        be.sync()
+        ms = _time(st, step, 100)
+        bytes_ = B * GDN_BYTES_PER_REQ
+        out[f"gdn_decode_B{B}"] = {"value": B / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+                                   "GBs": bytes_ / (ms / 1e3) / 1e9,
+                                   "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm,
+                                   "l2_note": "state larger than L2" if bytes_ > 126e6 else
+                                   "state fits L2 (repeated steps re-read it from L2)"}
+    return {"gdn_decode_grid": out}
 
 
 def run_prefill_secondary(be, args, st, peak_tc):
@@ -661,6 +795,7 @@ def main():
     ap.add_argument("--gdn-kheads", type=int, default=0,
                     help="GDN prefill leg: K heads owned by this GPU (e.g. 2 = one rank of an 8-way head shard)")
     ap.add_argument("--stack-batch", type=int, default=256, help="stack decode requests (all GPUs)")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 40-layer stack legs of the default run")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="stack prefill: gather layer outputs with NCCL instead of the fused peer stores")
     args = ap.parse_args()

@@ -61,7 +61,7 @@ struct GdnLayer {
 // Grow-only device scratch slots (activations staging, partials, indices).
 enum Slot { S_IN0, S_IN1, S_IN2, S_IN3, S_OUT, S_Q, S_PO, S_PML, S_POS, S_CREQ, S_P0, S_P1, S_P2,
             S_GQ, S_GK, S_GKT, S_GV, S_GL, S_GB, S_GW, S_GU, S_GM, S_GDT, S_GQH, S_GHS, S_GXS,
-            S_XB, S_PQ, S_PK, S_PV, S_PCTX, S_LPART, S_PAR, S_PY, S_RX, S_RXO, S_RN, S_RNB, S_RP, S_LCNT, S_COUNT };
+            S_XB, S_PQ, S_PK, S_PV, S_PCTX, S_PY2, S_LPART, S_PAR, S_PY, S_RX, S_RXO, S_RN, S_RNB, S_RP, S_LCNT, S_COUNT };
 
 struct Global {
     int ready = 0;

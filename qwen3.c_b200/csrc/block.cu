@@ -5,7 +5,8 @@
 // end of backend.cu (one translation unit).
 //
 // Weights are held in bf16 ([O][I], the engine's row-major layout), uploaded
-// once; activations between the steps stay on the device (bf16), only x goes
+// once; activations between the steps stay on the device (bf16, except the
+// GDN block's qkv / z, kept fp32 for the recurrence), only x goes
 // up and the block output comes back, as in the Vulkan backend's single
 // submit. The projections run on linear_kernel (tcgen05); the mixer steps are
 // the same kernels as the *_dev entry points.
@@ -238,27 +239,34 @@ int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTens
     if (!tensor_shape(gqkv_t, D, conv_dim, "in_proj_qkv") || !tensor_shape(gz_t, D, VH * VD, "in_proj_z") ||
         !tensor_shape(out_t, VH * VD, Dout, "out_proj"))
         return 0;
+    // The projections leave qkv and z in fp32: the recurrence is sensitive to
+    // the rounding of q and k (for a fast-decaying head y_t is nearly
+    // (q_t . k_t) d_t, and the gated norm rescales a small row back to unit
+    // size), so they are not rounded to bf16 between the GEMM and the mixer.
     const int ps = 2 * VH + VD;
-    auto *qkv = (__nv_bfloat16 *)scratch(S_PQ, (size_t)S * conv_dim * 2);
-    auto *z = (__nv_bfloat16 *)scratch(S_PK, (size_t)S * VH * VD * 2);
+    auto *qkv = (float *)scratch(S_PQ, (size_t)S * conv_dim * 4);
+    auto *z = (float *)scratch(S_PK, (size_t)S * VH * VD * 4);
+    auto *yf = (float *)scratch(S_PY2, (size_t)S * VH * VD * 4);
     auto *y = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * VH * VD * 2);
-    if (!qkv || !z || !y) return 0;
+    if (!qkv || !z || !yf || !y) return 0;
     {
         const ColiCudaTensor *ts[2] = {gqkv_t, gz_t};
         void *ys[2] = {qkv, z};
-        if (!linear_dev_multi(ts, 2, xb, S, ys, 1)) return 0;
+        if (!linear_dev_multi(ts, 2, xb, S, ys, 0)) return 0;
     }
     if (S >= GDN_CHUNK_MIN_ROWS) {
-        if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, y, KH, KD, VH, VD, eps, 1, 0, -1, pd))
+        if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, yf, KH, KD, VH, VD, eps, 0, 0, -1, pd))
             return 0;
     } else {
         for (int s = 0; s < S; ++s) {
             const float *pr = pd + (size_t)s * ps;
             if (!gdn_decode_run(layer, 1, 0, qkv + (size_t)s * conv_dim, z + (size_t)s * VH * VD, nullptr, nullptr,
-                                y + (size_t)s * VH * VD, KH, KD, VH, VD, eps, 1, pr, pr + VH, pr + 2 * VH))
+                                yf + (size_t)s * VH * VD, KH, KD, VH, VD, eps, 0, pr, pr + VH, pr + 2 * VH))
                 return 0;
         }
     }
+    CK(launch_f32_to_bf16(yf, y, (size_t)S * VH * VD, stream()));
+    g_launches += 1;
     return linear_dev(out_t, y, S, od, 0);
 }
 

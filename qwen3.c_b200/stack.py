@@ -7,7 +7,8 @@ every layer here reads synthetic, already-projected activations (random
 weights of the real shapes for the per-layer parameters). The KV caches and
 GDN states are resident per layer, as the engine would hold them.
 
-Two modes, each on one GPU of a multi-GPU job (one process per GPU):
+MixerStack (the benchmark form) has two modes, each on one GPU of a
+multi-GPU job (one process per GPU):
   decode   a batch of requests, each rank owning its own block of requests
            (sharding.request_shard); no collective on the data path.
   prefill  one long prompt, each rank computing a block of heads of every
@@ -15,6 +16,9 @@ Two modes, each on one GPU of a multi-GPU job (one process per GPU):
            by the output kernels themselves, storing into every rank's
            buffer over NVLink (fused=True, peer.PeerBuffer, one device-side
            barrier per layer), or by an NCCL all-gather after each layer.
+BlockStack is the same 40 layers with their projections and the residual
+stream flowing from layer to layer (the engine's loop without the MoE), for
+parity checks through the host-buffer block ABI.
 """
 import torch
 
@@ -214,3 +218,97 @@ class MixerStack:
         n_gqa = sum(k == "gqa" for k in self.kinds)
         n_gdn = self.n - n_gqa
         return n_gqa * 8192.0 * self.S * (self.S + 1), n_gdn * (self.S * 32896 + 2 * 1024 * 1024)
+
+
+# ------------------------------------------------------------ whole blocks
+D_MODEL = 2048
+
+
+def block_weights(seed, i):
+    """Random weights of the real shapes for model layer i (N(0, 0.02)
+    matrices; small vectors as a freshly initialised layer has them), a pure
+    function of (seed, i) so a checker can regenerate them."""
+    import numpy as np
+    rng = np.random.default_rng([seed, i])
+    w = lambda *s: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))   # noqa: E731
+    if is_full(i):
+        return dict(q=w(H * 2 * HD, D_MODEL), k=w(KH * HD, D_MODEL), v=w(KH * HD, D_MODEL),
+                    o=w(D_MODEL, H * HD), qn=np.zeros(HD, np.float32), kn=np.zeros(HD, np.float32),
+                    in_ln=np.zeros(D_MODEL, np.float32))
+    return dict(qkv=w(CD, D_MODEL), z=w(GVH * GVD, D_MODEL), a=w(GVH, D_MODEL), b=w(GVH, D_MODEL),
+                out=w(D_MODEL, GVH * GVD), conv=(rng.standard_normal((CD, 4), dtype=np.float32) * np.float32(0.3)),
+                A_log=np.log(rng.uniform(1.0, 16.0, GVH)).astype(np.float32), dt_bias=np.ones(GVH, np.float32),
+                gnorm=np.ones(GVD, np.float32), in_ln=np.zeros(D_MODEL, np.float32))
+
+
+def rmsnorm_zc(x, w, eps=EPS):
+    """x * rsqrt(mean x^2 + eps) * (1 + w), mean square in double (c/qwen.c:326-330)."""
+    import numpy as np
+    x = np.asarray(x, np.float32)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    return (x * (1.0 / np.sqrt((ms + eps).astype(np.float32))) * (1.0 + w)).astype(np.float32)
+
+
+def gdn_params_rows(wt, xn):
+    """The engine's per-token [decay | beta | gnorm] rows from the tiny a / b
+    projections it keeps on the host (c/qwen.c:681-686, 1356-1368)."""
+    import numpy as np
+    a, b = xn @ wt["a"].T, xn @ wt["b"].T
+    sp = np.where(a + wt["dt_bias"] > 20, a + wt["dt_bias"], np.log1p(np.exp(a + wt["dt_bias"])))
+    decay = np.exp(-np.exp(wt["A_log"]) * sp).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-b))).astype(np.float32)
+    return np.concatenate([decay, beta, np.broadcast_to(wt["gnorm"], (xn.shape[0], GVD))], axis=1).astype(np.float32)
+
+
+class BlockStack:
+    """The token-mixing blocks of the 40-layer stack with data flowing between
+    layers, as in the engine's layer loop minus the MoE (c/qwen.c:1347-1387):
+    x_{i+1} = x_i + block_i(rmsnorm_zc(x_i, in_ln_i)), each block = its
+    projections + mixer + out-projection on the device (coli_cuda_gqa_full /
+    coli_cuda_gdn_full_seq), weights bf16-resident, KV / state carried across
+    calls. Host buffers in and out per block (the engine-facing ABI)."""
+
+    def __init__(self, be, n_layers=40, seed=0, max_t=4096):
+        from .coli_cuda import DenseTensor
+        self.be, self.n, self.seed, self.max_t = be, n_layers, seed, max_t
+        self.t = []
+        kvi = gi = 0
+        for i in range(n_layers):
+            wt = block_weights(seed, i)
+            if is_full(i):
+                be.kv_ensure(KV_BASE + kvi, 1, KH, max_t)
+                be.gqa_norm_weight(KV_BASE + kvi, wt["qn"], wt["kn"])
+                self.t.append({n: DenseTensor(be, wt[n]) for n in ("q", "k", "v", "o")})
+                kvi += 1
+            else:
+                be.gdn_setup(GDN_BASE + gi, 1, wt["conv"], wt["A_log"], wt["dt_bias"], wt["gnorm"])
+                self.t.append({n: DenseTensor(be, wt[n]) for n in ("qkv", "z", "out")})
+                gi += 1
+        be.gdn_reset()
+        self.pos = 0
+
+    def forward(self, x):
+        """S new tokens through all layers; returns (per-layer normed inputs,
+        per-layer block outputs, final residual)."""
+        be, ins, outs = self.be, [], []
+        kvi = gi = 0
+        for i in range(self.n):
+            wt = block_weights(self.seed, i)
+            xn = rmsnorm_zc(x, wt["in_ln"])
+            t = self.t[i]
+            if is_full(i):
+                o = be.gqa_full(KV_BASE + kvi, xn, t["q"], t["k"], t["v"], t["o"], self.pos, max_t=self.max_t)
+                kvi += 1
+            else:
+                o = be.gdn_full_seq(GDN_BASE + gi, xn, gdn_params_rows(wt, xn), t["qkv"], t["z"], t["out"])
+                gi += 1
+            ins.append(xn)
+            outs.append(o)
+            x = x + o
+        self.pos += x.shape[0]
+        return ins, outs, x
+
+    def close(self):
+        for t in self.t:
+            for d in t.values():
+                d.free()

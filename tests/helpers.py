@@ -70,3 +70,4 @@ def record(what, value):
     if path:
         with open(path, "a") as f:
             f.write(json.dumps({what: value}) + "\n")
+

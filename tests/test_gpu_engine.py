@@ -24,9 +24,11 @@ ABI served by this backend. Both run the random 4-layer container on the same
   a second container whose matrices are stored already int8-round-tripped,
   so the CPU run computes with the very weights the device holds; the
   device keeps activations between the steps in bf16. Every block call is
-  dumped and replayed through fp32 projections (the container's weights)
-  around the oracle mixers, with the oracle's own KV cache / GDN state
-  chained over the run, and must agree within max-abs 2e-2 / cosine 0.9999,
+  dumped and replayed through the oracle mixers with the oracle's own KV
+  cache / GDN state chained over the run, between projections that take the
+  device's bf16-rounded operands with fp32 accumulation (the a / b gate
+  projections stay fp32 on the host, as the engine computes them), and must
+  agree within max-abs 2e-2 / cosine 0.9999,
   residual / post-norm / router outputs of the route tail included. The
   generated ids are recorded, not asserted: the top-2 expert choice and the
   greedy argmax are discontinuous, so a bf16-level difference in a block
@@ -41,6 +43,7 @@ import pytest
 
 import engine_container as ec
 from helpers import MAX_ABS, MIN_COS, cosine, record
+import synth
 from oracle import Oracle
 
 pytestmark = pytest.mark.gpu
@@ -134,6 +137,10 @@ def _rms_zc(x, w, eps):
     return (x * (1.0 / np.sqrt((ms + eps).astype(np.float32))) * (1.0 + w)).astype(np.float32)
 
 
+def bf(a):
+    return synth.bf16_round(np.ascontiguousarray(a, np.float32))
+
+
 def _check(what, got, want, worst):
     err = float(np.max(np.abs(np.asarray(got, np.float64) - want)))
     cos = cosine(got, want)
@@ -170,34 +177,38 @@ def test_engine_whole_blocks_on_gpu(tmp_path_factory):
     def gqa_block(kvi, x, pos_base, max_t):
         li = full[kvi]
         S = x.shape[0]
-        qg = (x @ w(li, "self_attn.q_proj.weight").T).reshape(S, H, 2 * hd).astype(np.float32)
-        k = (x @ w(li, "self_attn.k_proj.weight").T).reshape(S, KH, hd).astype(np.float32)
-        v = (x @ w(li, "self_attn.v_proj.weight").T).reshape(S, KH, hd).astype(np.float32)
+        xb = bf(x)
+        qg = bf(xb @ bf(w(li, "self_attn.q_proj.weight")).T).reshape(S, H, 2 * hd)
+        k = bf(xb @ bf(w(li, "self_attn.k_proj.weight")).T).reshape(S, KH, hd)
+        v = bf(xb @ bf(w(li, "self_attn.v_proj.weight")).T).reshape(S, KH, hd)
         Kc, Vc = kv.setdefault(kvi, (np.zeros((KH, max_t, hd), np.float32), np.zeros((KH, max_t, hd), np.float32)))
         orc.gqa_prologue(qg, k, v, w(li, "self_attn.q_norm.weight"), w(li, "self_attn.k_norm.weight"), pos_base,
                          Kc, Vc, rot=rot, theta=c["rope_theta"], eps=eps)
         ctx = orc.gqa_attend(qg, Kc, Vc, pos_base)
-        return ctx.reshape(S, H * hd) @ w(li, "self_attn.o_proj.weight").T
+        return bf(ctx.reshape(S, H * hd)) @ bf(w(li, "self_attn.o_proj.weight")).T
 
     def gdn_block(gi, x):
         li = lin[gi]
         kd, vh, vd = c["linear_key_head_dim"], c["linear_num_value_heads"], c["linear_value_head_dim"]
         cd = 2 * c["linear_num_key_heads"] * kd + vh * vd
         st = gstate.setdefault(gi, (np.zeros((vh, kd, vd), np.float32), np.zeros((4, cd), np.float32)))
-        f = lambda n: np.ascontiguousarray(x @ w(li, n).T, np.float32)   # noqa: E731
+        f = lambda n: np.ascontiguousarray(bf(x) @ bf(w(li, n)).T, np.float32)   # noqa: E731
+        ab = lambda n: np.ascontiguousarray(x @ w(li, n).T, np.float32)   # noqa: E731
         y = orc.gdn_seq(f("linear_attn.in_proj_qkv.weight"), f("linear_attn.in_proj_z.weight"),
-                        f("linear_attn.in_proj_a.weight"), f("linear_attn.in_proj_b.weight"),
+                        ab("linear_attn.in_proj_a.weight"), ab("linear_attn.in_proj_b.weight"),
                         w(li, "linear_attn.conv1d.weight"), w(li, "linear_attn.A_log"),
                         w(li, "linear_attn.dt_bias"), w(li, "linear_attn.norm.weight"), st[1], st[0],
                         KH=c["linear_num_key_heads"], KD=kd, eps=eps)
-        return y.reshape(x.shape[0], -1) @ w(li, "linear_attn.out_proj.weight").T
+        return bf(y.reshape(x.shape[0], -1)) @ bf(w(li, "linear_attn.out_proj.weight")).T
 
     def tail(li, resid, delta, r):
-        ro = resid + delta
-        nrm = _rms_zc(ro, w(li, "post_attention_layernorm.weight"), eps)
-        _check("resid_out", r["resid_out"], ro, worst)
+        # each step of the route tail against its own device inputs: the
+        # residual add against the oracle block, the post-norm of the device's
+        # residual, the router over the device's normed rows
+        _check("resid_out", r["resid_out"], resid + delta, worst)
+        nrm = _rms_zc(r["resid_out"], w(li, "post_attention_layernorm.weight"), eps)
         _check("nrm_out", r["nrm_out"], nrm, worst)
-        _check("router logits", r["pr_out"], nrm @ w(li, "mlp.gate.weight").T, worst)
+        _check("router logits", r["pr_out"], r["nrm_out"] @ w(li, "mlp.gate.weight").T, worst)
 
     for rec in ec.read_dump(dump):
         kind, layer, r = rec[0], rec[1], rec[2] if len(rec) > 2 else None
