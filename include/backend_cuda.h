@@ -46,6 +46,17 @@ int  coli_cuda_available(void);
 void coli_cuda_mem_info(size_t *used_bytes, size_t *tensor_count);
 /* New: the reason for the last 0 return (never NULL). */
 const char *coli_cuda_last_error(void);
+/* New: the time limit of every device-side wait (mbarrier waits in the
+ * kernels, the cross-rank barrier) in nanoseconds; 0 restores the default
+ * 2 s. On time-out a kernel raises the device error word and returns, the
+ * next synchronising call returns 0 with "pipeline wait timed out" and the
+ * backend is marked not ready (c/backend_vulkan.c:1836: a lost device), until
+ * coli_cuda_init is called again. */
+int  coli_cuda_set_wait_limit(unsigned long long ns);
+/* New, a failure-injection hook for tests: after n more successful device
+ * allocations the next one is refused as if cudaMalloc had failed (the call
+ * that needed it returns 0; the backend stays usable). n < 0 disables. */
+void coli_cuda_debug_fail_alloc(int n);
 /* New: wait for queued *_dev work and check the device error word. */
 int  coli_cuda_sync(void);
 /* New: the cudaStream_t the backend launches on; set it to run inside a

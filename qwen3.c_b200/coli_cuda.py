@@ -29,6 +29,8 @@ SIGNATURES = {
     "coli_cuda_available": ([], _i),
     "coli_cuda_mem_info": ([_sz, _sz], None),
     "coli_cuda_last_error": ([], ctypes.c_char_p),
+    "coli_cuda_set_wait_limit": ([ctypes.c_ulonglong], _i),
+    "coli_cuda_debug_fail_alloc": ([_i], None),
     "coli_cuda_sync": ([], _i),
     "coli_cuda_get_stream": ([], _vp),
     "coli_cuda_set_stream": ([_vp], _i),

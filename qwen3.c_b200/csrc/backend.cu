@@ -150,8 +150,16 @@ int cuda_fail(cudaError_t e, const char *what)
         if (!G.ready) return fail("backend not ready: %s", G.err); \
     } while (0)
 
+int g_fail_alloc_after = -1;   // test hook: allocations left before one is refused (-1 = off)
+
 int dev_alloc(void **p, size_t bytes)
 {
+    if (g_fail_alloc_after == 0) {
+        g_fail_alloc_after = -1;
+        *p = nullptr;
+        return fail("cudaMalloc(%zu): refused by the allocation-failure test hook", bytes);
+    }
+    if (g_fail_alloc_after > 0) --g_fail_alloc_after;
     cudaError_t e = cudaMalloc(p, bytes);
     if (e != cudaSuccess) { *p = nullptr; cudaGetLastError(); return fail("cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e)); }
     G.bytes += bytes;
@@ -621,6 +629,16 @@ void coli_cuda_mem_info(size_t *used_bytes, size_t *tensor_count)
 }
 
 const char *coli_cuda_last_error(void) { return G.err; }
+
+int coli_cuda_set_wait_limit(unsigned long long ns)
+{
+    READY();
+    const unsigned long long v = ns ? ns : COLI_WAIT_NS;
+    CK(cudaMemcpyToSymbol(g_wait_ns, &v, sizeof(v)));
+    return 1;
+}
+
+void coli_cuda_debug_fail_alloc(int n) { g_fail_alloc_after = n; }
 
 int coli_cuda_sync(void)
 {

@@ -64,18 +64,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait; returns false (and raises error 1) after COLI_WAIT_NS of
-// polling (or COLI_SPIN_LIMIT polls, whichever comes first).
+// Bounded wait; returns false (and raises error 1) after g_wait_ns of
+// polling (or COLI_SPIN_LIMIT polls, whichever comes first). The limit is
+// COLI_WAIT_NS unless the host set another (coli_cuda_set_wait_limit).
 #ifndef COLI_WAIT_NS
 #define COLI_WAIT_NS 2000000000ull
 #endif
+__device__ unsigned long long g_wait_ns = COLI_WAIT_NS;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *(volatile unsigned long long *)&g_wait_ns; }
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const uint64_t t0 = globaltimer_ns(), lim = wait_limit_ns();
     for (uint32_t i = 1; i < COLI_SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255) == 0) {
-            if (globaltimer_ns() - t0 > COLI_WAIT_NS) break;
+            if (globaltimer_ns() - t0 > lim) break;
             if (*(volatile int *)&g_dev_error) return false;  // another CTA gave up: bail out
         }
     }

@@ -28,12 +28,12 @@ __global__ void peer_barrier_kernel(PeerFlags a)
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.f[r] + a.rank), "r"(a.epoch) : "memory");
         // wait until rank r has announced the same epoch in this rank's array
         const uint32_t *mine = a.f[a.rank] + r;
-        const uint64_t t0 = globaltimer_ns();
+        const uint64_t t0 = globaltimer_ns(), lim = wait_limit_ns();
         for (uint32_t i = 0;; ++i) {
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
             if ((int32_t)(v - a.epoch) >= 0) break;
-            if ((i & 63) == 63 && globaltimer_ns() - t0 > COLI_WAIT_NS) {
+            if ((i & 63) == 63 && globaltimer_ns() - t0 > lim) {
                 raise_error(1);
                 break;
             }
