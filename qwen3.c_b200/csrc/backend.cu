@@ -640,6 +640,16 @@ int coli_cuda_set_wait_limit(unsigned long long ns)
 
 void coli_cuda_debug_fail_alloc(int n) { g_fail_alloc_after = n; }
 
+#ifdef COLI_SCAN_PROBE
+// development builds only: the chunk-walk timing probe (see gdn_prefill.cu)
+int coli_cuda_debug_scan_probe(long long *out, int n)
+{
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpyFromSymbol(out, coli::g_scan_probe, sizeof(long long) * (size_t)(n < 8192 ? n : 8192)));
+    return 1;
+}
+#endif
+
 int coli_cuda_sync(void)
 {
     READY();

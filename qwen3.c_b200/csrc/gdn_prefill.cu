@@ -716,6 +716,15 @@ template <int NC> struct ScanSmem {
 };
 
 
+// Timing probe of the chunk walk (development builds with -DCOLI_SCAN_PROBE
+// only): clock64 at fixed points of every chunk of the first CTA.
+#ifdef COLI_SCAN_PROBE
+__device__ long long g_scan_probe[1024 * 8];
+#define SCAN_PROBE(i, slot) do { if (!TRANS && blockIdx.x == 0 && (i) < 1024) g_scan_probe[(i) * 8 + (slot)] = clock64(); } while (0)
+#else
+#define SCAN_PROBE(i, slot) do { } while (0)
+#endif
+
 // Grid: blockIdx.x = (seg * VH + h) * NB + blk, NB = 128 / NC state blocks
 // (replay) or 256 / NC blocks of [Phi | Psi] (TRANS, segments 0 .. nseg-2).
 template <bool TRANS, int NC>
@@ -750,8 +759,11 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
         for (int s = 0; s < 2; ++s) { mbar_init(&a_full[s], 1); mbar_init(&a_empty[s], 1); }
         mbar_init(&k_full, 1); mbar_init(&k_empty, 1);
         mbar_init(&u_full, 1); mbar_init(&u_empty, SCAN_EPI / 64);  // one arrival per W-row warp
-        mbar_init(&h_ready, SCAN_EPI); mbar_init(&hs_ready, SCAN_EPI); mbar_init(&a_done, 1);
-        mbar_init(&d_ready, SCAN_EPI / 2); mbar_init(&c_done, 1);
+        // hand-off barriers count one arrival per epilogue warp (lane 0 after
+        // a __syncwarp), not one per thread: 512 arrivals on one shared word
+        // serialise and sat on the chain's critical path
+        mbar_init(&h_ready, SCAN_EPI / 32); mbar_init(&hs_ready, SCAN_EPI / 32); mbar_init(&a_done, 1);
+        mbar_init(&d_ready, SCAN_EPI / 64); mbar_init(&c_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) tc::alloc(&tmem_base, 2 * NC);
@@ -789,7 +801,9 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             for (int i = 0; i < cnt; ++i) {
                 const int s = i & 1;
                 mbar_wait(&a_full[s], (i >> 1) & 1);
+                SCAN_PROBE(i, 7);
                 mbar_wait(&h_ready, i & 1);
+                SCAN_PROBE(i, 0);
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < PFG_D / 8; ++ks)
@@ -800,6 +814,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 mbar_wait(&k_full, i & 1);
                 mbar_wait(&d_ready, i & 1);
                 mbar_wait(&hs_ready, i & 1);
+                SCAN_PROBE(i, 1);
                 tc::fence_after();
 #pragma unroll
                 for (int ks = 0; ks < PFG_C / 8; ++ks)
@@ -860,6 +875,7 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             // ---- h -> h^T (tf32) for (a); gamma_C h back into TMEM for (c)
             if (i > 0) {
                 mbar_wait(&c_done, (i - 1) & 1);
+                if (warp == 4 && lane == 0) SCAN_PROBE(i, 2);
                 tc::fence_after();
                 tc::ldn<EC>(tH + lane_off, hv);
                 tc::wait_ld();
@@ -868,15 +884,20 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             for (int j = 0; j < EC; ++j) *reinterpret_cast<float *>(sBh + kmaj_off(NC, c0 + j, r)) = tf32r(hv[j]);
             fence_proxy_async();                    // h^T visible to the tensor core
             tc::fence_before();
-            mbar_arrive(&h_ready);                  // (a) may start
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&h_ready);   // (a) may start
+            if (warp == 4 && lane == 0) SCAN_PROBE(i, 3);
 #pragma unroll
             for (int j = 0; j < EC; ++j) hv[j] *= gC;
             tc::stn<EC>(tH + lane_off, hv);
             tc::wait_st();
             tc::fence_before();
-            mbar_arrive(&hs_ready);                 // gamma_C h in place for (c)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&hs_ready);  // gamma_C h in place for (c)
+            if (warp == 4 && lane == 0) SCAN_PROBE(i, 4);
             // ---- P = [W; Q] h is in TMEM
             mbar_wait(&a_done, i & 1);
+            if (warp == 4 && lane == 0) SCAN_PROBE(i, 5);
             tc::fence_after();
             if (q < 2 || !TRANS) {
                 tc::ldn<EC>(tP + lane_off, pv);
@@ -903,7 +924,9 @@ gdn_pf_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                     *reinterpret_cast<float *>(sBd + kmaj_off(NC, c0 + j, t)) = tf32r(pv[j] * sc);
                 fence_proxy_async();                // D'^T visible to the tensor core
                 tc::fence_before();
-                mbar_arrive(&d_ready);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&d_ready);
+                if (warp == 4 && lane == 0) SCAN_PROBE(i, 6);
                 if (!TRANS) {  // D^T for the output kernel, off the critical path
                     float *dt = p.Dt + (((size_t)n * VH + h) * PFG_D + cl) * PFG_C + t;
 #pragma unroll
