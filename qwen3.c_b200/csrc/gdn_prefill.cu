@@ -354,12 +354,19 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
     }
     // V^T of the chunk per V head ([dv][64 tokens], tokens past S zero, tf32):
     // a warp writes 32 consecutive tokens of one row
+    // (four consecutive tokens per thread: one 16-byte store each)
     float *vt = p.VT + ((size_t)(2 * kh) * gridDim.x + blockIdx.x) * PFG_D * PFG_C;
-    for (int e = tid; e < 2 * PFG_D * PFG_C; e += 256) {
-        const int c = e >> 6, t = e & 63;     // c = local V channel (head c / 128)
-        const float *vrow = reinterpret_cast<const float *>(sX + t * PRT_CH);
-        const float v = t < nrow ? tf32r(vrow[c ^ (t & 31)]) : 0.f;
-        vt[(size_t)(c >> 7) * gridDim.x * PFG_D * PFG_C + (c & 127) * PFG_C + t] = v;
+    for (int e = tid; e < 2 * PFG_D * (PFG_C / 4); e += 256) {
+        const int c = e >> 4, t4 = (e & 15) * 4;   // c = local V channel (head c / 128)
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int t = t4 + u;
+            const float *vrow = reinterpret_cast<const float *>(sX + t * PRT_CH);
+            v[u] = t < nrow ? tf32r(vrow[c ^ (t & 31)]) : 0.f;
+        }
+        *reinterpret_cast<float4 *>(vt + (size_t)(c >> 7) * gridDim.x * PFG_D * PFG_C + (c & 127) * PFG_C + t4) =
+            make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
