@@ -307,6 +307,9 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     sa.part_o = po;
     sa.part_ml = pml;
     sa.nq = nq; sa.H = H; sa.KH = L.KH; sa.max_t = L.max_t; sa.n_splits = ns; sa.chunk = chunk;
+    // batched decode appends one row per request; the S rows of one request
+    // (creq given) append up to S rows ending at each query row's position
+    sa.appended = creq_d ? nq : 1;
     sa.scale_log2 = scale * 1.4426950408889634f;
     kt_mark(COLI_K_GQA_SPLIT);
     CK(launch_gqa_split(L.tmK, L.tmV, sa, stream()));

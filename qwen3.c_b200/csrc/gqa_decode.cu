@@ -38,6 +38,7 @@ template <typename TI>
 __global__ void __launch_bounds__(GQA_HD)
 gqa_prologue_kernel(GqaPrologueArgs p)
 {
+    griddep_launch();    // the split kernel may start its cache loads now
     const int n = blockIdx.x, j = blockIdx.y, d = threadIdx.x;
     const int H = p.H, KH = p.KH;
     const int Hin = p.Hin ? p.Hin : H, KHin = p.KHin ? p.KHin : KH;
@@ -150,6 +151,7 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
 {
     __shared__ float cs_t[GQA_PRO_ROWS][GQA_HD / 2], sn_t[GQA_PRO_ROWS][GQA_HD / 2];
     __shared__ float vec[GQA_PRO_WARPS][GQA_HD];
+    griddep_launch();    // the split kernel may start its cache loads now
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * rpc, rows = min(rpc, p.nq - n0);
     const int H = p.H, KH = p.KH, nv = H + KH;
@@ -272,12 +274,6 @@ gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant_
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KH = p.KH;
 
-    // q of the 8 heads sharing this KV head (bf16, roped)
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)n * p.H + kh * GQA_GRP) * GQA_HD);
-        uint4 *dst = reinterpret_cast<uint4 *>(qsm);
-        for (int i = tid; i < GQA_GRP * GQA_HD / 8; i += WARPS * 32) dst[i] = src[i];
-    }
     if (lane == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[warp][s], 1);
         fence_mbar_init();
@@ -306,8 +302,30 @@ gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant_
             tma_load_2d(vb + c * 2048, &tmV, 64 * c, row, &full[warp][s]);
         }
     };
+    // Launched as a programmatic dependent of the prologue: the first tiles of
+    // the ring stream in while the prologue still runs, except the tile that
+    // holds the row the prologue appends (position T - 1), which is loaded
+    // after the wait together with the prologue's roped q.
+    uint32_t deferred = 0;
     if (lane == 0)
-        for (int it = 0; it < STAGES && it < my_tiles; ++it) issue(it);
+        for (int it = 0; it < STAGES && it < my_tiles; ++it) {
+            if (start + (warp + it * WARPS) * GQA_TILE + GQA_TILE > T - p.appended) deferred |= 1u << it;
+            else issue(it);
+        }
+    griddep_wait();      // the prologue's q and appended rows are visible
+    griddep_launch();    // the combine may launch; it waits for this grid to finish
+    if (lane == 0 && deferred) {
+        fence_proxy_async();   // generic-proxy cache writes of the prologue before the async-proxy read
+        for (int it = 0; it < STAGES; ++it)
+            if (deferred >> it & 1u) issue(it);
+    }
+    // q of the 8 heads sharing this KV head (bf16, roped)
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)n * p.H + kh * GQA_GRP) * GQA_HD);
+        uint4 *dst = reinterpret_cast<uint4 *>(qsm);
+        for (int i = tid; i < GQA_GRP * GQA_HD / 8; i += WARPS * 32) dst[i] = src[i];
+    }
+    __syncthreads();
 
     // Q^T as the B operand: b0 = (dim = 16kk + 2(lane&3) + {0,1}, head = lane>>2), b1 = dim + 8
     uint32_t qf[16][2];
@@ -455,6 +473,7 @@ template <typename TI, typename TO>
 __global__ void __launch_bounds__(GQA_HD)
 gqa_combine_kernel(GqaCombineArgs p)
 {
+    griddep_wait();      // launched as a programmatic dependent of the split kernel
     const int n = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     const int kh = h / GQA_GRP, hl = h % GQA_GRP;
     const size_t base = ((size_t)n * p.KH + kh) * p.n_splits;
@@ -511,18 +530,27 @@ cudaError_t launch_gqa_split(const CUtensorMap &tk, const CUtensorMap &tv, const
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
-    dim3 grid(a.n_splits, a.KH, a.nq);
-    kern<<<grid, SPLIT_WARPS * 32, smem, st>>>(tk, tv, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_splits, a.KH, a.nq); cfg.blockDim = dim3(SPLIT_WARPS * 32);
+    cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // a dependent of the prologue
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
 }
 
 cudaError_t launch_gqa_combine(const GqaCombineArgs &a, int in_bf16, int out_bf16, cudaStream_t st)
 {
-    dim3 grid(a.nq, a.H);
-    if (in_bf16 && out_bf16) gqa_combine_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, GQA_HD, 0, st>>>(a);
-    else if (!in_bf16 && !out_bf16) gqa_combine_kernel<float, float><<<grid, GQA_HD, 0, st>>>(a);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nq, a.H); cfg.blockDim = dim3(GQA_HD); cfg.dynamicSmemBytes = 0; cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // a dependent of the split kernel
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    if (in_bf16 && out_bf16) return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<__nv_bfloat16, __nv_bfloat16>, a);
+    if (!in_bf16 && !out_bf16) return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<float, float>, a);
+    return cudaErrorInvalidValue;
 }
 
 int gqa_pick_splits(int nq, int KH, int tmax, int num_sms)

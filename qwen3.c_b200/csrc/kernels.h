@@ -57,6 +57,8 @@ struct GqaSplitArgs {
     float *part_o;           // [nq][KH][n_splits][8][hd]
     float *part_ml;          // [nq][KH][n_splits][8][2]
     int nq, H, KH, max_t, n_splits, chunk;
+    int appended;            // rows pos-appended+1 .. pos of each query row may be written by the
+                             // kernel just before (the prologue): loaded only after the grid dependency
     float scale_log2;
 };
 struct GqaCombineArgs {

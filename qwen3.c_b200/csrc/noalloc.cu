@@ -98,7 +98,7 @@ extern "C" int coli_cuda_gqa_decode_noalloc(int layer, int B, const void *qg, co
 
     GqaSplitArgs sa{};
     sa.q = q; sa.pos = pos_dev; sa.creq = nullptr; sa.part_o = po; sa.part_ml = pml;
-    sa.nq = B; sa.H = H; sa.KH = KH; sa.max_t = L.max_t; sa.n_splits = ns;
+    sa.nq = B; sa.H = H; sa.KH = KH; sa.max_t = L.max_t; sa.n_splits = ns; sa.appended = 1;
     sa.chunk = gqa_chunk_for(L.max_t, ns);
     sa.scale_log2 = (1.f / sqrtf((float)hd)) * 1.4426950408889634f;
     CK(launch_gqa_split(L.tmK, L.tmV, sa, stream()));
