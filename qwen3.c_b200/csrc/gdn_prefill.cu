@@ -1100,11 +1100,17 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
         y[nt][2] = sw_ld(sQT, PFG_D, col, r0 + g + 8); y[nt][3] = sw_ld(sQT, PFG_D, col + 1, r0 + g + 8);
     }
     const uint32_t aM = smem_u32(sM), aD = smem_u32(sDT);
-    // M D in split tf32 (M and D arrive in full fp32; each fragment is split
-    // into hi = tf32(x) and lo = tf32(x - hi), and hi.hi + lo.hi + hi.lo is
-    // accumulated), so the outputs keep about fp32 accuracy
+    // M D (M is causal: token columns past this warp's 16 rows are zero and
+    // skipped). The diagonal 16 x 16 block runs in split tf32 (M and D arrive
+    // in full fp32; each fragment is split into hi = tf32(x) and
+    // lo = tf32(x - hi), and hi.hi + lo.hi + hi.lo is accumulated): there
+    // M_tj carries the outputs of fast-decaying heads, whose rows the gated
+    // norm rescales. Older tokens come in with decayed weights and take
+    // plain tf32.
 #pragma unroll
     for (int ks = 0; ks < PFG_C / 8; ++ks) {
+        if (8 * ks > r0 + 15) break;               // warp-uniform: M is zero beyond the diagonal
+        const bool diag = 8 * ks >= r0;
         uint32_t a[4], ah[4], al[4];
         lda_sw(aM, r0, ks, lane, a);
 #pragma unroll
@@ -1117,10 +1123,12 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
             uint32_t b0, b1;
             ldb_sw_rows(aD, PFG_D, cq + nt * 8, ks, lane, b0, b1);
             const uint32_t bh0 = f2tf32(__uint_as_float(b0)), bh1 = f2tf32(__uint_as_float(b1));
-            const uint32_t bl0 = f2tf32(__uint_as_float(b0) - __uint_as_float(bh0));
-            const uint32_t bl1 = f2tf32(__uint_as_float(b1) - __uint_as_float(bh1));
-            mma_tf32(y[nt], al[0], al[1], al[2], al[3], bh0, bh1);
-            mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+            if (diag) {
+                const uint32_t bl0 = f2tf32(__uint_as_float(b0) - __uint_as_float(bh0));
+                const uint32_t bl1 = f2tf32(__uint_as_float(b1) - __uint_as_float(bh1));
+                mma_tf32(y[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+                mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+            }
             mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
         }
     }
