@@ -406,6 +406,13 @@ __device__ __forceinline__ uint32_t kmaj_off(int rows, int r, int k)
 // puts row 16 q + i in TMEM lane 32 q + i, so warp w reads rows 16 (w % 4)..
 // through the 16x256b shape, which is the mma.sync fragment layout.
 // Warps 0-3 own the K K^T / W rows, warps 4-7 the Q K^T / U rows.
+#ifdef COLI_SCAN_PROBE
+__device__ long long g_prep_probe[2 * 16];
+#define PREP_PROBE(slot) do { if (tid == 0 && blockIdx.y == 0 && (blockIdx.x == 0 || blockIdx.x == 200)) \
+    g_prep_probe[(blockIdx.x ? 16 : 0) + (slot)] = clock64(); } while (0)
+#else
+#define PREP_PROBE(slot) do { } while (0)
+#endif
 constexpr int PREP_THREADS = 256;
 __global__ void __launch_bounds__(PREP_THREADS)
 gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -462,7 +469,9 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // Q_lo lives in the A / T area (free until these products complete), then
     // K is loaded there again for K_lo.
     float *sLo = sA;                            // [64 x 128] swizzled like sQV / sK (32 KiB over sA, sT)
+    PREP_PROBE(0);
     mbar_wait(&bar_qk, 0);
+    PREP_PROBE(1);
     for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
         const float q = sQV[i], qh = tf32r(q);
         sQV[i] = qh;
@@ -495,7 +504,9 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int c = 0; c < 4; ++c) tma_load_3d(sLo + c * PFG_C * 32, &tmK, 32 * c, s0, kh, &bar_k2);
         }
     }
+    PREP_PROBE(2);
     const bool k2 = mbar_wait(&bar_k2, 0);
+    PREP_PROBE(3);
     for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
         const float k = sLo[i];
         sLo[i] = tf32r(k - tf32r(k));
@@ -515,6 +526,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         tc::commit(&bar_mma);
     }
     mbar_wait(&bar_mma, 1);   // a time-out raises the device error word
+    PREP_PROBE(4);
     tc::fence_after();
 
     // this warp's 16 rows of K K^T (w < 4) or Q K^T (w >= 4), all 64 columns:
@@ -553,6 +565,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int c = 0; c < 2; ++c) tma_load_3d(sQV + c * PFG_D * 32, &tmV, 32 * c, 0, h * nch + n, &bar_v);
         for (int c = 0; c < 2; ++c) tma_load_3d(sK + c * PFG_D * 32, &tmKT, 32 * c, 0, kh * nch + n, &bar_v);
     }
+    PREP_PROBE(5);
     // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
     // diagonal blocks by forward substitution (one column per thread), then
     // T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one block diagonal at a time.
@@ -607,6 +620,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     }
     __syncthreads();
+    PREP_PROBE(6);
     // T diag(beta gamma) and T diag(beta) as K-major tf32 A operands, over A and T
     {
         const int i = tid >> 2, j0 = (tid & 3) * 16;
@@ -650,7 +664,9 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
         tc::commit(&bar_mma);
     }
+    PREP_PROBE(7);
     mbar_wait(&bar_mma, 0);   // third completion
+    PREP_PROBE(8);
     tc::fence_after();
     // this warp's 16 rows of W (w < 4) or U (w >= 4), 128 columns in two halves
     float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
@@ -672,6 +688,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     tc::fence_before();
     __syncthreads();
+    PREP_PROBE(9);
     if (warp == 0) {
         tc::fence_after();
         tc::dealloc(tbase, 256);

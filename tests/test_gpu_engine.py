@@ -65,6 +65,10 @@ def _run(exe, snap, args, logits, env_extra=None):
     assert m, r.stdout[-2000:]
     ids = [int(t) for t in m.group(1).split()]
     lg = np.fromfile(logits, np.float32).reshape(-1, VOCAB)
+    rate = re.search(r"Prefill: ([0-9.]+)s .*decode: \d+ tok in [0-9.]+s \(([0-9.]+) tok/s\)", r.stdout)
+    if rate:
+        record(f"engine {os.path.basename(exe)} {' '.join(args) or 'default'}",
+               {"prefill_s_128": float(rate.group(1)), "decode_tok_s": float(rate.group(2))})
     return ids, lg, r.stdout
 
 
