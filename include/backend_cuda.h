@@ -315,6 +315,16 @@ int  coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTen
                             ColiCudaTensor *gz_t, const float *params, ColiCudaTensor *out_t,
                             float *out, int KH, int KD, int VH, int VD, int conv_dim,
                             int conv_k, float eps, int Dout);
+/* The same block with the tiny a / b projections on the device as well
+ * (c/qwen.c:709-711; the engine keeps them on the host and passes params,
+ * c/qwen.c:681-686): ga_t / gb_t are in_proj_a / in_proj_b [VH][D], run in
+ * one launch with in_proj_qkv / in_proj_z (S <= 16), and the gates come from
+ * the layer's A_log / dt_bias / gnorm (coli_cuda_gdn_params; c/qwen.c:722-727).
+ * S >= 64 runs the chunk-parallel prefill. No counterpart in the Vulkan ABI. */
+int  coli_cuda_gdn_full_ab(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t,
+                           ColiCudaTensor *gz_t, ColiCudaTensor *ga_t, ColiCudaTensor *gb_t,
+                           ColiCudaTensor *out_t, float *out, int KH, int KD, int VH, int VD,
+                           int conv_dim, int conv_k, float eps, int Dout);
 
 /* Route tail (the fused residual + post_ln + router epilogue):
  * coli_vk_layer_norm_weight / coli_vk_moe_route_available /

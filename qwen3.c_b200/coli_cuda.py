@@ -90,6 +90,7 @@ SIGNATURES = {
     "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
     "coli_cuda_gdn_full": ([_i, _fp, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_gdn_full_seq": ([_i, _fp, _i, _i, _vp, _vp, _fp, _vp, _fp] + [_i] * 6 + [_f, _i], _i),
+    "coli_cuda_gdn_full_ab": ([_i, _fp, _i, _i] + [_vp] * 5 + [_fp] + [_i] * 6 + [_f, _i], _i),
     "coli_cuda_moe_route_available": ([], _i),
     "coli_cuda_st_open": ([ctypes.c_char_p], _i),
     "coli_cuda_st_close": ([_i], None),
@@ -455,6 +456,17 @@ def _block_methods():
         self._ok(rc, "gdn_full")
         return out
 
+    def gdn_full_ab(self, layer, x, gqkv, gz, ga, gb, gout, KH=16, KD=128, VH=32, VD=128, eps=1e-6):
+        """S tokens with the a / b projections on the device (no params rows)."""
+        x, xp = _f32(x)
+        S, D = x.shape
+        out = np.zeros((S, gout.O), np.float32)
+        CD = 2 * KH * KD + VH * VD
+        rc = self.lib.coli_cuda_gdn_full_ab(layer, xp, S, D, gqkv.h, gz.h, ga.h, gb.h, gout.h, out.ctypes.data_as(_fp),
+                                            KH, KD, VH, VD, CD, 4, eps, gout.O)
+        self._ok(rc, "gdn_full_ab")
+        return out
+
     def matmul_dev(self, t, x, S, y, y_bf16=0):
         """Device pointers: x bf16 [S][I], y [S][O]."""
         self._ok(self.lib.coli_cuda_matmul_dev(t.h, x, S, y, y_bf16), "matmul_dev")
@@ -492,7 +504,8 @@ def _block_methods():
                                                    router.O), "gdn_full_route")
         return ro, nr, pr
 
-    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq, layer_norm_weight, gqa_full_route, gdn_full_route):
+    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq, gdn_full_ab, layer_norm_weight, gqa_full_route,
+              gdn_full_route):
         setattr(Backend, f.__name__, f)
 
 

@@ -514,7 +514,6 @@ int gdn_prefill_chunked(int layer, int req, int S, const void *qkv, const void *
         !make_f32_3d(&m.M, p.M, 64, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.U, p.U, 128, 64, nch * VH, 32, 64) ||
         !make_f32_3d(&m.Dt, p.Dt, 64, 128, nch * VH, 32, 128) ||
-        !make_f32_3d(&m.QH, p.QH, 64, 128, nch * VH, 32, 128) ||
         !make_f32_3d(&m.KT, p.KT, 64, 128, nch * KH, 32, 128))
         return 0;
     kt_mark(COLI_K_GDN_PREFILL);

@@ -227,11 +227,16 @@ int gqa_block_dev(int layer, const __nv_bfloat16 *xb, int D, ColiCudaTensor *gq_
     return linear_dev(out_t, ctx, S, od, 0);
 }
 
-// The GDN block on device data (request 0): x bf16 [S][D], params device
-// [S][2*VH+VD] -> out fp32 [S][Dout].
+// The GDN block on device data (request 0): x bf16 [S][D] -> out fp32
+// [S][Dout]. The gates come either from params rows on the device
+// [S][2*VH+VD] (decay | beta | gnorm, the engine's packing), or, with ga_t /
+// gb_t given (pd unused), from the a / b projections run on the device in the
+// same launch as in_proj_qkv / in_proj_z (c/qwen.c:709-711) and turned into
+// decay / beta inside the mixer kernels with the layer's A_log / dt_bias /
+// gnorm (c/qwen.c:722-727).
 int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
                   const float *pd, ColiCudaTensor *out_t, float *od, int KH, int KD, int VH, int VD, int conv_dim,
-                  int conv_k, float eps, int Dout)
+                  int conv_k, float eps, int Dout, ColiCudaTensor *ga_t = nullptr, ColiCudaTensor *gb_t = nullptr)
 {
     if (!check_layer(layer)) return fail("layer %d out of range", layer);
     if (S < 1) return fail("bad S");
@@ -239,6 +244,16 @@ int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTens
     if (!tensor_shape(gqkv_t, D, conv_dim, "in_proj_qkv") || !tensor_shape(gz_t, D, VH * VD, "in_proj_z") ||
         !tensor_shape(out_t, VH * VD, Dout, "out_proj"))
         return 0;
+    const bool dev_ab = ga_t && gb_t;
+    if (dev_ab) {
+        if (!tensor_shape(ga_t, D, VH, "in_proj_a") || !tensor_shape(gb_t, D, VH, "in_proj_b")) return 0;
+        const GdnLayer &L = G.gdn[layer];
+        if (!L.A_log || !L.gnorm || L.pVH != VH || L.pVD != VD)
+            return fail("GDN A_log/dt_bias/gnorm not set for %d x %d", VH, VD);
+        pd = nullptr;
+    } else if (!pd) {
+        return fail("GDN params rows or a / b projections required");
+    }
     // The projections leave qkv and z in fp32: the recurrence is sensitive to
     // the rounding of q and k (for a fast-decaying head y_t is nearly
     // (q_t . k_t) d_t, and the gated norm rescales a small row back to unit
@@ -248,20 +263,24 @@ int gdn_block_dev(int layer, const __nv_bfloat16 *xb, int S, int D, ColiCudaTens
     auto *z = (float *)scratch(S_PK, (size_t)S * VH * VD * 4);
     auto *yf = (float *)scratch(S_PY2, (size_t)S * VH * VD * 4);
     auto *y = (__nv_bfloat16 *)scratch(S_PCTX, (size_t)S * VH * VD * 2);
-    if (!qkv || !z || !yf || !y) return 0;
+    auto *ab = dev_ab ? (float *)scratch(S_PV, (size_t)S * 2 * VH * 4) : nullptr;   // a [S][VH] | b [S][VH]
+    if (!qkv || !z || !yf || !y || (dev_ab && !ab)) return 0;
+    float *a = dev_ab ? ab : nullptr, *b = dev_ab ? ab + (size_t)S * VH : nullptr;
     {
-        const ColiCudaTensor *ts[2] = {gqkv_t, gz_t};
-        void *ys[2] = {qkv, z};
-        if (!linear_dev_multi(ts, 2, xb, S, ys, 0)) return 0;
+        const ColiCudaTensor *ts[4] = {gqkv_t, gz_t, ga_t, gb_t};
+        void *ys[4] = {qkv, z, a, b};
+        if (!linear_dev_multi(ts, dev_ab ? 4 : 2, xb, S, ys, 0)) return 0;
     }
     if (S >= GDN_CHUNK_MIN_ROWS) {
-        if (!gdn_prefill_chunked(layer, 0, S, qkv, z, nullptr, nullptr, yf, KH, KD, VH, VD, eps, 0, 0, -1, pd))
+        if (!gdn_prefill_chunked(layer, 0, S, qkv, z, a, b, yf, KH, KD, VH, VD, eps, 0, 0, -1, pd))
             return 0;
     } else {
         for (int s = 0; s < S; ++s) {
-            const float *pr = pd + (size_t)s * ps;
-            if (!gdn_decode_run(layer, 1, 0, qkv + (size_t)s * conv_dim, z + (size_t)s * VH * VD, nullptr, nullptr,
-                                yf + (size_t)s * VH * VD, KH, KD, VH, VD, eps, 0, pr, pr + VH, pr + 2 * VH))
+            const float *pr = pd ? pd + (size_t)s * ps : nullptr;
+            if (!gdn_decode_run(layer, 1, 0, qkv + (size_t)s * conv_dim, z + (size_t)s * VH * VD,
+                                a ? a + (size_t)s * VH : nullptr, b ? b + (size_t)s * VH : nullptr,
+                                yf + (size_t)s * VH * VD, KH, KD, VH, VD, eps, 0, pr, pr ? pr + VH : nullptr,
+                                pr ? pr + 2 * VH : nullptr))
                 return 0;
         }
     }
@@ -348,6 +367,23 @@ int coli_cuda_gdn_full_seq(int layer, const float *x, int S, int D, ColiCudaTens
 {
     return gdn_full_rows(layer, x, S, D, gqkv_t, gz_t, params, out_t, out, KH, KD, VH, VD, conv_dim, conv_k, eps,
                          Dout);
+}
+
+int coli_cuda_gdn_full_ab(int layer, const float *x, int S, int D, ColiCudaTensor *gqkv_t, ColiCudaTensor *gz_t,
+                          ColiCudaTensor *ga_t, ColiCudaTensor *gb_t, ColiCudaTensor *out_t, float *out, int KH,
+                          int KD, int VH, int VD, int conv_dim, int conv_k, float eps, int Dout)
+{
+    READY();
+    if (S < 1 || !x || !out) return fail("bad S / buffers");
+    if (!ga_t || !gb_t) return fail("in_proj_a / in_proj_b required");
+    const __nv_bfloat16 *xb = upload_bf16(x, (size_t)S * D);
+    float *od = (float *)scratch(S_PY, (size_t)S * Dout * 4);
+    if (!xb || !od) return 0;
+    if (!gdn_block_dev(layer, xb, S, D, gqkv_t, gz_t, nullptr, out_t, od, KH, KD, VH, VD, conv_dim, conv_k, eps,
+                       Dout, ga_t, gb_t))
+        return 0;
+    if (!download(out, od, (size_t)S * Dout * 4)) return 0;
+    return check_dev_error();
 }
 
 int coli_cuda_moe_route_available(void) { return G.ready; }

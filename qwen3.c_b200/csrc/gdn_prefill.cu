@@ -1068,15 +1068,14 @@ size_t gdn_combine_smem() { return (size_t)(2 * PFG_D * CMB_LD + PFG_D * CMB_NC)
 // head's 128 columns (all in this CTA) and y = Y * rsqrt(mean Y^2 + eps) *
 // gnorm * silu(z).
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)   // three CTAs per SM (48 KiB shared memory each): at most 80 registers
 gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmDt,
-                  const __grid_constant__ CUtensorMap tmQH, GdnPrefillArgs p)
+                  GdnPrefillArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *sM = base;                    // [64 x 64] swizzled (2 boxes of 32 columns)
     float *sDT = sM + PFG_C * PFG_C;     // D^T [128 dv x 64 tokens] swizzled (2 boxes of 32 tokens)
-    float *sQT = sDT + PFG_D * PFG_C;    // QH^T, same layout
     __shared__ __align__(8) uint64_t bar;
     const int n = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
@@ -1085,37 +1084,27 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
-        mbar_expect_tx(&bar, (PFG_C * PFG_C + 2 * PFG_D * PFG_C) * 4);
+        mbar_expect_tx(&bar, (PFG_C * PFG_C + PFG_D * PFG_C) * 4);
         for (int c = 0; c < 2; ++c) tma_load_3d(sM + c * PFG_C * 32, &tmM, 32 * c, 0, n * VH + h, &bar);
         for (int c = 0; c < 2; ++c) tma_load_3d(sDT + c * PFG_D * 32, &tmDt, 32 * c, 0, n * VH + h, &bar);
-        for (int c = 0; c < 2; ++c) tma_load_3d(sQT + c * PFG_D * 32, &tmQH, 32 * c, 0, n * VH + h, &bar);
-    }
-    // the gate rows this thread stores at the end, loaded now so that their
-    // latency overlaps the tile loads and the products (item e = tid + 256 k:
-    // token e / 16, 8 columns from 8 (e % 16))
-    const TI *z = static_cast<const TI *>(p.z);
-    constexpr int ZW = sizeof(TI) == 2 ? 1 : 2;          // 16-byte pieces per 8 gate values
-    uint4 zpre[4][ZW];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int e = tid + 256 * k, tok = n * PFG_C + (e >> 4);
-        const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + (e & 15) * 8;
-#pragma unroll
-        for (int w = 0; w < ZW; ++w)
-            zpre[k][w] = tok < S ? reinterpret_cast<const uint4 *>(zr)[w] : make_uint4(0u, 0u, 0u, 0u);
     }
     // warp w: token rows 16 (w % 4).., value columns 64 (w / 4)..
     const int r0 = (warp & 3) * 16, cq = (warp >> 2) * 64;
     __shared__ float rsum[2][PFG_C];
+    // Y starts from QH, read from QH^T straight into the fragment layout
+    // (8 consecutive tokens of a column per 32-byte sector)
     float y[8][4];
+    {
+        const float *qt = p.QH + ((size_t)n * VH + h) * PFG_D * PFG_C;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int col = cq + nt * 8 + 2 * tq;
+            y[nt][0] = qt[col * PFG_C + r0 + g];     y[nt][1] = qt[(col + 1) * PFG_C + r0 + g];
+            y[nt][2] = qt[col * PFG_C + r0 + g + 8]; y[nt][3] = qt[(col + 1) * PFG_C + r0 + g + 8];
+        }
+    }
     __syncthreads();
     mbar_wait(&bar, 0);
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {    // Y starts from QH (element (token, dv) of QH^T)
-        const int col = cq + nt * 8 + 2 * tq;
-        y[nt][0] = sw_ld(sQT, PFG_D, col, r0 + g);     y[nt][1] = sw_ld(sQT, PFG_D, col + 1, r0 + g);
-        y[nt][2] = sw_ld(sQT, PFG_D, col, r0 + g + 8); y[nt][3] = sw_ld(sQT, PFG_D, col + 1, r0 + g + 8);
-    }
     const uint32_t aM = smem_u32(sM), aD = smem_u32(sDT);
     // M D (M is causal: token columns past this warp's 16 rows are zero and
     // skipped). The diagonal 16 x 16 block runs in split tf32 (M and D arrive
@@ -1149,6 +1138,21 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
             mma_tf32(y[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
         }
     }
+    // the gate rows this thread stores at the end, loaded now so that their
+    // latency overlaps the row statistics (item e = tid + 256 k: token e / 16,
+    // 8 columns from 8 (e % 16)); not earlier, to keep the products' registers
+    // within three CTAs per SM
+    const TI *z = static_cast<const TI *>(p.z);
+    constexpr int ZW = sizeof(TI) == 2 ? 1 : 2;          // 16-byte pieces per 8 gate values
+    uint4 zpre[4][ZW];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = tid + 256 * k, tok = n * PFG_C + (e >> 4);
+        const TI *zr = z + (size_t)tok * VHin * VD + vg * VD + (e & 15) * 8;
+#pragma unroll
+        for (int w = 0; w < ZW; ++w)
+            zpre[k][w] = tok < S ? reinterpret_cast<const uint4 *>(zr)[w] : make_uint4(0u, 0u, 0u, 0u);
+    }
     float sa = 0.f, sb = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
@@ -1158,14 +1162,14 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
     sa += __shfl_xor_sync(0xffffffffu, sa, 1); sa += __shfl_xor_sync(0xffffffffu, sa, 2);
     sb += __shfl_xor_sync(0xffffffffu, sb, 1); sb += __shfl_xor_sync(0xffffffffu, sb, 2);
     if (tq == 0) { rsum[warp >> 2][r0 + g] = sa; rsum[warp >> 2][r0 + g + 8] = sb; }
-    __syncthreads();                     // row sums of both column halves; every warp is done with sDT / sQT
+    __syncthreads();                     // row sums of both column halves; every warp is done with sM / sDT
     sa = rsum[0][r0 + g] + rsum[1][r0 + g];
     sb = rsum[0][r0 + g + 8] + rsum[1][r0 + g + 8];
     const float ra_ = 1.f / sqrtf(sa / VD + p.eps), rb_ = 1.f / sqrtf(sb / VD + p.eps);
     // normalised rows (times gnorm) to shared memory, then the gate and the
     // store row by row so that z loads and y stores are 16-byte vectors
     constexpr int YLD = PFG_D + 4;
-    float *sY = sDT;                     // [64][YLD] over the D^T / QH^T tiles
+    float *sY = sM;                      // [64][YLD] over the M / D^T tiles (33 KiB of 48)
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
         const int col = cq + nt * 8 + 2 * tq;
@@ -1217,7 +1221,7 @@ gdn_pf_out_kernel(const __grid_constant__ CUtensorMap tmM, const __grid_constant
 // ---------------------------------------------------------------- launch
 size_t gdn_prep_smem() { return (size_t)(2 * PFG_C * PFG_D + 2 * PFG_C * PREP_LD + 3 * 256) * 4 + 1024; }
 template <int NC> size_t gdn_scan_smem() { return (size_t)ScanSmem<NC>::TOTAL + 1024; }
-size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + 2 * PFG_D * PFG_C) * 4 + 1024; }
+size_t gdn_out_smem() { return (size_t)(PFG_C * PFG_C + PFG_D * PFG_C) * 4 + 1024; }
 
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st)
@@ -1263,7 +1267,7 @@ cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m,
     auto out = [&](auto kern) -> cudaError_t {
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_out_smem());
         if (e2 != cudaSuccess) return e2;
-        kern<<<dim3(nchunks, a.VH), 256, gdn_out_smem(), st>>>(m.M, m.Dt, m.QH, a);
+        kern<<<dim3(nchunks, a.VH), 256, gdn_out_smem(), st>>>(m.M, m.Dt, a);
         return cudaGetLastError();
     };
     return bf16 ? out(gdn_pf_out_kernel<__nv_bfloat16, __nv_bfloat16>) : out(gdn_pf_out_kernel<float, float>);

@@ -128,7 +128,7 @@ struct GdnPrefillArgs {
     int kh0, KHin, VHin;
 };
 struct GdnPrefillMaps {
-    CUtensorMap Q, K, V, W, U, M, Dt, QH, KT;
+    CUtensorMap Q, K, V, W, U, M, Dt, KT;
 };
 cudaError_t launch_gdn_prefill(const GdnPrefillArgs &a, const GdnPrefillMaps &m, int bf16,
                                cudaStream_t st);

@@ -141,6 +141,42 @@ def test_gdn_block_vs_oracle(be, orc, S):
         t.free()
 
 
+@pytest.mark.parametrize("S", [1, 20, 100])
+def test_gdn_block_device_ab_vs_oracle(be, orc, S):
+    """coli_cuda_gdn_full_ab: the a / b projections on the device too, in the
+    same launch as in_proj_qkv / in_proj_z (c/qwen.c:709-711), the gates from
+    the layer's A_log / dt_bias (c/qwen.c:722-727) inside the mixer kernels.
+    The checker's projections take the same bf16-rounded operands (x and W)
+    with fp32 accumulation and feed the oracle's gdn_step loop, so the state
+    is held to the recurrence's own bound (rel-L2 1e-3)."""
+    cfg = f"gdn_block_ab_{S}"
+    prm = gdn_params(cfg)
+    state, ring = gdn_state0(cfg)
+    Ws = {n: synth.bf16_round(_w(cfg, n, O, D)) for n, O in
+          (("qkv", CD), ("z", VH_G * VD), ("a", VH_G), ("b", VH_G))}
+    Wo = synth.bf16_round(_w(cfg, "o", D, VH_G * VD))
+    x = synth.normal(synth.seed_of(cfg, "x"), (S, D))
+    xb = synth.bf16_round(x)
+    layer = 20 + S % 7
+    be.gdn_setup(layer, 1, prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"])
+    be.gdn_state_set(layer, 0, state)
+    be.gdn_conv_set(layer, 0, ring)
+    ts = {n: _dense(be, w) for n, w in Ws.items()}
+    to = _dense(be, Wo)
+    got = be.gdn_full_ab(layer, x, ts["qkv"], ts["z"], ts["a"], ts["b"], to)
+    s_ref, r_ref = state.copy(), ring.copy()
+    p = {n: xb @ w.T for n, w in Ws.items()}
+    y = orc.gdn_seq(p["qkv"], p["z"], p["a"], p["b"], prm["conv_w"], prm["A_log"], prm["dt_bias"], prm["gnorm"],
+                    r_ref, s_ref, KH=KH_G, KD=KD)
+    want = synth.bf16_round(y.reshape(S, VH_G * VD)) @ Wo.T
+    assert_close(got, want, what=f"gdn block (device a/b) S={S}")
+    err = rel_l2(be.gdn_state_get(layer, 0), s_ref)
+    record(f"gdn block S={S} state rel-L2 (device a/b)", err)
+    assert err <= 1e-3, err
+    for t in list(ts.values()) + [to]:
+        t.free()
+
+
 def _rmsnorm_zc(x, w, eps=1e-6):
     """c/qwen.c:326-330 (double accumulation of the mean square)."""
     x = np.asarray(x, np.float32)
