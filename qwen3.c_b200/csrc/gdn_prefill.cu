@@ -427,7 +427,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1; later T diag(beta), K-major
     float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
     __shared__ float G[PFG_C], bet[PFG_C], bgam[PFG_C];   // bgam = beta e^G
-    __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_mma, bar_k2;
+    __shared__ __align__(8) uint64_t bar_qk, bar_v, bar_mma;
     __shared__ uint32_t tmem_base;
 
     const int n = blockIdx.x, h = blockIdx.y, kh = h >> 1;
@@ -437,7 +437,6 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_init(&bar_qk, 1);
         mbar_init(&bar_v, 1);
         mbar_init(&bar_mma, 1);
-        mbar_init(&bar_k2, 1);
         fence_mbar_init();
     }
     if (warp == 0) tc::alloc(&tmem_base, 256);
@@ -464,19 +463,20 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // Q and K arrive in full fp32. Q K^T becomes M, which carries the outputs
     // (for a fast-decaying head almost all of y_t is M_tt d_t), so it runs as
     // three tf32 products, hi.hi + lo.hi + hi.lo (the split-tf32 scheme; a
-    // product of plain tf32 roundings misses the output tolerance there).
-    // K K^T only enters through the T solve and uses the rounded operands.
-    // Q_lo lives in the A / T area (free until these products complete), then
-    // K is loaded there again for K_lo.
+    // product of plain tf32 roundings misses the output tolerance there);
+    // K K^T, which enters the T solve, likewise. The tensor core reads the
+    // tf32 truncation of an fp32 operand, so the Q and K tiles serve as the
+    // hi parts as they are (hi = x with the 13 low mantissa bits cleared) and
+    // lo = x - hi is exact in fp32: only the lo tiles are written, first Q_lo,
+    // then K_lo over it, in the A / T area (free until these products complete).
     float *sLo = sA;                            // [64 x 128] swizzled like sQV / sK (32 KiB over sA, sT)
+    auto lo_of = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
     PREP_PROBE(0);
     mbar_wait(&bar_qk, 0);
     PREP_PROBE(1);
-    for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
-        const float q = sQV[i], qh = tf32r(q);
-        sQV[i] = qh;
-        sLo[i] = tf32r(q - qh);
-        sK[i] = tf32r(sK[i]);
+    for (int i = tid; i < PFG_C * PFG_D / 4; i += PREP_THREADS) {
+        const float4 q = reinterpret_cast<const float4 *>(sQV)[i];
+        reinterpret_cast<float4 *>(sLo)[i] = make_float4(lo_of(q.x), lo_of(q.y), lo_of(q.z), lo_of(q.w));
     }
     fence_proxy_async();                        // generic-proxy writes visible to the tensor core
     tc::fence_before();
@@ -484,7 +484,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     constexpr uint32_t IDP = tc::idesc_tf32(64, 64);
     const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQV), aLo = smem_u32(sLo);
     if (tid == 0) {
-        // K K^T -> columns 0..63, Q K^T -> 64..127
+        // K K^T -> columns 0..63, Q K^T -> 64..127: hi.hi, then Q_lo.K_hi
         tc::fence_after();
 #pragma unroll
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
@@ -498,30 +498,27 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aLo + off), tc::desc_k_sw128(aK + off), IDP, 1);
         }
         tc::commit(&bar_mma);
-        // full K again, over Q_lo, once the products above have read it
-        if (mbar_wait(&bar_mma, 0)) {
-            mbar_expect_tx(&bar_k2, PFG_C * PFG_D * 4);
-            for (int c = 0; c < 4; ++c) tma_load_3d(sLo + c * PFG_C * 32, &tmK, 32 * c, s0, kh, &bar_k2);
-        }
     }
     PREP_PROBE(2);
-    const bool k2 = mbar_wait(&bar_k2, 0);
+    mbar_wait(&bar_mma, 0);                     // Q_lo has been read: K_lo over it
+    tc::fence_after();
     PREP_PROBE(3);
-    for (int i = tid; i < PFG_C * PFG_D; i += PREP_THREADS) {
-        const float k = sLo[i];
-        sLo[i] = tf32r(k - tf32r(k));
+    for (int i = tid; i < PFG_C * PFG_D / 4; i += PREP_THREADS) {
+        const float4 k = reinterpret_cast<const float4 *>(sK)[i];
+        reinterpret_cast<float4 *>(sLo)[i] = make_float4(lo_of(k.x), lo_of(k.y), lo_of(k.z), lo_of(k.w));
     }
     fence_proxy_async();
     tc::fence_before();
     __syncthreads();
     if (tid == 0) {
+        // Q_hi.K_lo; K_hi.K_lo + K_lo.K_hi
         tc::fence_after();
-        if (k2) {
 #pragma unroll
-            for (int ks = 0; ks < PFG_D / 8; ++ks) {
-                const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
-                tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aLo + off), IDP, 1);
-            }
+        for (int ks = 0; ks < PFG_D / 8; ++ks) {
+            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aLo + off), IDP, 1);
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aLo + off), IDP, 1);
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aLo + off), tc::desc_k_sw128(aK + off), IDP, 1);
         }
         tc::commit(&bar_mma);
     }
@@ -555,6 +552,31 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
         }
     }
+    // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks. The
+    // diagonal block of this warp's 16 A rows right away, by forward
+    // substitution (lane c < 16 = column c, kept in registers; two partial
+    // sums shorten the dependent chain), while warps 4-7 store M.
+    if (!second) {
+        __syncwarp();                              // this warp's A rows written
+        if (lane < 16) {
+            const int c = lane;
+            float t[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                // t[j] = 0 for j < c, so the sum may run over every j < i
+                float acc0 = (i == c) ? 1.f : 0.f, acc1 = 0.f;
+#pragma unroll
+                for (int j = 0; j + 1 < i; j += 2) {
+                    acc0 -= sA[(r0 + i) * PREP_LD + r0 + j] * t[j];
+                    acc1 -= sA[(r0 + i) * PREP_LD + r0 + j + 1] * t[j + 1];
+                }
+                if (i & 1) acc0 -= sA[(r0 + i) * PREP_LD + r0 + i - 1] * t[i - 1];
+                t[i] = acc0 + acc1;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sT[(r0 + i) * PREP_LD + r0 + c] = t[i];
+        }
+    }
     tc::fence_before();
     __syncthreads();
     // V^T replaces Q and K^T replaces K in shared memory while T is solved
@@ -566,27 +588,10 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int c = 0; c < 2; ++c) tma_load_3d(sK + c * PFG_D * 32, &tmKT, 32 * c, 0, kh * nch + n, &bar_v);
     }
     PREP_PROBE(5);
-    // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks: the four
-    // diagonal blocks by forward substitution (one column per thread), then
-    // T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one block diagonal at a time.
-    // The blocks above the diagonal are never written: the operand build
-    // below treats them as zero.
+    // The off-diagonal blocks: T_pq = -T_pp * sum_{r=q}^{p-1} A_pr T_rq one
+    // block diagonal at a time. The blocks above the diagonal are never
+    // written: the operand build below treats them as zero.
     {
-        if (tid < 64) {   // column c of diagonal block o, kept in registers
-            const int o = (tid >> 4) * 16, c = tid & 15;
-            float t[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                // t[j] = 0 for j < c, so the sum may run over every j < i
-                float acc = (i == c) ? 1.f : 0.f;
-#pragma unroll
-                for (int j = 0; j < i; ++j) acc -= sA[(o + i) * PREP_LD + o + j] * t[j];
-                t[i] = acc;
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sT[(o + i) * PREP_LD + o + c] = t[i];
-        }
-        __syncthreads();
         for (int dist = 1; dist < 4; ++dist) {
             const int nblk = 4 - dist;                 // blocks (p, p - dist), p = dist..3
             // X_p = sum_{r=q}^{p-1} A_pr T_rq; a thread owns 4 adjacent columns
