@@ -650,6 +650,12 @@ int coli_cuda_debug_scan_probe(long long *out, int n)
     CK(cudaMemcpyFromSymbol(out, coli::g_scan_probe, sizeof(long long) * (size_t)(n < 8192 ? n : 8192)));
     return 1;
 }
+int coli_cuda_debug_lin_probe(unsigned long long *out, int n)
+{
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpyFromSymbol(out, coli::g_lin_probe, sizeof(unsigned long long) * (size_t)(n < 8192 ? n : 8192)));
+    return 1;
+}
 int coli_cuda_debug_prep_probe(long long *out)
 {
     CK(cudaDeviceSynchronize());

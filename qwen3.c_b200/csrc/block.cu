@@ -33,6 +33,9 @@ int make_bf16_2d(CUtensorMap *m, const void *base, int inner, int outer, int box
 }
 
 // y[S][O] = x[S][I] W^T on the device (x bf16, y fp32 or bf16).
+#ifndef LIN_CTA_MULT
+#define LIN_CTA_MULT 1      // split-K targets this many CTAs per SM for decode
+#endif
 int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, int y_bf16)
 {
     if (!t || !t->w) return fail("dense tensor not uploaded");
@@ -41,7 +44,7 @@ int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, 
     if (!make_bf16_2d(&tx, x, t->I, S, 64, bn)) return 0;
     const int tiles = ((t->O + 127) / 128) * ((S + bn - 1) / bn), nk = (t->I + 63) / 64;
     int splits = 1;
-    if (2 * tiles <= G.num_sms) splits = std::max(1, std::min(G.num_sms / tiles, nk / 4));
+    if (2 * tiles <= LIN_CTA_MULT * G.num_sms) splits = std::max(1, std::min(LIN_CTA_MULT * G.num_sms / tiles, nk / 4));
     LinearArgs la;
     memset(&la, 0, sizeof(la));
     la.y = y; la.S = S; la.I = t->I; la.O = t->O; la.y_bf16 = y_bf16;
@@ -57,8 +60,9 @@ int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, 
         }
         la.tile_cnt = (int *)G.slot[S_LCNT];
     }
-    CK(launch_linear(t->tm, tx, la, bn, splits, stream()));
-    g_launches += (splits > 1 && bn > 16) ? 2 : 1;
+    int nl = 1;
+    CK(launch_linear(t->tm, tx, la, bn, splits, stream(), &nl));
+    g_launches += nl;
     return 1;
 }
 
@@ -85,7 +89,7 @@ int linear_dev_multi(const ColiCudaTensor *const *t, int nw, const __nv_bfloat16
     if (!make_bf16_2d(&tx, x, t[0]->I, S, 64, 16)) return 0;
     const int nk = (t[0]->I + 63) / 64;
     int splits = 1;
-    if (2 * tiles <= G.num_sms) splits = std::max(1, std::min(G.num_sms / tiles, nk / 4));
+    if (2 * tiles <= LIN_CTA_MULT * G.num_sms) splits = std::max(1, std::min(LIN_CTA_MULT * G.num_sms / tiles, nk / 4));
     LinearArgs la;
     memset(&la, 0, sizeof(la));
     la.S = S; la.I = t[0]->I; la.O = Osum; la.y_bf16 = y_bf16;

@@ -144,9 +144,11 @@ struct LinearArgs {
     int y_bf16;
     int *tile_cnt;        // split-K arrival counters, one per output tile, zero between
                           // launches (nullptr = a separate reduce kernel adds the splits)
+    int cluster;          // set by the launchers: the K splits of a tile form one thread-block
+                          // cluster and are added through distributed shared memory
 };
 cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
-                          cudaStream_t st);
+                          cudaStream_t st, int *launches = nullptr);
 // Up to LIN_MAXW projections of the same x ([S][I], S <= 16) in one launch:
 // weight w has O[w] outputs into y[w]; the output tiles of all weights share
 // the grid (and the split-K plan, with the reduction in the kernel).

@@ -10,14 +10,29 @@
 // are added in split order (deterministic): for up to 16 tokens by the last
 // split of each output tile to arrive (an atomic counter per tile), with no
 // second launch; for more tokens by linear_reduce_kernel.
+// For up to 16 tokens and at most 8 splits the splits of a tile run as one
+// thread-block cluster instead: each leaves its partial in its own shared
+// memory and the first adds them in split order through distributed shared
+// memory (no global partials, counters or fences on the tail).
 // Warp roles: 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 = epilogue
 // (TMEM lane = output feature; stores are contiguous along o for each token).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc05.cuh"
 
 namespace coli {
 
+#ifndef LIN_DEC_STAGES
+#define LIN_DEC_STAGES 6    // ring stages of the decode (BN = 16) kernel: two CTAs fit an SM
+#endif
+#ifndef LIN_EARLY
+#define LIN_EARLY 0         // 1: let the next programmatic launch start as soon as this grid is resident (measured: no gain)
+#endif
+#ifndef LIN_MAX_CLUSTER
+#define LIN_MAX_CLUSTER 8   // most K splits reduced in a cluster (portable cluster size)
+#endif
 constexpr int LN_BM = 128, LN_BK = 64;
 constexpr int LN_A_BYTES = LN_BM * LN_BK * 2;   // 16 KiB
 
@@ -27,7 +42,8 @@ template <int BN> struct LinSmem {
     // as many ring stages as ~220 KiB holds (at most 12): a weight-streaming
     // decode pass needs many bytes in flight per SM to cover HBM latency
     static constexpr int STAGES_FIT = (220 * 1024) / STAGE;
-    static constexpr int STAGES = STAGES_FIT > 12 ? 12 : (STAGES_FIT < 2 ? 2 : STAGES_FIT);
+    static constexpr int STAGES_MAX = BN == 16 ? LIN_DEC_STAGES : 12;
+    static constexpr int STAGES = STAGES_FIT > STAGES_MAX ? STAGES_MAX : (STAGES_FIT < 2 ? 2 : STAGES_FIT);
     static constexpr int TOTAL = STAGES * STAGE + 1024;
     static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
 };
@@ -42,6 +58,16 @@ struct LinWeights {
     size_t part_off[LIN_MAXW];
     int nw;
 };
+
+// Timing probe (development builds with -DCOLI_SCAN_PROBE only): globaltimer
+// at fixed points of every CTA of the decode kernel.
+#ifdef COLI_SCAN_PROBE
+__device__ unsigned long long g_lin_probe[1024 * 8];
+#define LIN_PROBE(slot) do { if (BN == 16) { const int c_ = blockIdx.x + gridDim.x * blockIdx.z; \
+    if (c_ < 1024) g_lin_probe[c_ * 8 + (slot)] = globaltimer_ns(); } } while (0)
+#else
+#define LIN_PROBE(slot) do { } while (0)
+#endif
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
@@ -63,6 +89,7 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
     const int o0 = ((int)blockIdx.x - (wi ? lw.tile_end[wi - 1] : 0)) * LN_BM, s0 = blockIdx.y * BN, z = blockIdx.z;
     const int nk = (a.I + LN_BK - 1) / LN_BK;
     const int k0 = z * a.kchunks, k1 = min(nk, k0 + a.kchunks), cnt = max(0, k1 - k0);
+    const bool clus = BN <= 64 && a.cluster && gridDim.z > 1;   // uniform across the cluster
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < LN_STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
@@ -74,9 +101,11 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
     __syncthreads();
     tc::fence_after();
     const uint32_t tD = tmem_base;
+    if (LIN_EARLY) griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
+            LIN_PROBE(0);
             tma_prefetch_desc(tmW); tma_prefetch_desc(&tmX);
             // the weights do not depend on the previous kernel: the first ring's
             // worth streams in while that kernel finishes (programmatic launch)
@@ -86,6 +115,7 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
                 tma_load_2d(sm + i * LinSmem<BN>::STAGE, tmW, (k0 + i) * LN_BK, o0, &full[i]);
             }
             griddep_wait();
+            LIN_PROBE(1);
             for (int i = 0; i < pre; ++i)
                 tma_load_2d(sm + i * LinSmem<BN>::STAGE + LN_A_BYTES, &tmX, (k0 + i) * LN_BK, s0, &full[i]);
             for (int i = pre; i < cnt; ++i) {
@@ -122,6 +152,7 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
             mbar_wait(&done, 0);
             tc::fence_after();
         }
+        if (threadIdx.x == 64) LIN_PROBE(2);
         griddep_launch();
         for (int c0 = 0; c0 < BN; c0 += 16) {
             float v[16];
@@ -131,6 +162,12 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            }
+            if (clus) {   // [BN tokens][128 outputs] over the first ring stages (every MMA has completed)
+                float *red = reinterpret_cast<float *>(sm);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) red[(c0 + j) * LN_BM + q * 32 + lane] = v[j];
+                continue;
             }
             if (o < O) {
 #pragma unroll
@@ -145,13 +182,16 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
             }
         }
         tc::fence_before();
-        if (BN == 16 && part && a.tile_cnt) {
+        if (BN == 16 && part && a.tile_cnt && !clus) {
             // split-K: the last split of this output tile to arrive adds the
             // partials in split order (the same sum as linear_reduce_kernel)
             __threadfence();
             asm volatile("bar.sync 2, 128;" ::: "memory");
             const int tile = blockIdx.x + gridDim.x * blockIdx.y;
-            if (threadIdx.x == 64) last_split = atomicAdd(&a.tile_cnt[tile], 1) == (int)gridDim.z - 1;
+            if (threadIdx.x == 64) {
+                LIN_PROBE(3);
+                last_split = atomicAdd(&a.tile_cnt[tile], 1) == (int)gridDim.z - 1;
+            }
             asm volatile("bar.sync 2, 128;" ::: "memory");
             if (last_split) {
                 __threadfence();
@@ -176,9 +216,43 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
                         else static_cast<float *>(yout)[idx] = acc[r];
                     }
                 }
-                if (threadIdx.x == 64) a.tile_cnt[tile] = 0;
+                if (threadIdx.x == 64) {
+                    a.tile_cnt[tile] = 0;
+                    LIN_PROBE(4);
+                }
             }
         }
+    }
+    if (clus) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();                                 // every split's partial in its shared memory
+        if (z == 0 && warp >= 2) {
+            const int q = warp & 3, ol = q * 32 + lane, o = o0 + ol;
+            if (threadIdx.x == 64) LIN_PROBE(3);
+            for (int c0 = 0; c0 < BN && o < O; c0 += 16) {   // 16 token rows at a time
+                const int rows = min(a.S - s0 - c0, 16);
+                if (rows <= 0) break;
+                float acc[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+                for (int zz = 0; zz < (int)gridDim.z; ++zz) {
+                    const float *pr = cl.map_shared_rank(reinterpret_cast<const float *>(sm), zz) + c0 * LN_BM + ol;
+#pragma unroll
+                    for (int r = 0; r < 16; ++r)
+                        if (r < rows) acc[r] += pr[r * LN_BM];
+                }
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    if (r >= rows) break;
+                    const size_t idx = (size_t)(s0 + c0 + r) * O + o;
+                    if (a.y_bf16) static_cast<__nv_bfloat16 *>(yout)[idx] = __float2bfloat16_rn(acc[r]);
+                    else static_cast<float *>(yout)[idx] = acc[r];
+                }
+            }
+            if (threadIdx.x == 64) LIN_PROBE(4);
+        }
+        cl.sync();                                 // the peers' shared memory stays until it has been read
     }
     __syncthreads();
     if (warp == 1) {
@@ -328,12 +402,17 @@ int linear_pick_bn(int S)
 }
 
 cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, LinearArgs a, int bn, int splits,
-                          cudaStream_t st)
+                          cudaStream_t st, int *launches)
 {
+    static_assert(64 * LN_BM * 4 <= 2 * LinSmem<64>::STAGE, "cluster partials fit the first two ring stages");
+    if (launches) *launches = 1;
     const int nk = (a.I + LN_BK - 1) / LN_BK;
     a.kchunks = (nk + splits - 1) / splits;
     splits = (nk + a.kchunks - 1) / a.kchunks;   // no split without K chunks
     if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
+    // clusters of up to 8 CTAs at two CTAs per SM (BN = 16); the larger tiles
+    // hold one CTA per SM, where 8-CTA clusters no longer fit one wave
+    a.cluster = bn <= 64 && splits > 1 && splits <= (bn == 16 ? LIN_MAX_CLUSTER : 4);
     dim3 grid((a.O + LN_BM - 1) / LN_BM, (a.S + bn - 1) / bn, splits);
     // the shared-memory opt-in, once per instantiation and device
     static bool attr_set[16][7] = {};
@@ -351,10 +430,15 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = grid; cfg.blockDim = dim3(192); cfg.dynamicSmemBytes = smem; cfg.stream = st;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr; cfg.numAttrs = 1;
+        if (a.cluster) {
+            attr[1].id = cudaLaunchAttributeClusterDimension;
+            attr[1].val.clusterDim.x = 1; attr[1].val.clusterDim.y = 1; attr[1].val.clusterDim.z = grid.z;
+            cfg.numAttrs = 2;
+        }
         return cudaLaunchKernelEx(&cfg, kern, wts, tmX, a);
     };
     cudaError_t e;
@@ -375,7 +459,8 @@ cudaError_t launch_linear(const CUtensorMap &tmW, const CUtensorMap &tmX, Linear
     case 256: e = run(linear_kernel<256>, LinSmem<256>::TOTAL, 4, lw); break;
     default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess || splits == 1 || (bn == 16 && a.tile_cnt)) return e;
+    if (e != cudaSuccess || splits == 1 || a.cluster || (bn == 16 && a.tile_cnt)) return e;
+    if (launches) *launches = 2;
     const size_t n = (size_t)a.S * a.O;
     linear_reduce_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(a, splits);
     return cudaGetLastError();
@@ -389,7 +474,8 @@ cudaError_t launch_linear_multi(const CUtensorMap *const *tmW, const int *O, voi
     a.kchunks = (nk + splits - 1) / splits;
     splits = (nk + a.kchunks - 1) / a.kchunks;
     if (splits == 1) { a.part = nullptr; a.tile_cnt = nullptr; }
-    if (splits > 1 && (!a.part || !a.tile_cnt)) return cudaErrorInvalidValue;
+    a.cluster = splits > 1 && splits <= LIN_MAX_CLUSTER;
+    if (splits > 1 && !a.cluster && (!a.part || !a.tile_cnt)) return cudaErrorInvalidValue;
     LinWeights lw;
     memset(&lw, 0, sizeof(lw));
     int tiles = 0;
@@ -413,10 +499,15 @@ cudaError_t launch_linear_multi(const CUtensorMap *const *tmW, const int *O, voi
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles, 1, splits); cfg.blockDim = dim3(192);
     cfg.dynamicSmemBytes = LinSmem<16>::TOTAL; cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr; cfg.numAttrs = 1;
+    if (a.cluster) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1; attr[1].val.clusterDim.y = 1; attr[1].val.clusterDim.z = splits;
+        cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelEx(&cfg, linear_kernel<16>, lw, tmX, a);
 }
 
