@@ -413,7 +413,7 @@ __device__ long long g_prep_probe[2 * 16];
 #else
 #define PREP_PROBE(slot) do { } while (0)
 #endif
-constexpr int PREP_THREADS = 256;
+constexpr int PREP_THREADS = 512;   // 16 warps: the SIMT phases of the chain run on twice the threads
 __global__ void __launch_bounds__(PREP_THREADS)
 gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKT,
@@ -526,19 +526,19 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     PREP_PROBE(4);
     tc::fence_after();
 
-    // this warp's 16 rows of K K^T (w < 4) or Q K^T (w >= 4), all 64 columns:
-    // the decay-masked A to shared memory, M to global
-    const int r0 = (warp & 3) * 16, second = warp >> 2;
+    // this warp's 16 rows of K K^T (w % 8 < 4) or Q K^T (w % 8 >= 4), 32 of
+    // the 64 columns (w / 8): the decay-masked A to shared memory, M to global
+    const int r0 = (warp & 3) * 16, second = (warp >> 2) & 1, ch = warp >> 3;
     {
-        float acc[32];
-        tc::ld16x256_x8(tbase + lane_off + (second ? 64u : 0u), acc);
+        float acc[16];
+        tc::ld16x256_x4(tbase + lane_off + (second ? 64u : 0u) + 32u * ch, acc);
         tc::wait_ld();
         float *Mg = p.M + ((size_t)n * p.VH + h) * PFG_C * PFG_C;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
-                const int i = r0 + g + 8 * hr, j = nt * 8 + 2 * tq;
+                const int i = r0 + g + 8 * hr, j = ch * 32 + nt * 8 + 2 * tq;
                 const float d0 = ex2_approx((G[i] - G[j]) * 1.4426950408889634f);
                 const float d1 = ex2_approx((G[i] - G[j + 1]) * 1.4426950408889634f);
                 const float v0 = acc[4 * nt + 2 * hr], v1 = acc[4 * nt + 2 * hr + 1];
@@ -553,10 +553,11 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     }
     // T = (I + A)^-1, A strictly lower triangular, by 16x16 blocks. The
-    // diagonal block of this warp's 16 A rows right away, by forward
-    // substitution (lane c < 16 = column c, kept in registers; two partial
-    // sums shorten the dependent chain), while warps 4-7 store M.
-    if (!second) {
+    // diagonal block of these 16 A rows right away, by the warp that wrote its
+    // columns, by forward substitution (lane c < 16 = column c, kept in
+    // registers; two partial sums shorten the dependent chain), while the
+    // Q K^T warps store M.
+    if (!second && ch == (r0 >> 5)) {
         __syncwarp();                              // this warp's A rows written
         if (lane < 16) {
             const int c = lane;
@@ -628,10 +629,10 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     PREP_PROBE(6);
     // T diag(beta gamma) and T diag(beta) as K-major tf32 A operands, over A and T
     {
-        const int i = tid >> 2, j0 = (tid & 3) * 16;
-        float t[16];
+        const int i = tid >> 3, j0 = (tid & 7) * 8;   // row i, columns j0 .. j0 + 7 (one 16-block)
+        float t[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
             const float4 v = (j0 >> 4) > (i >> 4) ? make_float4(0.f, 0.f, 0.f, 0.f)
                                                   : *reinterpret_cast<const float4 *>(sT + i * PREP_LD + j0 + 4 * q);
             t[4 * q] = v.x; t[4 * q + 1] = v.y; t[4 * q + 2] = v.z; t[4 * q + 3] = v.w;
@@ -639,7 +640,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         __syncthreads();
         uint8_t *aw = reinterpret_cast<uint8_t *>(sA), *au = reinterpret_cast<uint8_t *>(sT);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 2; ++q) {
             const int j = j0 + 4 * q;
             *reinterpret_cast<float4 *>(aw + kmaj_off(PFG_C, i, j)) =
                 make_float4(tf32r(t[4 * q] * bgam[j]), tf32r(t[4 * q + 1] * bgam[j + 1]),
@@ -673,10 +674,10 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     mbar_wait(&bar_mma, 0);   // third completion
     PREP_PROBE(8);
     tc::fence_after();
-    // this warp's 16 rows of W (w < 4) or U (w >= 4), 128 columns in two halves
+    // this warp's 16 rows of W (w % 8 < 4) or U (w % 8 >= 4), 64 of the 128 columns (w / 8)
     float *Og = (second ? p.U : p.W) + ((size_t)n * p.VH + h) * PFG_C * PFG_D;
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
+    {
+        const int half = ch;
         float w[32];
         tc::ld16x256_x8(tbase + lane_off + (second ? 128u : 0u) + 64 * half, w);
         tc::wait_ld();
