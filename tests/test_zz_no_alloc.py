@@ -70,6 +70,33 @@ def test_noalloc_matches_allocating_entry_on_two_calls(be):
                      what=f"noalloc call {call}")
 
 
+def test_noalloc_cuts_splits_to_fit_and_allocates_nothing(be):
+    """64 requests at T = 8192: the default plan (8 KV splits) needs ~16 MB of
+    partial sums, more than the fixed 8 MiB array, so the call runs with fewer
+    splits; its results equal the allocating entry's. The allocation-failure
+    hook is armed around the call (any device allocation would be refused and
+    the call would fail), and the backend's allocation total is unchanged."""
+    import torch
+    B, T = 64, 8192
+    g = _setup(be, torch, B, T, seed=5)
+    qg, k, v, pos = _inputs(torch, g, B, T)
+    want = torch.zeros(B, H, HD, dtype=torch.bfloat16, device="cuda")
+    got = torch.full((B, H, HD), float("nan"), dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    be.gqa_decode_dev(LAYER, B, qg.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), want.data_ptr())
+    be.sync()
+    before = be.mem_info()
+    be.lib.coli_cuda_debug_fail_alloc(0)
+    try:
+        be.gqa_decode_noalloc(LAYER, B, qg.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(),
+                              got.data_ptr())
+        be.sync()
+    finally:
+        be.lib.coli_cuda_debug_fail_alloc(-1)
+    assert be.mem_info() == before
+    assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(), what="noalloc with fewer splits")
+
+
 def test_noalloc_rejects_batch_beyond_fixed_scratch(be):
     import torch
     BackendError = load_pkg().BackendError
