@@ -748,6 +748,32 @@ def run_linear(be, args, st, peak_hbm):
                                    "frac_of_bf16": 2.0 * S * O * I / us / 1e6 / peak_tc}
         for t in ts:
             t.free()
+    # a decode step's input projections as the block calls issue them: one
+    # launch for all weights of the layer (q|gate, k, v; qkv, z, a, b)
+    for name, Os in {"gqa_in_S1_multi": (8192, 512, 512), "gdn_in_S1_multi": (8192, 4096, 32, 32)}.items():
+        I = 2048
+        sets = [[pkg.coli_cuda.DenseTensor(be, rng.standard_normal((O, I), dtype=np.float32) * 0.02) for O in Os]
+                for _ in range(6)]
+        x = torch.randn(1, I, device="cuda").bfloat16()
+        ys = [torch.empty(1, O, device="cuda", dtype=torch.bfloat16) for O in Os]
+        yp = [y.data_ptr() for y in ys]
+        for i in range(6):
+            be.matmul_multi_dev(sets[i], x.data_ptr(), 1, yp, 1)
+        reps = 30
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        be.sync()
+        e0.record(st)
+        for i in range(reps):
+            be.matmul_multi_dev(sets[i % 6], x.data_ptr(), 1, yp, 1)
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        wbytes = sum(O * I * 2 + (I + O) * 2 for O in Os)
+        out[name] = {"O": list(Os), "I": I, "S": 1, "us": us, "GBs": wbytes / us / 1e3,
+                     "frac_of_hbm": wbytes / us / 1e3 / peak_hbm}
+        for ts in sets:
+            for t in ts:
+                t.free()
     return {"linear": out}
 
 

@@ -275,6 +275,14 @@ int  coli_cuda_matmul(ColiCudaTensor **tensor, float *y, const float *x, const v
  * (y_bf16 = 0) or bf16 (1), asynchronous on the backend stream. */
 int  coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, void *y, int y_bf16);
 
+/* Up to 4 projections of the same x in one launch when S <= 16 (the output
+ * tiles of all weights share the grid and the split-K plan; a decode step's
+ * q|gate / k / v, or qkv / z / a / b, as the block calls issue them); larger
+ * S runs them one by one. Same argument rules as coli_cuda_matmul_dev; the
+ * weights need the same input width. */
+int  coli_cuda_matmul_multi_dev(const ColiCudaTensor *const *tensors, int n, const void *x, int S,
+                                void *const *y, int y_bf16);
+
 /* Attention + resident o_proj in one call, ctx staying on the device:
  * coli_vk_gqa_project (c/backend_vulkan.h:165-170; called at c/qwen.c:623).
  * Same q / cache contract as coli_cuda_gqa; out [S][Dout] fp32 host. */

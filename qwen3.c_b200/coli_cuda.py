@@ -85,6 +85,7 @@ SIGNATURES = {
     "coli_cuda_tensor_bytes": ([_vp], ctypes.c_size_t),
     "coli_cuda_matmul": ([ctypes.POINTER(_vp), _fp, _fp, _vp, _fp] + [_i] * 5, _i),
     "coli_cuda_matmul_dev": ([_vp, _vp, _i, _vp, _i], _i),
+    "coli_cuda_matmul_multi_dev": ([ctypes.POINTER(_vp), _i, _vp, _i, ctypes.POINTER(_vp), _i], _i),
     "coli_cuda_gqa_project": ([_i, _fp, _vp, _fp] + [_i] * 7 + [_f, _i], _i),
     "coli_cuda_gdn_project": ([_i] + [_fp] * 7 + [_vp, _fp] + [_i] * 4 + [_f, _i], _i),
     "coli_cuda_gqa_full": ([_i, _fp, _i, _vp, _vp, _vp, _vp, _fp] + [_i] * 7 + [_f, _f, _i], _i),
@@ -456,6 +457,13 @@ def _block_methods():
         self._ok(rc, "gdn_full")
         return out
 
+    def matmul_multi_dev(self, tensors, x, S, ys, y_bf16=0):
+        """Device pointers: x bf16 [S][I], ys[i] [S][O_i]; one launch for S <= 16."""
+        n = len(tensors)
+        th = (_vp * n)(*[t.h for t in tensors])
+        yh = (_vp * n)(*ys)
+        self._ok(self.lib.coli_cuda_matmul_multi_dev(th, n, x, S, yh, y_bf16), "matmul_multi_dev")
+
     def gdn_full_ab(self, layer, x, gqkv, gz, ga, gb, gout, KH=16, KD=128, VH=32, VD=128, eps=1e-6):
         """S tokens with the a / b projections on the device (no params rows)."""
         x, xp = _f32(x)
@@ -504,8 +512,8 @@ def _block_methods():
                                                    router.O), "gdn_full_route")
         return ro, nr, pr
 
-    for f in (matmul, matmul_dev, gqa_full, gdn_full_seq, gdn_full_ab, layer_norm_weight, gqa_full_route,
-              gdn_full_route):
+    for f in (matmul, matmul_dev, matmul_multi_dev, gqa_full, gdn_full_seq, gdn_full_ab, layer_norm_weight,
+              gqa_full_route, gdn_full_route):
         setattr(Backend, f.__name__, f)
 
 

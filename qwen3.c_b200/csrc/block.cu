@@ -33,9 +33,19 @@ int make_bf16_2d(CUtensorMap *m, const void *base, int inner, int outer, int box
 }
 
 // y[S][O] = x[S][I] W^T on the device (x bf16, y fp32 or bf16).
-#ifndef LIN_CTA_MULT
-#define LIN_CTA_MULT 1      // split-K targets this many CTAs per SM for decode
-#endif
+// K splits of a projection whose output tiles cannot fill the GPU: the
+// 16-token decode kernel holds two CTAs per SM, so it targets 7/8 of two per
+// SM (clusters placed near the full count spilled into a second wave), at
+// most 8 splits (one thread-block cluster reduces them); the larger tiles hold
+// one CTA per SM.
+int linear_splits(int tiles, int nk, int bn)
+{
+    const int slots = bn == 16 ? 2 * G.num_sms * 7 / 8 : G.num_sms;
+    if (2 * tiles > slots) return 1;
+    int s = std::max(1, std::min(slots / tiles, nk / 4));
+    if (bn == 16) s = std::min(s, 8);
+    return s;
+}
 int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, int y_bf16)
 {
     if (!t || !t->w) return fail("dense tensor not uploaded");
@@ -43,8 +53,7 @@ int linear_dev(const ColiCudaTensor *t, const __nv_bfloat16 *x, int S, void *y, 
     CUtensorMap tx;
     if (!make_bf16_2d(&tx, x, t->I, S, 64, bn)) return 0;
     const int tiles = ((t->O + 127) / 128) * ((S + bn - 1) / bn), nk = (t->I + 63) / 64;
-    int splits = 1;
-    if (2 * tiles <= LIN_CTA_MULT * G.num_sms) splits = std::max(1, std::min(LIN_CTA_MULT * G.num_sms / tiles, nk / 4));
+    const int splits = linear_splits(tiles, nk, bn);
     LinearArgs la;
     memset(&la, 0, sizeof(la));
     la.y = y; la.S = S; la.I = t->I; la.O = t->O; la.y_bf16 = y_bf16;
@@ -88,8 +97,7 @@ int linear_dev_multi(const ColiCudaTensor *const *t, int nw, const __nv_bfloat16
     CUtensorMap tx;
     if (!make_bf16_2d(&tx, x, t[0]->I, S, 64, 16)) return 0;
     const int nk = (t[0]->I + 63) / 64;
-    int splits = 1;
-    if (2 * tiles <= LIN_CTA_MULT * G.num_sms) splits = std::max(1, std::min(LIN_CTA_MULT * G.num_sms / tiles, nk / 4));
+    const int splits = linear_splits(tiles, nk, 16);
     LinearArgs la;
     memset(&la, 0, sizeof(la));
     la.S = S; la.I = t[0]->I; la.O = Osum; la.y_bf16 = y_bf16;
@@ -197,6 +205,17 @@ int coli_cuda_matmul_dev(const ColiCudaTensor *tensor, const void *x, int S, voi
     if (S < 1 || !x || !y) return fail("bad matmul_dev arguments");
     if (reinterpret_cast<uintptr_t>(x) & 15) return fail("x must be 16-byte aligned");
     return linear_dev(tensor, static_cast<const __nv_bfloat16 *>(x), S, y, y_bf16);
+}
+
+int coli_cuda_matmul_multi_dev(const ColiCudaTensor *const *tensors, int n, const void *x, int S,
+                               void *const *y, int y_bf16)
+{
+    READY();
+    if (n < 1 || n > LIN_MAXW || S < 1 || !tensors || !x || !y) return fail("bad matmul_multi_dev arguments");
+    if (reinterpret_cast<uintptr_t>(x) & 15) return fail("x must be 16-byte aligned");
+    for (int i = 0; i < n; ++i)
+        if (!y[i]) return fail("matmul_multi_dev: output %d missing", i);
+    return linear_dev_multi(tensors, n, static_cast<const __nv_bfloat16 *>(x), S, y, y_bf16);
 }
 
 }  // extern "C"

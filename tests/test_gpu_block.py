@@ -51,6 +51,30 @@ def test_linear_vs_bf16_product(be, S):
     t.free()
 
 
+@pytest.mark.parametrize("S", [1, 5, 16, 20])
+def test_linear_multi_launch_vs_bf16_product(be, S):
+    """coli_cuda_matmul_multi_dev: four projections of one x (output widths
+    1000, 512, 32, 32: not multiples of the tile, two of them smaller than
+    one tile) in one launch for S <= 16 (shared grid, split-K across a
+    cluster), one by one above; against the bf16-operand product."""
+    import torch
+    Os = (1000, 512, 32, 32)
+    Ws = [_w("linm", f"W{i}", O, D) for i, O in enumerate(Os)]
+    x = synth.normal(synth.seed_of("linm", "x", S), (S, D))
+    ts = [_dense(be, W) for W in Ws]
+    xd = torch.from_numpy(synth.bf16_round(x)).cuda().bfloat16()
+    ys = [torch.full((S, O), float("nan"), device="cuda") for O in Os]
+    torch.cuda.synchronize()
+    be.matmul_multi_dev(ts, xd.data_ptr(), S, [y.data_ptr() for y in ys], 0)
+    be.sync()
+    for W, y, O in zip(Ws, ys, Os):
+        ref = synth.bf16_round(x).astype(np.float64) @ synth.bf16_round(W).astype(np.float64).T
+        err = np.max(np.abs(y.cpu().numpy() - ref))
+        assert err <= 1e-4 * np.max(np.abs(ref)) + 1e-6, (O, err)
+    for t in ts:
+        t.free()
+
+
 def test_linear_int8_rows(be):
     rng = np.random.default_rng(5)
     q = rng.integers(-127, 128, size=(384, D), dtype=np.int8)
