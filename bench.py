@@ -644,21 +644,22 @@ def run_gdn_prefill_secondary(be, args, st, peak_hbm):
         for _ in range(2):
             step()
         be.sync()
-        reps = 5
+        reps = 10 if S <= 8192 else 5
         be.ktimer_enable(True)
         be.ktimer_read(be.K_GDN_PREFILL)
-        tot = 0.0
+        # back-to-back calls in one event pair (the state carried from call to
+        # call, as consecutive prompts or layers would): single calls after
+        # an idle gap measured 5-10 % apart from run to run on this pool
+        be.gdn_reset()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
         for _ in range(reps):
-            be.gdn_reset()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
             call()
-            e1.record(st)
-            torch.cuda.synchronize()
-            tot += e0.elapsed_time(e1)
+        e1.record(st)
+        torch.cuda.synchronize()
         be.ktimer_enable(False)
         be.ktimer_read(be.K_GDN_PREFILL)
-        ms = tot / reps
+        ms = e0.elapsed_time(e1) / reps
         bytes_ = (S * 32896 + 2 * 1024 * 1024) * nkh // KHg
         out[f"gdn_prefill_{S}" + (f"_kheads{nkh}" if nkh != KHg else "")] = {
             "metric": "GDN chunked prefill tok/s (one layer)", "S": S, "k_heads": nkh,
