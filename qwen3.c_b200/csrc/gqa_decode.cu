@@ -469,26 +469,58 @@ gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant_
 }
 
 // ------------------------------------------------------------------ combine
+// One CTA per (request, query head), 256 threads. Warp w merges the splits
+// w, w + 8, .. with a running maximum (lane = 8 head dims, all of a warp's
+// loads independent of each other), then thread d merges the 8 warp partials
+// of dim d from shared memory: the loads of one request's splits are spread
+// over the warps instead of two serial passes of every thread over all splits
+// (a single request at 32k context has 74 splits).
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(GQA_HD)
 gqa_combine_kernel(GqaCombineArgs p)
 {
+    constexpr int CW = GQA_HD / 32;      // warps
+    __shared__ float sm_ml[CW][2];
+    __shared__ __align__(16) float sm_o[CW][GQA_HD];
     griddep_wait();      // launched as a programmatic dependent of the split kernel
-    const int n = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int n = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kh = h / GQA_GRP, hl = h % GQA_GRP;
     const size_t base = ((size_t)n * p.KH + kh) * p.n_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, p.part_ml[((base + s) * GQA_GRP + hl) * 2]);
-    float o = 0.f, L = 0.f;
-    for (int s = 0; s < p.n_splits; ++s) {
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.f;
+#pragma unroll 2
+    for (int s = warp; s < p.n_splits; s += CW) {
         const size_t pi = (base + s) * GQA_GRP + hl;
-        const float ms = p.part_ml[pi * 2];
-        const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
-        o += p.part_o[pi * GQA_HD + d] * f;
-        L += p.part_ml[pi * 2 + 1] * f;
+        const float2 ml = *reinterpret_cast<const float2 *>(p.part_ml + pi * 2);
+        const float4 a = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane);
+        const float4 b = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane + 4);
+        if (ml.x == -INFINITY) continue;                     // a split with no keys for this row
+        const float mn = fmaxf(m, ml.x);
+        const float fo = m == -INFINITY ? 0.f : exp2f(m - mn), fs = exp2f(ml.x - mn);
+        const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = o[i] * fo + x[i] * fs;
+        l = l * fo + ml.y * fs;
+        m = mn;
     }
-    const float gate = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * p.H + h) * 2 * GQA_HD + GQA_HD + d]);
-    static_cast<TO *>(p.ctx)[((size_t)n * p.H + h) * GQA_HD + d] = from_f32<TO>(o / L * sigmoidf_(gate));
+    if (lane == 0) { sm_ml[warp][0] = m; sm_ml[warp][1] = l; }
+    *reinterpret_cast<float4 *>(&sm_o[warp][8 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4 *>(&sm_o[warp][8 * lane + 4]) = make_float4(o[4], o[5], o[6], o[7]);
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) M = fmaxf(M, sm_ml[w][0]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) {
+        const float mw = sm_ml[w][0];
+        const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+        O += sm_o[w][tid] * f;
+        L += sm_ml[w][1] * f;
+    }
+    const float gate = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * p.H + h) * 2 * GQA_HD + GQA_HD + tid]);
+    static_cast<TO *>(p.ctx)[((size_t)n * p.H + h) * GQA_HD + tid] = from_f32<TO>(O / L * sigmoidf_(gate));
 }
 
 // ------------------------------------------------------------------ launch
