@@ -489,20 +489,32 @@ gqa_combine_kernel(GqaCombineArgs p)
     float m = -INFINITY, l = 0.f, o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = 0.f;
-#pragma unroll 2
-    for (int s = warp; s < p.n_splits; s += CW) {
-        const size_t pi = (base + s) * GQA_GRP + hl;
-        const float2 ml = *reinterpret_cast<const float2 *>(p.part_ml + pi * 2);
-        const float4 a = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane);
-        const float4 b = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane + 4);
-        if (ml.x == -INFINITY) continue;                     // a split with no keys for this row
-        const float mn = fmaxf(m, ml.x);
-        const float fo = m == -INFINITY ? 0.f : exp2f(m - mn), fs = exp2f(ml.x - mn);
-        const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    constexpr int CU = 4;                // splits whose loads a warp issues together
+    for (int s0 = warp; s0 < p.n_splits; s0 += CU * CW) {
+        float2 ml[CU];
+        float4 a[CU], b[CU];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = o[i] * fo + x[i] * fs;
-        l = l * fo + ml.y * fs;
-        m = mn;
+        for (int u = 0; u < CU; ++u) {
+            const int s = s0 + u * CW;
+            ml[u] = make_float2(-INFINITY, 0.f);
+            if (s < p.n_splits) {
+                const size_t pi = (base + s) * GQA_GRP + hl;
+                ml[u] = *reinterpret_cast<const float2 *>(p.part_ml + pi * 2);
+                a[u] = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane);
+                b[u] = *reinterpret_cast<const float4 *>(p.part_o + pi * GQA_HD + 8 * lane + 4);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+            if (ml[u].x == -INFINITY) continue;             // no keys for this row (or past the last split)
+            const float mn = fmaxf(m, ml[u].x);
+            const float fo = m == -INFINITY ? 0.f : exp2f(m - mn), fs = exp2f(ml[u].x - mn);
+            const float x[8] = {a[u].x, a[u].y, a[u].z, a[u].w, b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = o[i] * fo + x[i] * fs;
+            l = l * fo + ml[u].y * fs;
+            m = mn;
+        }
     }
     if (lane == 0) { sm_ml[warp][0] = m; sm_ml[warp][1] = l; }
     *reinterpret_cast<float4 *>(&sm_o[warp][8 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
