@@ -604,7 +604,10 @@ int gqa_pick_splits(int nq, int KH, int tmax, int num_sms)
     double best_eff = -1.0;
     for (int s = 1; s <= 256; ++s) {
         const int per = (tiles + s - 1) / s;        // tiles per CTA
-        if (s > 1 && per < 2 * SPLIT_WARPS) break;  // keep every warp busy for >= 2 tiles
+        // keep every warp busy for >= 2 tiles, or >= 1 while the grid is far
+        // below one wave (a single request at short context: latency bound)
+        const bool small = (long)nq * KH * s * 2 <= num_sms;
+        if (s > 1 && per < (small ? SPLIT_WARPS : 2 * SPLIT_WARPS)) break;
         const long ctas = (long)nq * KH * s;
         const long waves = (ctas + num_sms - 1) / num_sms;
         // wave-quantisation efficiency, with a mild preference for fewer splits
