@@ -27,9 +27,6 @@ namespace coli {
 #ifndef LIN_DEC_STAGES
 #define LIN_DEC_STAGES 6    // ring stages of the decode (BN = 16) kernel: two CTAs fit an SM
 #endif
-#ifndef LIN_EARLY
-#define LIN_EARLY 0         // 1: let the next programmatic launch start as soon as this grid is resident (measured: no gain)
-#endif
 #ifndef LIN_MAX_CLUSTER
 #define LIN_MAX_CLUSTER 8   // most K splits reduced in a cluster (portable cluster size)
 #endif
@@ -101,7 +98,6 @@ linear_kernel(const __grid_constant__ LinWeights lw, const __grid_constant__ CUt
     __syncthreads();
     tc::fence_after();
     const uint32_t tD = tmem_base;
-    if (LIN_EARLY) griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
