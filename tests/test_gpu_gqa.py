@@ -74,7 +74,9 @@ def test_golden_reference_long_context(be):
     assert_close(ctx, g["ctx"], what="decode at T=4096")
 
 
-@pytest.mark.parametrize("B,tmax", [(1, 1), (3, 17), (16, 5000), (4, 32768)])
+# (1, 4096): a grid far below one wave (one tile per warp); (1, 32768): 74
+# KV splits merged by the combine's warps four at a time
+@pytest.mark.parametrize("B,tmax", [(1, 1), (3, 17), (16, 5000), (4, 32768), (1, 4096), (1, 32768)])
 def test_batched_decode_vs_oracle(be, orc, B, tmax):
     cfg = f"gqa_b{B}_t{tmax}"
     rng = np.random.default_rng(B * 7919 + tmax)
