@@ -421,8 +421,11 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 {
     extern __shared__ uint8_t smem_raw[];
     float *base = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *sQV = base;                          // Q chunk [64 x 128], later V^T [128 x 64] swizzled
-    float *sK = sQV + PFG_C * PFG_D;            // K chunk, later K^T [128 x 64] swizzled
+    // [K; Q] of the chunk: 4 k-atoms of 128 rows (K rows 0-63, Q rows 64-127),
+    // 128B-swizzled; later V^T | K^T [128 x 64] swizzled
+    float *sKQ = base;
+    float *sQV = base;                          // V^T, after the products
+    float *sK = base + PFG_C * PFG_D;           // K^T, after the products
     float *sA = sK + PFG_C * PFG_D;             // [64][68] strictly lower A; later T diag(beta gamma), K-major
     float *sT = sA + PFG_C * PREP_LD;           // [64][68] T = (I + A)^-1; later T diag(beta), K-major
     float *sX = sT + PFG_C * PREP_LD;           // [3][16][16] block products
@@ -448,8 +451,8 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (tid == 0) {
         mbar_expect_tx(&bar_qk, 2 * PFG_C * PFG_D * 4);
         for (int c = 0; c < 4; ++c) {
-            tma_load_3d(sQV + c * PFG_C * 32, &tmQ, 32 * c, s0, kh, &bar_qk);
-            tma_load_3d(sK + c * PFG_C * 32, &tmK, 32 * c, s0, kh, &bar_qk);
+            tma_load_3d(sKQ + c * 2 * PFG_C * 32, &tmK, 32 * c, s0, kh, &bar_qk);
+            tma_load_3d(sKQ + c * 2 * PFG_C * 32 + PFG_C * 32, &tmQ, 32 * c, s0, kh, &bar_qk);
         }
     }
     if (warp == 0) {
@@ -465,60 +468,60 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // three tf32 products, hi.hi + lo.hi + hi.lo (the split-tf32 scheme; a
     // product of plain tf32 roundings misses the output tolerance there);
     // K K^T, which enters the T solve, likewise. The tensor core reads the
-    // tf32 truncation of an fp32 operand, so the Q and K tiles serve as the
-    // hi parts as they are (hi = x with the 13 low mantissa bits cleared) and
-    // lo = x - hi is exact in fp32: only the lo tiles are written, first Q_lo,
-    // then K_lo over it, in the A / T area (free until these products complete).
-    float *sLo = sA;                            // [64 x 128] swizzled like sQV / sK (32 KiB over sA, sT)
+    // tf32 truncation of an fp32 operand, so the K and Q rows serve as the hi
+    // parts as they are (hi = x with the 13 low mantissa bits cleared) and
+    // lo = x - hi is exact in fp32: only the lo tiles are written, K_lo then
+    // Q_lo, in the A / T area (free until these products complete). Both
+    // products come out of K [K; Q]^T (M = 64, N = 128: K K^T in TMEM columns
+    // 0-63, K Q^T = (Q K^T)^T in 64-127), which takes a third fewer MMA
+    // issues than separate N = 64 products:
+    //   K_h [K_h; Q_h]^T + K_l [K_h; Q_h]^T + K_h K_l^T (cols 0-63) + K_h Q_l^T (cols 64-127)
+    float *sLo = sA;                            // [64 x 128] in 4 k-atoms of 64 rows (32 KiB over sA, sT)
     auto lo_of = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
+    // lo of the K (part 0) or Q (part 1) rows of the [K; Q] atoms into sLo
+    auto lo_pass = [&](int part) {
+        for (int i = tid; i < PFG_C * PFG_D / 4; i += PREP_THREADS) {
+            const int atom = i >> 9, o = i & 511;          // 512 float4 per 64-row atom
+            const float4 x = reinterpret_cast<const float4 *>(sKQ)[atom * 1024 + part * 512 + o];
+            reinterpret_cast<float4 *>(sLo)[i] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+        }
+    };
     PREP_PROBE(0);
     mbar_wait(&bar_qk, 0);
     PREP_PROBE(1);
-    for (int i = tid; i < PFG_C * PFG_D / 4; i += PREP_THREADS) {
-        const float4 q = reinterpret_cast<const float4 *>(sQV)[i];
-        reinterpret_cast<float4 *>(sLo)[i] = make_float4(lo_of(q.x), lo_of(q.y), lo_of(q.z), lo_of(q.w));
-    }
+    lo_pass(0);
     fence_proxy_async();                        // generic-proxy writes visible to the tensor core
     tc::fence_before();
     __syncthreads();
-    constexpr uint32_t IDP = tc::idesc_tf32(64, 64);
-    const uint32_t aK = smem_u32(sK), aQ = smem_u32(sQV), aLo = smem_u32(sLo);
+    constexpr uint32_t IDP64 = tc::idesc_tf32(64, 64), IDP128 = tc::idesc_tf32(64, 128);
+    const uint32_t aKQ = smem_u32(sKQ), aLo = smem_u32(sLo);
     if (tid == 0) {
-        // K K^T -> columns 0..63, Q K^T -> 64..127: hi.hi, then Q_lo.K_hi
         tc::fence_after();
 #pragma unroll
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
-            tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aK + off), IDP, ks > 0);
-            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aK + off), IDP, ks > 0);
-        }
-#pragma unroll
-        for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
-            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aLo + off), tc::desc_k_sw128(aK + off), IDP, 1);
+            const uint32_t okq = (ks >> 2) * (2 * PFG_C * 128) + (ks & 3) * 32;   // K rows / [K; Q] rows
+            const uint32_t olo = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aKQ + okq), tc::desc_k_sw128(aKQ + okq), IDP128, ks > 0);
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aLo + olo), tc::desc_k_sw128(aKQ + okq), IDP128, 1);
+            tc::mma_tf32(tbase, tc::desc_k_sw128(aKQ + okq), tc::desc_k_sw128(aLo + olo), IDP64, 1);
         }
         tc::commit(&bar_mma);
     }
     PREP_PROBE(2);
-    mbar_wait(&bar_mma, 0);                     // Q_lo has been read: K_lo over it
+    mbar_wait(&bar_mma, 0);                     // K_lo has been read: Q_lo over it
     tc::fence_after();
     PREP_PROBE(3);
-    for (int i = tid; i < PFG_C * PFG_D / 4; i += PREP_THREADS) {
-        const float4 k = reinterpret_cast<const float4 *>(sK)[i];
-        reinterpret_cast<float4 *>(sLo)[i] = make_float4(lo_of(k.x), lo_of(k.y), lo_of(k.z), lo_of(k.w));
-    }
+    lo_pass(1);
     fence_proxy_async();
     tc::fence_before();
     __syncthreads();
     if (tid == 0) {
-        // Q_hi.K_lo; K_hi.K_lo + K_lo.K_hi
         tc::fence_after();
 #pragma unroll
         for (int ks = 0; ks < PFG_D / 8; ++ks) {
-            const uint32_t off = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
-            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aLo + off), IDP, 1);
-            tc::mma_tf32(tbase, tc::desc_k_sw128(aK + off), tc::desc_k_sw128(aLo + off), IDP, 1);
-            tc::mma_tf32(tbase, tc::desc_k_sw128(aLo + off), tc::desc_k_sw128(aK + off), IDP, 1);
+            const uint32_t okq = (ks >> 2) * (2 * PFG_C * 128) + (ks & 3) * 32;
+            const uint32_t olo = (ks >> 2) * (PFG_C * 128) + (ks & 3) * 32;
+            tc::mma_tf32(tbase + 64, tc::desc_k_sw128(aKQ + okq), tc::desc_k_sw128(aLo + olo), IDP64, 1);
         }
         tc::commit(&bar_mma);
     }
@@ -526,7 +529,7 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     PREP_PROBE(4);
     tc::fence_after();
 
-    // this warp's 16 rows of K K^T (w % 8 < 4) or Q K^T (w % 8 >= 4), 32 of
+    // this warp's 16 rows of K K^T (w % 8 < 4) or K Q^T (w % 8 >= 4), 32 of
     // the 64 columns (w / 8): the decay-masked A to shared memory, M to global
     const int r0 = (warp & 3) * 16, second = (warp >> 2) & 1, ch = warp >> 3;
     {
@@ -539,13 +542,17 @@ gdn_pf_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
             for (int hr = 0; hr < 2; ++hr) {
                 const int i = r0 + g + 8 * hr, j = ch * 32 + nt * 8 + 2 * tq;
-                const float d0 = ex2_approx((G[i] - G[j]) * 1.4426950408889634f);
-                const float d1 = ex2_approx((G[i] - G[j + 1]) * 1.4426950408889634f);
                 const float v0 = acc[4 * nt + 2 * hr], v1 = acc[4 * nt + 2 * hr + 1];
                 if (second) {
-                    *reinterpret_cast<float2 *>(Mg + i * PFG_C + j) =
-                        make_float2(j <= i ? d0 * v0 : 0.f, j + 1 <= i ? d1 * v1 : 0.f);
+                    // K Q^T: row = key token i, column = query token j, so
+                    // M[j][i] = e^{G_j - G_i} q_j.k_i for i <= j
+                    const float e0 = ex2_approx((G[j] - G[i]) * 1.4426950408889634f);
+                    const float e1 = ex2_approx((G[j + 1] - G[i]) * 1.4426950408889634f);
+                    Mg[j * PFG_C + i] = i <= j ? e0 * v0 : 0.f;
+                    Mg[(j + 1) * PFG_C + i] = i <= j + 1 ? e1 * v1 : 0.f;
                 } else {
+                    const float d0 = ex2_approx((G[i] - G[j]) * 1.4426950408889634f);
+                    const float d1 = ex2_approx((G[i] - G[j + 1]) * 1.4426950408889634f);
                     sA[i * PREP_LD + j] = j < i ? bet[i] * d0 * v0 : 0.f;
                     sA[i * PREP_LD + j + 1] = j + 1 < i ? bet[i] * d1 * v1 : 0.f;
                 }
