@@ -268,8 +268,12 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
              : lc < 2 * PFG_D ? key_dim + kg * PFG_D + (lc - PFG_D)
                               : 2 * key_dim + 2 * kg * PFG_D + (lc - 2 * PFG_D);
     };
-    {   // the tile: 64 rows x 64 16-byte pieces, all loads in flight before any store
+    {   // the tile (64 rows x 64 16-byte pieces), the 3 halo rows and the conv
+        // taps: every load in flight before the first store, so the CTA waits
+        // on global memory once
         uint4 v[16];
+        float hv[3 * PRT_CH / 256];
+        float4 wv[PRT_CH / 256];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const int e = tid + 256 * i, row = e >> 6, lc = (e & 63) * 8;
@@ -277,16 +281,29 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
                               : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
+        for (int i = 0; i < 3 * PRT_CH / 256; ++i) {
+            const int e = tid + 256 * i, j = e / PRT_CH, lc = e - j * PRT_CH, ts = s_begin - 3 + j;
+            hv[i] = ts >= 0 ? __bfloat162float(x[(size_t)ts * CD + gch(lc)]) : p.hist[(size_t)j * CD + gch(lc)];
+        }
+#pragma unroll
+        for (int i = 0; i < PRT_CH / 256; ++i)
+            wv[i] = *reinterpret_cast<const float4 *>(p.conv_w + (size_t)gch(tid + 256 * i) * 4);
+        // the decay / beta gates of the chunk's 64 tokens x 2 V heads, one per
+        // thread (their loads overlap the tile's instead of stalling a warp
+        // once per token inside the token loop)
+        if (tid < 2 * PRO_T && (tid >> 1) < nrow)
+            gdn_gates(p, s_begin + (tid >> 1), kh * 2 + (tid & 1), kg * 2 + (tid & 1), VHin,
+                      static_cast<const __nv_bfloat16 *>(p.a), static_cast<const __nv_bfloat16 *>(p.b));
+#pragma unroll
         for (int i = 0; i < 16; ++i) {
             const int e = tid + 256 * i, row = e >> 6, lc = (e & 63) * 8;
             *reinterpret_cast<uint4 *>(sX + row * PRT_CH + lc) = v[i];
         }
+#pragma unroll
+        for (int i = 0; i < 3 * PRT_CH / 256; ++i) sHalo[tid + 256 * i] = hv[i];
+#pragma unroll
+        for (int i = 0; i < PRT_CH / 256; ++i) sW[tid + 256 * i] = wv[i];
     }
-    for (int e = tid; e < 3 * PRT_CH; e += 256) {
-        const int j = e / PRT_CH, lc = e - j * PRT_CH, ts = s_begin - 3 + j;
-        sHalo[e] = ts >= 0 ? __bfloat162float(x[(size_t)ts * CD + gch(lc)]) : p.hist[(size_t)j * CD + gch(lc)];
-    }
-    for (int lc = tid; lc < PRT_CH; lc += 256) sW[lc] = *reinterpret_cast<const float4 *>(p.conv_w + (size_t)gch(lc) * 4);
     __syncthreads();
 
     const int r0 = warp * (PRO_T / 8);
@@ -336,9 +353,6 @@ gdn_pf_prologue_tile_kernel(GdnPrefillArgs p)
         float *vrow = reinterpret_cast<float *>(sX + r * PRT_CH);
 #pragma unroll
         for (int j = 0; j < 8; ++j) vrow[(j * 32 + lane) ^ (r & 31)] = out[8 + j];
-        if (lane < 2)   // local / input-layout V head
-            gdn_gates(p, s, kh * 2 + lane, kg * 2 + lane, VHin, static_cast<const __nv_bfloat16 *>(p.a),
-                      static_cast<const __nv_bfloat16 *>(p.b));
     }
     __syncthreads();
     // K^T of the chunk ([dk][64 tokens], tokens past S zero), row-contiguous
