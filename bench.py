@@ -264,7 +264,8 @@ def run_ours(args, ws, rank, local):
     if args.only:  # one secondary leg alone (profiling runs)
         fn = {"gdn": run_gdn_secondary, "prefill": run_prefill_secondary,
               "gdnprefill": run_gdn_prefill_secondary, "stack": run_stack_decode,
-              "stackprefill": run_stack_prefill, "linear": run_linear}[args.only]
+              "stackprefill": run_stack_prefill, "linear": run_linear,
+              "gqagrid": run_gqa_grid, "gdngrid": run_gdn_grid}[args.only]
         res = fn(be, args, st, peak_tc if args.only in ("prefill", "stackprefill") else peak_hbm)
         if rank == 0:
             print(json.dumps(res))
@@ -486,6 +487,44 @@ def _time(st, fn, n):
     return e0.elapsed_time(e1) / n
 
 
+def _time_graph(st, fn, n, reps=3):
+    """Device time per call of fn with the n calls captured in one CUDA graph
+    and the graph replayed: at a few microseconds per step a Python loop of
+    library calls measures the host, not the GPU (a serving loop replays
+    its decode step as a graph for the same reason). None when the capture
+    fails; the caller then keeps the eager figure."""
+    import torch
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st, capture_error_mode="thread_local"):
+            for _ in range(n):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * n)
+        del g
+        return ms
+    except Exception as e:   # noqa: BLE001 -- reported, the eager number stands
+        print(f"graph capture failed: {type(e).__name__}: {e}", file=sys.stderr)
+        torch.cuda.synchronize()
+        return None
+
+
+def _graph_entry(st, fn, n, ms_eager):
+    """ms per step (graph replay where it captured, else eager) and the
+    fields that say which."""
+    ms_g = _time_graph(st, fn, n)
+    if ms_g is None:
+        return ms_eager, {"timing": "eager launches (graph capture failed)"}
+    return ms_g, {"timing": f"CUDA graph of {n} steps, replayed", "ms_per_step_eager": ms_eager}
+
+
 def run_gqa_grid(be, args, st, peak_hbm):
     """BASELINE config 2's grid: GQA decode at batch {1, 16, 64} x context
     {4096, 32768} (one layer, bf16 cache; the headline is the 64 x 32768 point)."""
@@ -515,13 +554,14 @@ def run_gqa_grid(be, args, st, peak_hbm):
                 step()
             be.sync()
             n = 50 if B * T >= 64 * 4096 else 200
-            ms = _time(st, step, n)
+            ms, how = _graph_entry(st, step, n, _time(st, step, n))
             bytes_ = B * (2048 * T + 2048 + 16384 + 8192)
             out[f"gqa_decode_B{B}_T{T}"] = {"value": B / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
                                             "GBs": bytes_ / (ms / 1e3) / 1e9,
                                             "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm,
                                             "l2_note": "inputs larger than L2" if bytes_ > 126e6 else
-                                            "working set fits L2 (repeated steps re-read it from L2)"}
+                                            "working set fits L2 (repeated steps re-read it from L2)",
+                                            **how}
             del rows
             be.kv_reset()
     return {"gqa_decode_grid": out}
@@ -551,13 +591,13 @@ def run_gdn_grid(be, args, st, peak_hbm):
         for _ in range(5):
             step()
         be.sync()
-        ms = _time(st, step, 100)
+        ms, how = _graph_entry(st, step, 100, _time(st, step, 100))
         bytes_ = B * GDN_BYTES_PER_REQ
         out[f"gdn_decode_B{B}"] = {"value": B / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
                                    "GBs": bytes_ / (ms / 1e3) / 1e9,
                                    "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm,
                                    "l2_note": "state larger than L2" if bytes_ > 126e6 else
-                                   "state fits L2 (repeated steps re-read it from L2)"}
+                                   "state fits L2 (repeated steps re-read it from L2)", **how}
     return {"gdn_decode_grid": out}
 
 
@@ -824,7 +864,8 @@ def main():
     ap.add_argument("--context", type=int, default=T_CTX, help="decode context length")
     ap.add_argument("--quick", action="store_true",
                     help="headline kernel only (no e2e / secondary / CPU legs), for profiling")
-    ap.add_argument("--only", choices=["gdn", "prefill", "gdnprefill", "stack", "stackprefill", "linear"],
+    ap.add_argument("--only", choices=["gdn", "prefill", "gdnprefill", "stack", "stackprefill", "linear",
+                                       "gqagrid", "gdngrid"],
                     default=None,
                     help="run one secondary leg alone and print its JSON (profiling)")
     ap.add_argument("--lengths", default="8192,32768", help="prefill lengths of the secondary legs")

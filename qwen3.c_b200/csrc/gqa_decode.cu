@@ -157,6 +157,32 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
     const int H = p.H, KH = p.KH, nv = H + KH;
     const int Hin = p.Hin ? p.Hin : H, KHin = p.KHin ? p.KHin : KH;
     const int half = p.rot >> 1;
+    // the input loads of up to U head vectors of this warp (and, for k
+    // vectors with bf16 inputs, the v row appended beside them; fp32 v is
+    // loaded where it is stored, to stay within 64 registers), issued before
+    // any arithmetic
+    Raw8<TI> raw[GQA_PRO_U], vraw[GQA_PRO_U];
+    auto issue = [&](int b) {
+        int r = b / nv, j = b - r * nv;
+#pragma unroll
+        for (int u = 0; u < GQA_PRO_U; ++u) {
+            if (r < rows) {
+                const int n = n0 + r;
+                if (j < H) {
+                    raw[u].load(static_cast<const TI *>(p.qg) + ((size_t)n * Hin + p.h0 + j) * 2 * GQA_HD + lane * 8);
+                } else {
+                    const size_t off = ((size_t)n * KHin + p.kh0 + (j - H)) * GQA_HD + lane * 8;
+                    raw[u].load(static_cast<const TI *>(p.k) + off);
+                    if constexpr (sizeof(TI) == 2) vraw[u].load(static_cast<const TI *>(p.v) + off);
+                }
+            }
+            for (j += GQA_PRO_WARPS; j >= nv; j -= nv) ++r;
+        }
+    };
+    // the first batch goes out before the RoPE table, whose barrier would
+    // otherwise hold it back (one global-memory wait instead of two on the
+    // decode path, where a CTA holds one row)
+    issue(warp);
     // RoPE angles of these rows (c/qwen.c:570-579), shared by all their heads
     for (int i = threadIdx.x; i < rows * half; i += blockDim.x) {
         const int r = i / half, jj = i - r * half;
@@ -174,20 +200,8 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
     const bool rope_lane = d0 < p.rot;
     float *vw = vec[warp];
     for (int b = warp; b < total; b += GQA_PRO_WARPS * GQA_PRO_U) {
-        // issue the loads of up to U head vectors before any arithmetic
-        Raw8<TI> raw[GQA_PRO_U];
+        if (b != warp) issue(b);
         int r = b / nv, j = b - r * nv;
-        const int r0 = r, j0 = j;
-#pragma unroll
-        for (int u = 0; u < GQA_PRO_U; ++u) {
-            if (r < rows) {
-                const int n = n0 + r;
-                if (j < H) raw[u].load(static_cast<const TI *>(p.qg) + ((size_t)n * Hin + p.h0 + j) * 2 * GQA_HD + d0);
-                else raw[u].load(static_cast<const TI *>(p.k) + ((size_t)n * KHin + p.kh0 + (j - H)) * GQA_HD + d0);
-            }
-            for (j += GQA_PRO_WARPS; j >= nv; j -= nv) ++r;
-        }
-        r = r0; j = j0;
 #pragma unroll
         for (int u = 0; u < GQA_PRO_U; ++u) {
             if (r >= rows) break;
@@ -250,7 +264,8 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
                 const size_t row = ((size_t)creq * KH + kh) * p.max_t + p.pos[n];
                 store8(p.kcache + row * GQA_HD + d0, y);
                 float v[8];
-                load8<TI>(static_cast<const TI *>(p.v) + ((size_t)n * KHin + p.kh0 + kh) * GQA_HD + d0, v);
+                if constexpr (sizeof(TI) == 2) vraw[u].unpack(v);
+                else load8<TI>(static_cast<const TI *>(p.v) + ((size_t)n * KHin + p.kh0 + kh) * GQA_HD + d0, v);
                 store8(p.vcache + row * GQA_HD + d0, v);
             }
             for (j += GQA_PRO_WARPS; j >= nv; j -= nv) ++r;
@@ -482,8 +497,12 @@ gqa_combine_kernel(GqaCombineArgs p)
     constexpr int CW = GQA_HD / 32;      // warps
     __shared__ float sm_ml[CW][2];
     __shared__ __align__(16) float sm_o[CW][GQA_HD];
-    griddep_wait();      // launched as a programmatic dependent of the split kernel
     const int n = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The gate is a caller input, complete before the prologue (a plain
+    // launch) started and so before this kernel could: it is read ahead of
+    // the wait for the split partials.
+    const float gate = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * p.H + h) * 2 * GQA_HD + GQA_HD + tid]);
+    griddep_wait();      // launched as a programmatic dependent of the split kernel
     const int kh = h / GQA_GRP, hl = h % GQA_GRP;
     const size_t base = ((size_t)n * p.KH + kh) * p.n_splits;
     float m = -INFINITY, l = 0.f, o[8];
@@ -531,7 +550,6 @@ gqa_combine_kernel(GqaCombineArgs p)
         O += sm_o[w][tid] * f;
         L += sm_ml[w][1] * f;
     }
-    const float gate = to_f32(static_cast<const TI *>(p.qg)[((size_t)n * p.H + h) * 2 * GQA_HD + GQA_HD + tid]);
     static_cast<TO *>(p.ctx)[((size_t)n * p.H + h) * GQA_HD + tid] = from_f32<TO>(O / L * sigmoidf_(gate));
 }
 
