@@ -111,9 +111,18 @@ class ClockSampler:
         if self.t:
             self.t.join(timeout=2)
 
+    def brief(self):
+        """Median SM clock and reasons over a short timed region (a leg)."""
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+                "reasons": sorted(self.reasons), "samples": len(self.sm)}
+
     def summary(self):
         return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.smax,
                 "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 2 ms polling"}
+
+
+def _local_rank():
+    return int(os.environ.get("LOCAL_RANK", "0"))
 
 
 def dist_setup():
@@ -627,11 +636,12 @@ def run_prefill_secondary(be, args, st, peak_tc):
         be.ktimer_enable(True)
         be.ktimer_read(be.K_GQA_PREFILL)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(reps):
-            step()
-        e1.record(st)
-        torch.cuda.synchronize()
+        with ClockSampler(_local_rank()) as clk:
+            e0.record(st)
+            for _ in range(reps):
+                step()
+            e1.record(st)
+            torch.cuda.synchronize()
         be.ktimer_enable(False)
         kms, kn = be.ktimer_read(be.K_GQA_PREFILL)
         ms = e0.elapsed_time(e1) / reps
@@ -641,7 +651,7 @@ def run_prefill_secondary(be, args, st, peak_tc):
             "metric": "GQA prefill tok/s (one layer, causal)", "S": S, "value": S / (ms / 1e3),
             "unit": "tok/s", "ms_per_call": ms, "kernel_ms": kavg,
             "achieved_TFLOPs": flops / (kavg / 1e3) / 1e12,
-            "frac_of_bf16_peak": flops / (kavg / 1e3) / 1e12 / peak_tc}
+            "frac_of_bf16_peak": flops / (kavg / 1e3) / 1e12 / peak_tc, "clocks": clk.brief()}
         del qg, k, v, ctx
         be.kv_reset()
     return out
@@ -692,11 +702,12 @@ def run_gdn_prefill_secondary(be, args, st, peak_hbm):
         # an idle gap measured 5-10 % apart from run to run on this pool
         be.gdn_reset()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(reps):
-            call()
-        e1.record(st)
-        torch.cuda.synchronize()
+        with ClockSampler(_local_rank()) as clk:
+            e0.record(st)
+            for _ in range(reps):
+                call()
+            e1.record(st)
+            torch.cuda.synchronize()
         be.ktimer_enable(False)
         be.ktimer_read(be.K_GDN_PREFILL)
         ms = e0.elapsed_time(e1) / reps
@@ -705,7 +716,7 @@ def run_gdn_prefill_secondary(be, args, st, peak_hbm):
             "metric": "GDN chunked prefill tok/s (one layer)", "S": S, "k_heads": nkh,
             "value": S / (ms / 1e3),
             "unit": "tok/s", "ms_per_call": ms, "achieved_GBs": bytes_ / (ms / 1e3) / 1e9,
-            "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm}
+            "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / peak_hbm, "clocks": clk.brief()}
         del qkv, z, a, b, y
     return out
 

@@ -68,6 +68,10 @@ struct Global {
     int device = -1;
     int num_sms = 148;
     cudaStream_t stream = nullptr;     // backend's own stream
+    // host-buffer decode: the gate half of q|gate is uploaded on this stream
+    // while the kernels run (created at the first such call)
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_gate = nullptr;
     cudaStream_t user_stream = nullptr;
     bool user_stream_set = false;
     KvLayer kv[MAX_LAYERS];
@@ -110,6 +114,9 @@ void kt_mark(int k)  // call before and after the launch of kernel k
 // stream() use (any later launch or copy may raise it again).
 int g_err_host = 0;
 bool g_err_fresh = false;
+// Pinned landing word for that read (a pageable destination is a staged,
+// slower copy on every host-buffer call); null if it could not be allocated.
+int *g_err_pin = nullptr;
 
 cudaStream_t stream()
 {
@@ -252,8 +259,10 @@ int download(void *host, const void *dev, size_t bytes)
 {
     cudaStream_t st = stream();
     CK(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, st));
-    CK(cudaMemcpyFromSymbolAsync(&g_err_host, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyFromSymbolAsync(g_err_pin ? g_err_pin : &g_err_host, g_dev_error, sizeof(int), 0,
+                                 cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if (g_err_pin) g_err_host = *g_err_pin;
     g_err_fresh = true;
     return 1;
 }
@@ -293,7 +302,8 @@ __global__ void split_q_kernel(const float *q, __nv_bfloat16 *out, int n_heads_t
 // Runs split-KV attention + combine for nq query rows whose roped bf16 q is
 // in S_Q, positions in pos_d, cache requests in creq_d (nullable).
 int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, int tmax,
-               const void *qg_gate, void *ctx, int in_bf16, int out_bf16, float scale)
+               const void *qg_gate, void *ctx, int in_bf16, int out_bf16, float scale,
+               cudaEvent_t gate_ready = nullptr)
 {
     const int ns = gqa_pick_splits(nq, L.KH, tmax, G.num_sms);
     const int chunk = gqa_chunk_for(tmax, ns);
@@ -317,6 +327,7 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     GqaCombineArgs ca{};
     ca.part_o = po; ca.part_ml = pml; ca.qg = qg_gate; ca.ctx = ctx;
     ca.nq = nq; ca.H = H; ca.KH = L.KH; ca.n_splits = ns;
+    if (gate_ready) CK(cudaStreamWaitEvent(stream(), gate_ready, 0));   // the gate reads come last
     kt_mark(COLI_K_GQA_COMBINE);
     CK(launch_gqa_combine(ca, in_bf16, out_bf16, stream()));
     kt_mark(COLI_K_GQA_COMBINE);
@@ -352,7 +363,8 @@ int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void
 // prologue + attention for nq rows (pos_d/creq_d on device)
 int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, const int *pos_d,
              const int *creq_d, int tmax, void *ctx, int H, int KH, int hd, int rot, float eps,
-             float theta, int in_bf16, int out_bf16, int prefill_req = -1, int pos_base = 0)
+             float theta, int in_bf16, int out_bf16, int prefill_req = -1, int pos_base = 0,
+             cudaEvent_t gate_ready = nullptr)
 {
     KvLayer &L = G.kv[layer];
     if (!gqa_shape_ok(L, H, KH, hd)) return 0;
@@ -370,7 +382,8 @@ int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, co
     if (prefill_req >= 0 && nq >= PREFILL_MIN_ROWS)
         return gqa_prefill_rows(L, prefill_req, nq, pos_base, H, qg, ctx, in_bf16, out_bf16,
                                 1.f / sqrtf((float)hd));
-    return gqa_attend(L, nq, H, pos_d, creq_d, tmax, qg, ctx, in_bf16, out_bf16, 1.f / sqrtf((float)hd));
+    return gqa_attend(L, nq, H, pos_d, creq_d, tmax, qg, ctx, in_bf16, out_bf16, 1.f / sqrtf((float)hd),
+                      gate_ready);
 }
 
 // Causal prefill of S rows of one request on the tensor cores; the roped bf16
@@ -544,6 +557,10 @@ int coli_cuda_init(int device)
     if (prop.major != 10) return fail("device %d is sm_%d%d; this backend is built for sm_100a only", device, prop.major, prop.minor);
     G.num_sms = prop.multiProcessorCount;
     CK(cudaStreamCreateWithFlags(&G.stream, cudaStreamNonBlocking));
+    if (!g_err_pin && cudaHostAlloc((void **)&g_err_pin, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+        g_err_pin = nullptr;   // the pageable word serves
+        cudaGetLastError();
+    }
     cudaDriverEntryPointQueryResult q;
     void *fn = nullptr;
     CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
@@ -583,6 +600,15 @@ void coli_cuda_shutdown(void)
     }
     if (G.stream) cudaStreamDestroy(G.stream);
     G.stream = nullptr;
+    if (G.copy_stream) {
+        cudaStreamDestroy(G.copy_stream);
+        cudaEventDestroy(G.ev_fork);
+        cudaEventDestroy(G.ev_gate);
+    }
+    G.copy_stream = nullptr;
+    G.ev_fork = G.ev_gate = nullptr;
+    if (g_err_pin) cudaFreeHost(g_err_pin);
+    g_err_pin = nullptr;
     G.user_stream_set = false;
     G.ready = 0;
     G.device = -1;
@@ -897,20 +923,44 @@ int coli_cuda_gqa_decode(int layer, int B, const float *qg, const float *k, cons
                          float theta)
 {
     READY();
-    if (B < 1) return fail("bad batch");
-    const void *qd = upload(S_IN0, qg, (size_t)B * H * 2 * hd * 4);
+    if (B < 1 || hd < 1) return fail("bad batch");
+    if (!check_layer(layer)) return fail("layer %d out of range", layer);
+    if (B > G.kv[layer].batch) return fail("batch %d beyond the cache's %d requests", B, G.kv[layer].batch);
+    int tmax = 0;
+    for (int b = 0; b < B; ++b) {
+        if (pos[b] < 0) return fail("negative position");
+        tmax = pos[b] + 1 > tmax ? pos[b] + 1 : tmax;
+    }
+    // q|gate rows: the q halves go up first with k, v and the positions; the
+    // gate halves (needed only by the combine, at the end) follow on the copy
+    // stream while the prologue and the split kernel run
+    if (!G.copy_stream) {
+        CK(cudaStreamCreateWithFlags(&G.copy_stream, cudaStreamNonBlocking));
+        CK(cudaEventCreateWithFlags(&G.ev_fork, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&G.ev_gate, cudaEventDisableTiming));
+    }
+    const size_t half = (size_t)hd * 4, rows = (size_t)B * H;
+    char *qd = (char *)scratch(S_IN0, rows * 2 * half);
+    if (!qd) return 0;
+    CK(cudaMemcpy2DAsync(qd, 2 * half, qg, 2 * half, half, rows, cudaMemcpyHostToDevice, stream()));
     const void *kd = upload(S_IN1, k, (size_t)B * KH * hd * 4);
     const void *vd = upload(S_IN2, v, (size_t)B * KH * hd * 4);
     const int *pd = (const int *)upload(S_POS, pos, (size_t)B * 4);
     float *out = (float *)scratch(S_OUT, (size_t)B * H * hd * 4);
-    if (!qd || !kd || !vd || !pd || !out) return 0;
-    int tmax = 0;
-    for (int b = 0; b < B; ++b) tmax = pos[b] + 1 > tmax ? pos[b] + 1 : tmax;
-    if (!check_layer(layer)) return fail("layer %d out of range", layer);
-    if (B > G.kv[layer].batch) return fail("batch %d beyond the cache's %d requests", B, G.kv[layer].batch);
-    for (int b = 0; b < B; ++b)
-        if (pos[b] < 0) return fail("negative position");
-    if (!gqa_rows(layer, B, qd, kd, vd, pd, nullptr, tmax, out, H, KH, hd, rot, eps, theta, 0, 0)) return 0;
+    if (!kd || !vd || !pd || !out) return 0;
+    // after the q/k/v copies, so that the two do not share the link
+    CK(cudaEventRecord(G.ev_fork, stream()));
+    CK(cudaStreamWaitEvent(G.copy_stream, G.ev_fork, 0));
+    CK(cudaMemcpy2DAsync(qd + half, 2 * half, (const char *)qg + half, 2 * half, half, rows,
+                         cudaMemcpyHostToDevice, G.copy_stream));
+    CK(cudaEventRecord(G.ev_gate, G.copy_stream));
+    if (!gqa_rows(layer, B, qd, kd, vd, pd, nullptr, tmax, out, H, KH, hd, rot, eps, theta, 0, 0, -1, 0,
+                  G.ev_gate)) {
+        // rejected before the combine: the backend stream still joins the
+        // gate copy, so no later call frees or regrows its buffer under it
+        cudaStreamWaitEvent(stream(), G.ev_gate, 0);
+        return 0;
+    }
     if (!download(ctx, out, (size_t)B * H * hd * 4)) return 0;
     return check_dev_error();
 }
