@@ -303,7 +303,7 @@ __global__ void split_q_kernel(const float *q, __nv_bfloat16 *out, int n_heads_t
 // in S_Q, positions in pos_d, cache requests in creq_d (nullable).
 int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, int tmax,
                const void *qg_gate, void *ctx, int in_bf16, int out_bf16, float scale,
-               cudaEvent_t gate_ready = nullptr)
+               cudaEvent_t gate_ready = nullptr, const GqaPrologueArgs *fused = nullptr)
 {
     const int ns = gqa_pick_splits(nq, L.KH, tmax, G.num_sms);
     const int chunk = gqa_chunk_for(tmax, ns);
@@ -321,6 +321,10 @@ int gqa_attend(KvLayer &L, int nq, int H, const int *pos_d, const int *creq_d, i
     // (creq given) append up to S rows ending at each query row's position
     sa.appended = creq_d ? nq : 1;
     sa.scale_log2 = scale * 1.4426950408889634f;
+    if (fused) {   // the split kernel does the prologue's work (small-batch decode)
+        sa.fuse = in_bf16 ? 1 : 2;
+        sa.pro = *fused;
+    }
     kt_mark(COLI_K_GQA_SPLIT);
     CK(launch_gqa_split(L.tmK, L.tmV, sa, stream()));
     kt_mark(COLI_K_GQA_SPLIT);
@@ -357,6 +361,7 @@ int gqa_shape_ok(KvLayer &L, int H, int KH, int hd)
 }
 
 constexpr int PREFILL_MIN_ROWS = 64;
+constexpr int GQA_FUSE_MAX_ROWS = 8;   // decode batches up to this size use the fused split kernel (1: -13 % per step; 16: no gain measured)
 int gqa_prefill_rows(KvLayer &L, int req, int S, int pos_base, int H, const void *qg, void *ctx,
                      int in_bf16, int out_bf16, float scale);
 
@@ -377,13 +382,22 @@ int gqa_rows(int layer, int nq, const void *qg, const void *k, const void *v, co
     pa.qg = qg; pa.k = k; pa.v = v; pa.qnw = L.qnw; pa.knw = L.knw; pa.pos = pos_d; pa.creq = creq_d;
     pa.qout = q; pa.kcache = L.k; pa.vcache = L.v;
     pa.nq = nq; pa.H = H; pa.KH = KH; pa.max_t = L.max_t; pa.rot = rot; pa.eps = eps; pa.theta = theta;
-    CK(launch_gqa_prologue(pa, in_bf16, stream()));
-    g_launches += 1;
+    // Small-batch decode (one appended row per query row: a batch of
+    // requests, or a single row of one request; 16-byte aligned operands):
+    // the split kernel norms / ropes q and appends the k / v rows itself, one
+    // launch and one dependent wait fewer on a latency-bound step.
+    const uintptr_t al = (uintptr_t)qg | (uintptr_t)k | (uintptr_t)v | (uintptr_t)L.qnw | (uintptr_t)L.knw |
+                         (uintptr_t)L.k | (uintptr_t)L.v;
+    const bool fuse = (nq == 1 || (!creq_d && prefill_req < 0)) && nq <= GQA_FUSE_MAX_ROWS && (al & 15) == 0;
+    if (!fuse) {
+        CK(launch_gqa_prologue(pa, in_bf16, stream()));
+        g_launches += 1;
+    }
     if (prefill_req >= 0 && nq >= PREFILL_MIN_ROWS)
         return gqa_prefill_rows(L, prefill_req, nq, pos_base, H, qg, ctx, in_bf16, out_bf16,
                                 1.f / sqrtf((float)hd));
     return gqa_attend(L, nq, H, pos_d, creq_d, tmax, qg, ctx, in_bf16, out_bf16, 1.f / sqrtf((float)hd),
-                      gate_ready);
+                      gate_ready, fuse ? &pa : nullptr);
 }
 
 // Causal prefill of S rows of one request on the tensor cores; the roped bf16

@@ -25,6 +25,8 @@
 //                        sigmoid output gate, ctx out.
 // The dominant kernel is HBM bound: 2*hd*2 bytes of K+V per cached token per
 // KV head.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -145,6 +147,77 @@ __device__ __forceinline__ void store8(__nv_bfloat16 *dst, const float (&y)[8])
 
 constexpr int GQA_PRO_ROWS = 4, GQA_PRO_WARPS = 8, GQA_PRO_U = 3;
 
+// One head vector of q or k, one warp, lane = 8 consecutive dims (d0 = 8 lane):
+// zero-centred RMSNorm (c/qwen.c:326-330; per-lane partial sums of squares in
+// fp32, the cross-lane sum in double as the reference does), then partial
+// NeoX RoPE on dims [0, rot) (c/qwen.c:570-579) with the row's angle table
+// cs / sn [rot / 2]. The RoPE partner of dim d is d +- rot/2: when rot/2 is a
+// multiple of 8 it sits in the same slot of lane +- rot/16, else it goes
+// through vw, a 256-float scratch of this warp. Shared by the prologue kernel
+// and the fused decode split kernel, so both produce the same bits.
+__device__ __forceinline__ void gqa_norm_rope(float (&y)[8], const float (&x)[8], const float (&w)[8],
+                                              float eps, int rot, const float *cs, const float *sn,
+                                              float *vw, int lane)
+{
+    const int d0 = lane * 8, half = rot >> 1;
+    float sl = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sl = fmaf(x[i], x[i], sl);
+    double s2 = sl;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float rs = 1.f / sqrtf((float)(s2 / GQA_HD) + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = x[i] * rs * (1.f + w[i]);
+    if ((half & 7) == 0) {
+        const int hl = half >> 3;
+        const int src_lane = lane < hl ? lane + hl : lane - hl;
+        float q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = __shfl_sync(0xffffffffu, y[i], src_lane);
+        if (d0 < rot) {
+            const bool lo_half = d0 < half;
+            const int jj0 = lo_half ? d0 : d0 - half;
+            const float4 c0 = *reinterpret_cast<const float4 *>(&cs[jj0]);
+            const float4 c1 = *reinterpret_cast<const float4 *>(&cs[jj0 + 4]);
+            const float4 s0 = *reinterpret_cast<const float4 *>(&sn[jj0]);
+            const float4 s1 = *reinterpret_cast<const float4 *>(&sn[jj0 + 4]);
+            const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                y[i] = lo_half ? y[i] * c[i] - q[i] * sv[i] : y[i] * c[i] + q[i] * sv[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vw[d0 + i] = y[i];
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int d = d0 + i;
+            if (d < rot) {
+                const int jj = d < half ? d : d - half;
+                const float lo = vw[jj], hi = vw[jj + half];
+                y[i] = d < half ? lo * cs[jj] - hi * sn[jj] : hi * cs[jj] + lo * sn[jj];
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// RoPE angle table of position pos (c/qwen.c:570-579): entries [0, rot/2),
+// threads tid0, tid0 + nthr, ...
+__device__ __forceinline__ void gqa_rope_table(float *cs, float *sn, int pos, int rot, float theta, int tid0,
+                                               int nthr)
+{
+    const int half = rot >> 1;
+    for (int jj = tid0; jj < half; jj += nthr) {
+        const float inv = powf(theta, -2.0f * jj / rot);
+        const float ang = (float)pos * inv;
+        cs[jj] = cosf(ang); sn[jj] = sinf(ang);
+    }
+}
+
 template <typename TI>
 __global__ void __launch_bounds__(GQA_PRO_WARPS * 32, 4)
 gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
@@ -156,7 +229,6 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
     const int n0 = blockIdx.x * rpc, rows = min(rpc, p.nq - n0);
     const int H = p.H, KH = p.KH, nv = H + KH;
     const int Hin = p.Hin ? p.Hin : H, KHin = p.KHin ? p.KHin : KH;
-    const int half = p.rot >> 1;
     // the input loads of up to U head vectors of this warp (and, for k
     // vectors with bf16 inputs, the v row appended beside them; fp32 v is
     // loaded where it is stored, to stay within 64 registers), issued before
@@ -184,20 +256,10 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
     // decode path, where a CTA holds one row)
     issue(warp);
     // RoPE angles of these rows (c/qwen.c:570-579), shared by all their heads
-    for (int i = threadIdx.x; i < rows * half; i += blockDim.x) {
-        const int r = i / half, jj = i - r * half;
-        const float inv = powf(p.theta, -2.0f * jj / p.rot);
-        const float ang = (float)p.pos[n0 + r] * inv;
-        cs_t[r][jj] = cosf(ang); sn_t[r][jj] = sinf(ang);
-    }
+    for (int r = 0; r < rows; ++r)
+        gqa_rope_table(cs_t[r], sn_t[r], p.pos[n0 + r], p.rot, p.theta, threadIdx.x, blockDim.x);
     __syncthreads();
     const int d0 = lane * 8, total = rows * nv;
-    // RoPE partner of dim d is d +- half: when half is a multiple of 8 it sits in
-    // the same slot of lane +- half/8, else it goes through shared memory
-    const bool shfl_rope = (half & 7) == 0;
-    const int hl = half >> 3;
-    const int src_lane = lane < hl ? lane + hl : lane - hl;
-    const bool rope_lane = d0 < p.rot;
     float *vw = vec[warp];
     for (int b = warp; b < total; b += GQA_PRO_WARPS * GQA_PRO_U) {
         if (b != warp) issue(b);
@@ -207,55 +269,10 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
             if (r >= rows) break;
             const int n = n0 + r;
             const bool isq = j < H;
-            float w[8], x[8];
+            float w[8], x[8], y[8];
             load8<float>((isq ? p.qnw : p.knw) + d0, w);
             raw[u].unpack(x);
-            // zero-centred RMSNorm (c/qwen.c:326-330): per-lane partial sums of
-            // squares in fp32, the cross-lane sum in double as the reference does
-            float sl = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sl = fmaf(x[i], x[i], sl);
-            double s2 = sl;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-            const float rs = 1.f / sqrtf((float)(s2 / GQA_HD) + p.eps);
-            float y[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = x[i] * rs * (1.f + w[i]);
-            // partial NeoX RoPE on dims [0, rot)
-            if (shfl_rope) {
-                float q[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) q[i] = __shfl_sync(0xffffffffu, y[i], src_lane);
-                if (rope_lane) {
-                    const bool lo_half = d0 < half;
-                    const int jj0 = lo_half ? d0 : d0 - half;
-                    const float4 c0 = *reinterpret_cast<const float4 *>(&cs_t[r][jj0]);
-                    const float4 c1 = *reinterpret_cast<const float4 *>(&cs_t[r][jj0 + 4]);
-                    const float4 s0 = *reinterpret_cast<const float4 *>(&sn_t[r][jj0]);
-                    const float4 s1 = *reinterpret_cast<const float4 *>(&sn_t[r][jj0 + 4]);
-                    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        y[i] = lo_half ? y[i] * c[i] - q[i] * sn[i] : y[i] * c[i] + q[i] * sn[i];
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) vw[d0 + i] = y[i];
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int d = d0 + i;
-                    if (d < p.rot) {
-                        const int jj = d < half ? d : d - half;
-                        const float lo = vw[jj], hi = vw[jj + half];
-                        const float c = cs_t[r][jj], sn = sn_t[r][jj];
-                        y[i] = d < half ? lo * c - hi * sn : hi * c + lo * sn;
-                    }
-                }
-                __syncwarp();
-            }
+            gqa_norm_rope(y, x, w, p.eps, p.rot, cs_t[r], sn_t[r], vw, lane);
             if (isq) {
                 store8(p.qout + ((size_t)n * H + j) * GQA_HD + d0, y);
             } else {
@@ -274,7 +291,7 @@ gqa_prologue_warp_kernel(GqaPrologueArgs p, int rpc)
 }
 
 // ------------------------------------------------------------------ split-KV
-template <int WARPS, int STAGES>
+template <int WARPS, int STAGES, int FUSE>
 __global__ void __launch_bounds__(WARPS * 32, 1)
 gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                  GqaSplitArgs p)
@@ -327,18 +344,55 @@ gqa_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant_
             if (start + (warp + it * WARPS) * GQA_TILE + GQA_TILE > T - p.appended) deferred |= 1u << it;
             else issue(it);
         }
-    griddep_wait();      // the prologue's q and appended rows are visible
+    griddep_wait();      // the prologue's q and appended rows (or, fused, the inputs) are visible
     griddep_launch();    // the combine may launch; it waits for this grid to finish
-    if (lane == 0 && deferred) {
-        fence_proxy_async();   // generic-proxy cache writes of the prologue before the async-proxy read
-        for (int it = 0; it < STAGES; ++it)
-            if (deferred >> it & 1u) issue(it);
-    }
-    // q of the 8 heads sharing this KV head (bf16, roped)
-    {
+    if constexpr (FUSE == 0) {
+        if (lane == 0 && deferred) {
+            fence_proxy_async();   // generic-proxy cache writes of the prologue before the async-proxy read
+            for (int it = 0; it < STAGES; ++it)
+                if (deferred >> it & 1u) issue(it);
+        }
+        // q of the 8 heads sharing this KV head (bf16, roped)
         const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)n * p.H + kh * GQA_GRP) * GQA_HD);
         uint4 *dst = reinterpret_cast<uint4 *>(qsm);
         for (int i = tid; i < GQA_GRP * GQA_HD / 8; i += WARPS * 32) dst[i] = src[i];
+    } else {
+        // The prologue's work for this CTA, from the raw inputs: norm and rope
+        // the q of the 8 heads of this KV head into qsm (every split of the
+        // request does this for itself), and, in the CTA whose key range
+        // holds position T - 1, norm and rope k and append the k / v row
+        // there before the tile that holds it is loaded.
+        using TI = typename std::conditional<FUSE == 1, __nv_bfloat16, float>::type;
+        __shared__ __align__(16) float cs[GQA_HD / 2], sn[GQA_HD / 2];
+        __shared__ float vws[WARPS][GQA_HD];
+        const GqaPrologueArgs &a = p.pro;
+        if (ntiles > 0) {                      // uniform across the CTA
+            gqa_rope_table(cs, sn, T - 1, a.rot, a.theta, tid, WARPS * 32);
+            __syncthreads();
+            for (int hh = warp; hh < GQA_GRP; hh += WARPS) {
+                float x[8], w[8], y[8];
+                load8<TI>(static_cast<const TI *>(a.qg) + ((size_t)n * a.H + kh * GQA_GRP + hh) * 2 * GQA_HD + lane * 8, x);
+                load8<float>(a.qnw + lane * 8, w);
+                gqa_norm_rope(y, x, w, a.eps, a.rot, cs, sn, vws[warp], lane);
+                store8(qsm + hh * GQA_HD + lane * 8, y);
+            }
+            if (warp == WARPS - 1 && start <= T - 1 && T - 1 < end) {
+                float x[8], w[8], y[8], v[8];
+                const size_t in = ((size_t)n * a.KH + kh) * GQA_HD + lane * 8;
+                load8<TI>(static_cast<const TI *>(a.k) + in, x);
+                load8<TI>(static_cast<const TI *>(a.v) + in, v);
+                load8<float>(a.knw + lane * 8, w);
+                gqa_norm_rope(y, x, w, a.eps, a.rot, cs, sn, vws[warp], lane);
+                const size_t row = ((size_t)creq * a.KH + kh) * a.max_t + (T - 1);
+                store8(a.kcache + row * GQA_HD + lane * 8, y);
+                store8(a.vcache + row * GQA_HD + lane * 8, v);
+                fence_proxy_async_global();    // the row before the tile load below reads it
+            }
+        }
+        __syncthreads();
+        if (lane == 0 && deferred)
+            for (int it = 0; it < STAGES; ++it)
+                if (deferred >> it & 1u) issue(it);
     }
     __syncthreads();
 
@@ -584,19 +638,22 @@ cudaError_t launch_gqa_prologue(const GqaPrologueArgs &a, int in_bf16, cudaStrea
 cudaError_t launch_gqa_split(const CUtensorMap &tk, const CUtensorMap &tv, const GqaSplitArgs &a,
                              cudaStream_t st)
 {
-    auto kern = gqa_split_kernel<SPLIT_WARPS, SPLIT_STAGES>;
+    if (a.fuse < 0 || a.fuse > 2) return cudaErrorInvalidValue;
+    auto kern = a.fuse == 0 ? gqa_split_kernel<SPLIT_WARPS, SPLIT_STAGES, 0>
+              : a.fuse == 1 ? gqa_split_kernel<SPLIT_WARPS, SPLIT_STAGES, 1>
+                            : gqa_split_kernel<SPLIT_WARPS, SPLIT_STAGES, 2>;
     const size_t smem = gqa_split_smem_bytes();
-    static bool attr_done = false;
-    if (!attr_done) {
+    static bool attr_done[3] = {false, false, false};
+    if (!attr_done[a.fuse]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        attr_done = true;
+        attr_done[a.fuse] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_splits, a.KH, a.nq); cfg.blockDim = dim3(SPLIT_WARPS * 32);
     cfg.dynamicSmemBytes = smem; cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // a dependent of the prologue
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // a dependent of the prologue (or, fused, of the inputs' producer)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr; cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, tk, tv, a);

@@ -60,6 +60,13 @@ struct GqaSplitArgs {
     int appended;            // rows pos-appended+1 .. pos of each query row may be written by the
                              // kernel just before (the prologue): loaded only after the grid dependency
     float scale_log2;
+    // Small-batch decode (no cache request map, one appended row per query
+    // row): fuse = 1 (bf16 inputs) or 2 (fp32) makes the split kernel do the
+    // prologue's work itself from `pro` -- each CTA norms and ropes the q of
+    // its 8 heads, and the CTA whose key range holds position pos appends
+    // that row -- and q above is unused; 0 = q from gqa_prologue_warp_kernel.
+    int fuse;
+    GqaPrologueArgs pro;
 };
 struct GqaCombineArgs {
     const float *part_o, *part_ml;
