@@ -163,6 +163,38 @@ def test_prologue_rotary_widths(be, orc, rot):
     assert_close(ctx[S - 64:], orc.gqa_attend(q1[S - 64:], Kb, Vb, S - 64), what=f"rot {rot} tail rows")
 
 
+@pytest.mark.parametrize("rot", [36, 256])
+def test_small_batch_decode_rotary_widths(be, orc, rot):
+    """Decode batches of up to 8 rows run the prologue inside the split
+    kernel; rotary widths whose half is not a multiple of 8 (36) take its
+    shared-memory RoPE exchange, the full width (256) ropes every dim."""
+    cfg = f"gqa_fused_rot{rot}"
+    B, max_t = 3, 700
+    pos = np.array([699, 130, 64], np.int32)
+    be.kv_ensure(6, B, KH, max_t)
+    qnw, knw = _norm_w(cfg)
+    be.gqa_norm_weight(6, qnw, knw)
+    caches = []
+    for r in range(B):
+        Kc, Vc = _cache(cfg, max_t, r)
+        _upload(be, 6, r, Kc, Vc, int(pos[r]))
+        caches.append((Kc, Vc))
+    qg = synth.normal(synth.seed_of(cfg, "qg"), (B, H, 2 * HD))
+    k = synth.normal(synth.seed_of(cfg, "k"), (B, KH, HD))
+    v = synth.normal(synth.seed_of(cfg, "v"), (B, KH, HD), std=1.0 / 16)
+    ctx = be.gqa_decode(6, qg, k, v, pos, rot=rot)
+    for r in range(B):
+        Kc, Vc = caches[r][0].copy(), caches[r][1].copy()
+        q1, k1, v1 = qg[r:r + 1].copy(), k[r:r + 1].copy(), v[r:r + 1].copy()
+        orc.gqa_prologue(q1, k1, v1, qnw, knw, int(pos[r]), Kc, Vc, rot=rot)
+        for kh in range(KH):   # the appended row: normed + roped k, v as given
+            kd, vd = be.kv_read(6, r, kh * max_t + int(pos[r]), 1)
+            assert_close(kd[0], Kc[kh, pos[r]], what=f"rot {rot} req {r} appended k")
+            np.testing.assert_array_equal(vd[0], synth.bf16_round(v[r, kh]))
+        want = orc.gqa_attend(q1, Kc, Vc, int(pos[r]))
+        assert_close(ctx[r], want[0], what=f"rot {rot} req {r} pos {pos[r]}")
+
+
 def test_bf16_device_path(be, orc):
     import torch
     cfg = "gqa_dev"
