@@ -145,7 +145,9 @@ int  coli_cuda_gqa_prefill_heads_dev(int layer, int req, int S, int pos_base, co
 /* ---- New: batched GQA decode, one new token for each request b < B at its
  * own position pos[b] (requests 0..B-1 of the layer's cache). Same per-row
  * semantics as coli_cuda_gqa_step with S = 1. The _dev form takes pos on the
- * device (int32 [B]). */
+ * device (int32 [B]). The host form returns when ctx is written; inside, the
+ * gate halves of qg travel on a second, backend-owned copy stream while the
+ * attention runs (pinned host buffers make all its copies asynchronous). */
 int  coli_cuda_gqa_decode(int layer, int B, const float *qg, const float *k, const float *v,
                           const int *pos, float *ctx, int H, int KH, int hd, int rot, float eps,
                           float theta);
