@@ -948,10 +948,19 @@ int coli_cuda_gqa_decode(int layer, int B, const float *qg, const float *k, cons
     // q|gate rows: the q halves go up first with k, v and the positions; the
     // gate halves (needed only by the combine, at the end) follow on the copy
     // stream while the prologue and the split kernel run
-    if (!G.copy_stream) {
-        CK(cudaStreamCreateWithFlags(&G.copy_stream, cudaStreamNonBlocking));
-        CK(cudaEventCreateWithFlags(&G.ev_fork, cudaEventDisableTiming));
-        CK(cudaEventCreateWithFlags(&G.ev_gate, cudaEventDisableTiming));
+    if (!G.copy_stream) {   // all three or none
+        cudaStream_t cs = nullptr;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&e0, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&e1, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            if (e1) cudaEventDestroy(e1);
+            if (e0) cudaEventDestroy(e0);
+            if (cs) cudaStreamDestroy(cs);
+            return cuda_fail(e, "copy stream");
+        }
+        G.copy_stream = cs; G.ev_fork = e0; G.ev_gate = e1;
     }
     const size_t half = (size_t)hd * 4, rows = (size_t)B * H;
     char *qd = (char *)scratch(S_IN0, rows * 2 * half);
