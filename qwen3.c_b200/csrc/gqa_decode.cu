@@ -21,6 +21,11 @@
 //                        formed from the score fragments with movmatrix. The
 //                        warps' partial (max, sum, O) are merged in shared
 //                        memory and one partial per CTA goes to scratch.
+//                        For decode batches of up to 8 rows (FUSE != 0) it
+//                        also does the prologue's work for itself: its 8
+//                        heads' q normed and roped into shared memory, and
+//                        the new k / v row appended by the CTA whose key
+//                        range holds it, so no prologue launch precedes it.
 //   gqa_combine_kernel   log-sum-exp merge of the split partials, the
 //                        sigmoid output gate, ctx out.
 // The dominant kernel is HBM bound: 2*hd*2 bytes of K+V per cached token per
